@@ -1,0 +1,212 @@
+"""`vit3d`: plain 3D ViT over volumetric patches (reference `src/models/vit.py:16-253`).
+
+Same module names and shapes as the reference (`patch_embed` Conv3d with kernel == stride,
+`blocks.N` TransformerBlocks with per-block axial RoPE on integer patch coordinates, final `norm`),
+the split `embed`/`encode` API that lets masked autoencoding drop tokens in between, `patchify` in
+the same patch order, and mean-pooled `forward`.
+
+Differences:
+* `embed(x, index=None)` accepts the patch indices to keep. The patch embedding is a per-patch
+  GEMM (kernel == stride), so embedding only the kept patches gives exactly the tokens that
+  embedding all of them and gathering would, at a quarter of the cost for a 0.75 mask.
+* `pos_embed = "rope" | "sincos" | "learned"`. The reference has RoPE only (the default here);
+  "sincos" adds a fixed 3D sin-cos table and "learned" a trainable one (`pos_embed` parameter) to
+  the tokens instead of rotating attention.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from ..layers.common.blocks import TransformerBlock
+from ..ops.linear import compute_dtype, linear
+from ..ops.norm import layer_norm
+from ..ops.patch import patchify as patchify_op
+from .base import BaseModel
+from .registry import ModelRegistry
+
+SPATIAL_RANK = 3
+POS_EMBEDS = ("rope", "sincos", "learned")
+
+
+def sincos_3d(grid: tuple[int, int, int], dim: int) -> torch.Tensor:
+    """(prod(grid), dim) fixed table: a 1-D sin/cos embedding per axis on dim//3 channels each."""
+    per_axis = 2 * (dim // 6)
+    tables = []
+    for axis, count in enumerate(grid):
+        pos = torch.arange(count, dtype=torch.float64)
+        omega = 1.0 / (10000 ** (torch.arange(per_axis // 2, dtype=torch.float64) / max(1, per_axis // 2)))
+        ang = pos[:, None] * omega[None]
+        emb = torch.cat([ang.sin(), ang.cos()], dim=1)
+        shape = [1, 1, 1, per_axis]
+        shape[axis] = count
+        tables.append(emb.reshape(shape).expand(*grid, per_axis))
+    table = torch.cat(tables, dim=-1).reshape(-1, per_axis * 3)
+    if table.shape[1] < dim:
+        table = torch.cat([table, torch.zeros(table.shape[0], dim - table.shape[1], dtype=table.dtype)], 1)
+    return table.float()
+
+
+@ModelRegistry.register("vit3d")
+class ViT3D(BaseModel):
+    def __init__(
+        self,
+        img_size: tuple[int, int, int] = (64, 64, 64),
+        patch_size: tuple[int, int, int] = (8, 8, 8),
+        in_channels: int = 1,
+        embed_dim: int = 384,
+        depth: int = 6,
+        num_heads: int = 6,
+        mlp_ratio: float = 4.0,
+        attention_backend: str = "auto",
+        rotary_base: float = 10000.0,
+        pos_embed: str = "rope",
+    ) -> None:
+        super().__init__()
+        img_size = tuple(img_size)  # type: ignore[assignment]
+        patch_size = tuple(patch_size)  # type: ignore[assignment]
+        if len(img_size) != 3 or len(patch_size) != 3:
+            raise ValueError(f"img_size and patch_size must be 3D, got {img_size} {patch_size}")
+        for s, p in zip(img_size, patch_size, strict=True):
+            if s % p != 0:
+                raise ValueError(
+                    f"img_size {img_size} must be divisible by patch_size {patch_size} on every axis; "
+                    "a partial patch would silently crop the volume"
+                )
+        if pos_embed not in POS_EMBEDS:
+            raise ValueError(f"pos_embed must be one of {POS_EMBEDS}, got {pos_embed!r}")
+        self.img_size = img_size
+        self.patch_size = patch_size
+        self.in_channels = in_channels
+        self.embed_dim = embed_dim
+        self.mlp_ratio = mlp_ratio
+        self.attention_backend = attention_backend
+        self.pos_embed_kind = pos_embed
+        self.grid_size = tuple(s // p for s, p in zip(img_size, patch_size, strict=True))
+        self.patch_embed = nn.Conv3d(in_channels, embed_dim, kernel_size=patch_size, stride=patch_size)
+        use_rope = pos_embed == "rope"
+        self.blocks = nn.ModuleList(
+            TransformerBlock(
+                embed_dim, num_heads, mlp_ratio, attention_backend,
+                spatial_rank=SPATIAL_RANK, rotary_base=rotary_base, rotary=use_rope,
+            )
+            for _ in range(depth)
+        )
+        self.norm = nn.LayerNorm(embed_dim)
+        if pos_embed == "learned":
+            self.pos_embed = nn.Parameter(torch.zeros(1, self.num_patches, embed_dim))
+            nn.init.trunc_normal_(self.pos_embed, std=0.02)
+        elif pos_embed == "sincos":
+            self.register_buffer("pos_embed", sincos_3d(self.grid_size, embed_dim)[None], persistent=False)
+        else:
+            self.pos_embed = None
+
+    @property
+    def num_patches(self) -> int:
+        return int(math.prod(self.grid_size))
+
+    @property
+    def patch_volume(self) -> int:
+        return int(math.prod(self.patch_size)) * self.in_channels
+
+    def checkpointable_modules(self) -> tuple[nn.Module, ...]:
+        return tuple(self.blocks)
+
+    def prepare_input(self, batch: torch.Tensor, axes: str) -> torch.Tensor:
+        """(B, *axes) -> (B, C, D, H, W); exactly one scale level per sample."""
+        if "l" not in axes:
+            raise ValueError(f"axis order must contain 'l' (scale level), got {axes!r}")
+        rest = axes.replace("l", "", 1)
+        if not (len(rest) == 3 or (len(rest) == 4 and rest[0] == "c")):
+            raise ValueError(
+                f"axis order {axes!r} is not usable by a 3D encoder: after the level axis it must be "
+                f"three spatial axes, optionally preceded by 'c', got {rest!r}"
+            )
+        if batch.dim() != len(axes) + 1:
+            raise ValueError(
+                f"axis order {axes!r} implies a {len(axes) + 1}-D batch, got {tuple(batch.shape)}"
+            )
+        level_dim = axes.index("l") + 1
+        if batch.shape[level_dim] != 1:
+            raise ValueError(
+                f"{type(self).__name__} is single-scale, but this batch carries "
+                f"{batch.shape[level_dim]} scale levels on axis 'l' (shape {tuple(batch.shape)}); "
+                "configure the dataset for one level per sample"
+            )
+        volumes = batch.squeeze(level_dim)
+        return volumes.unsqueeze(1) if volumes.dim() == 4 else volumes
+
+    def patch_coords(self, batch_size: int, device: torch.device) -> torch.Tensor:
+        axes = [torch.arange(c, dtype=torch.float32, device=device) for c in self.grid_size]
+        grid = torch.stack(torch.meshgrid(*axes, indexing="ij"), dim=-1)
+        return grid.reshape(1, -1, SPATIAL_RANK).expand(batch_size, -1, -1)
+
+    def embed(self, x: torch.Tensor, index: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """(B, C, D, H, W) -> tokens (B, K, d) and coords (B, K, 3) for patches `index` (all if None)."""
+        if x.shape[1:] != (self.in_channels, *self.img_size):
+            raise ValueError(
+                f"expected input (B, {self.in_channels}, {', '.join(map(str, self.img_size))}), "
+                f"got {tuple(x.shape)}"
+            )
+        cdtype = compute_dtype(x) if x.is_cuda else x.dtype
+        rows = patchify_op(x, self.patch_size, index, out_dtype=cdtype)
+        weight = self.patch_embed.weight.reshape(self.embed_dim, -1)
+        tokens = linear(rows, weight, self.patch_embed.bias)
+        coords = self.patch_coords(x.shape[0], x.device)
+        if index is not None:
+            coords = torch.gather(coords, 1, index.unsqueeze(-1).expand(-1, -1, SPATIAL_RANK))
+        if self.pos_embed is not None:
+            table = self.pos_embed.expand(x.shape[0], -1, -1)
+            if index is not None:
+                table = torch.gather(table, 1, index.unsqueeze(-1).expand(-1, -1, self.embed_dim))
+            tokens = tokens + table.to(tokens.dtype)
+        return tokens, coords
+
+    def encode(self, tokens: torch.Tensor, coords: torch.Tensor) -> torch.Tensor:
+        if coords.shape[:2] != tokens.shape[:2]:
+            raise ValueError(
+                f"every token needs a coordinate: got {tokens.shape[1]} tokens but {coords.shape[1]} coordinates"
+            )
+        for block in self.blocks:
+            tokens = block(tokens, coords)
+        return layer_norm(tokens, self.norm.weight, self.norm.bias, self.norm.eps)
+
+    def patch_features(self, x: torch.Tensor) -> tuple[torch.Tensor, tuple[int, ...]]:
+        tokens, coords = self.embed(x)
+        return self.encode(tokens, coords), self.grid_size
+
+    def patchify(self, volumes: torch.Tensor) -> torch.Tensor:
+        """(B, C, D, H, W) -> (B, num_patches, patch_volume), in `embed`'s patch order."""
+        return patchify_op(volumes, self.patch_size)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        tokens, coords = self.embed(x)
+        return self.encode(tokens, coords).mean(dim=1)
+
+    def extra_forward_methods(self) -> tuple[str, ...]:
+        return ("embed", "encode")
+
+    def lora_target_groups(self) -> dict[str, tuple[nn.Linear, ...]]:
+        return {
+            "attn_qkv": tuple(b.attn.qkv for b in self.blocks),
+            "attn_proj": tuple(b.attn.proj for b in self.blocks),
+            "mlp": tuple(layer for b in self.blocks for layer in (b.mlp[0], b.mlp[2])),
+        }
+
+    def flops(self, input_shape: tuple[int, ...]) -> int:
+        if tuple(input_shape[-SPATIAL_RANK:]) != self.img_size:
+            raise ValueError(
+                f"input_shape {tuple(input_shape)} does not describe an input this model can run: its "
+                f"last {SPATIAL_RANK} axes must be the configured img_size {self.img_size}"
+            )
+        if len(input_shape) > SPATIAL_RANK and input_shape[-SPATIAL_RANK - 1] != self.in_channels:
+            raise ValueError(
+                f"input_shape {tuple(input_shape)}: the channel axis must be in_channels {self.in_channels}"
+            )
+        n, d, depth = self.num_patches, self.embed_dim, len(self.blocks)
+        hidden = int(d * self.mlp_ratio)
+        per_block = 2 * (4 * n * d * d) + 2 * (2 * n * n * d) + 2 * (2 * n * d * hidden)
+        return int(2 * n * self.patch_volume * d + depth * per_block)
