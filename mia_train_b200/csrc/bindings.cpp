@@ -1,0 +1,54 @@
+// Python bindings of the mia_train_b200._C extension (all kernels are sm_100a).
+#include <torch/extension.h>
+
+#include "errors.h"
+
+namespace mia {
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> bias,
+          c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> gamma,
+          c10::optional<torch::Tensor> aux_out, bool a_kmajor, bool b_kmajor, int64_t act, bool accumulate);
+void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate);
+void layernorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> b, torch::Tensor y,
+                   torch::Tensor mean, torch::Tensor rstd, double eps, bool rms);
+void layernorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> w, torch::Tensor mean,
+                   torch::Tensor rstd, torch::Tensor dx, c10::optional<torch::Tensor> dw,
+                   c10::optional<torch::Tensor> db, bool rms);
+void attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse, double scale);
+void attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
+                   torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, double scale);
+void rope_split_fwd(torch::Tensor qkv, c10::optional<torch::Tensor> angles, torch::Tensor pairs, torch::Tensor q,
+                    torch::Tensor k, torch::Tensor v);
+void rope_attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
+                        torch::Tensor lse, c10::optional<torch::Tensor> angles, torch::Tensor pairs,
+                        torch::Tensor dqkv, c10::optional<torch::Tensor> dangles, double scale);
+void multi_tensor_sumsq(std::vector<at::Tensor> tensors, at::Tensor out);
+void multi_tensor_scale(std::vector<at::Tensor> tensors, at::Tensor coef);
+void adamw_step(std::vector<at::Tensor> params, std::vector<at::Tensor> grads, std::vector<at::Tensor> exp_avgs,
+                std::vector<at::Tensor> exp_avg_sqs, std::vector<at::Tensor> steps, at::Tensor group_index,
+                at::Tensor hyper, double eps, c10::optional<at::Tensor> grad_scale, std::vector<at::Tensor> shadows);
+void patch_gather(torch::Tensor vol, torch::Tensor index, torch::Tensor out, int64_t pd, int64_t ph, int64_t pw);
+void mae_restore_fwd(torch::Tensor visible, torch::Tensor token, torch::Tensor restore, torch::Tensor out);
+void mae_restore_bwd(torch::Tensor dout, torch::Tensor restore, torch::Tensor dvis, torch::Tensor dtok);
+void norm_pix_mse(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, torch::Tensor loss, torch::Tensor grad,
+                  int64_t pd, int64_t ph, int64_t pw, bool norm_pix);
+}  // namespace mia
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "mia_train_b200 sm_100a kernels";
+  m.def("gemm", &mia::gemm, "tcgen05 bf16 GEMM with fused epilogue");
+  m.def("column_sum", &mia::column_sum);
+  m.def("layernorm_fwd", &mia::layernorm_fwd);
+  m.def("layernorm_bwd", &mia::layernorm_bwd);
+  m.def("attention_fwd", &mia::attention_fwd);
+  m.def("attention_bwd", &mia::attention_bwd);
+  m.def("rope_split_fwd", &mia::rope_split_fwd);
+  m.def("rope_attention_bwd", &mia::rope_attention_bwd);
+  m.def("multi_tensor_sumsq", &mia::multi_tensor_sumsq);
+  m.def("multi_tensor_scale", &mia::multi_tensor_scale);
+  m.def("adamw_step", &mia::adamw_step);
+  m.def("patch_gather", &mia::patch_gather);
+  m.def("mae_restore_fwd", &mia::mae_restore_fwd);
+  m.def("mae_restore_bwd", &mia::mae_restore_bwd);
+  m.def("norm_pix_mse", &mia::norm_pix_mse);
+  m.def("check_errors", &mia::read_and_clear_errors, "read and clear the device error word");
+}

@@ -1,0 +1,538 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), persistent and warp-specialised.
+//
+//   D[M, N] = epilogue( sum_k A[m, k] * B[n, k] )
+//
+// A is read K-major (row-major M x K) or M-major (row-major K x M); B K-major (N x K) or N-major
+// (K x N). The transposed reads serve the backward pass: dX = dY W reads W N-major and
+// dW = dY^T X reads both operands M/N-major, so no transpose is ever materialised.
+//
+// CTA = 6 warps, one CTA per SM, persistent over output tiles of 128 x BN:
+//   warp 0      TMA producer: one thread streams 128x64 A and BNx64 B tiles (128-byte swizzle)
+//               into a STAGES-deep shared-memory ring, one mbarrier per stage.
+//   warp 1      MMA issuer: allocates 2*BN TMEM columns (two fp32 accumulators), one thread issues
+//               tcgen05.mma (M=128, N=BN, K=16) per 16-wide K slice and commits each consumed stage
+//               back to the producer and each finished tile to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32*(w%4)..+31,
+//               i.e. output rows), bias / GELU (keeping the pre-activation) / GELU' / LayerScale /
+//               residual / accumulate-into-output, then 16-byte stores. While they drain one
+//               accumulator the MMA warp fills the other.
+//
+// All waits are bounded (see common.cuh); on a timeout the kernel records an error code, drains
+// the copies and MMAs it issued, frees its tensor memory and returns.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "errors.h"
+
+namespace mia {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
+
+enum Act : int { kActNone = 0, kActGelu = 1, kActDGelu = 2 };
+
+struct GemmParams {
+  int M, N, K;
+  void* D;
+  int d_fp32;
+  const float* bias;
+  const __nv_bfloat16* residual;
+  const __nv_bfloat16* aux;  // pre-activation input of GELU' (act == kActDGelu)
+  __nv_bfloat16* aux_out;    // pre-activation output (act == kActGelu)
+  const float* gamma;
+  int act;
+  int accumulate;
+  int num_m_tiles;
+  int num_tiles;
+  int* err;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kBTileBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n, const uint32_t (&r)[32]) {
+  if (m >= p.M || n >= p.N) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  const bool full = (n + 32 <= p.N);
+  const size_t row = (size_t)m * p.N;
+  if (p.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full || n + j < p.N) v[j] += __ldg(p.bias + n + j);
+  }
+  if (p.act == kActGelu) {
+    if (p.aux_out != nullptr) {
+      if (full) {
+        uint4* dst = reinterpret_cast<uint4*>(p.aux_out + row + n);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                              pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+      } else {
+        for (int j = 0; j < 32 && n + j < p.N; ++j) p.aux_out[row + n + j] = __float2bfloat16_rn(v[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+  } else if (p.act == kActDGelu) {
+    if (full) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.aux + row + n);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u = __ldg(src + q);
+        uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[8 * q + 2 * h] *= gelu_erf_grad(bf16_lo(w[h]));
+          v[8 * q + 2 * h + 1] *= gelu_erf_grad(bf16_hi(w[h]));
+        }
+      }
+    } else {
+      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] *= gelu_erf_grad(__bfloat162float(p.aux[row + n + j]));
+    }
+  }
+  if (p.gamma != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full || n + j < p.N) v[j] *= __ldg(p.gamma + n + j);
+  }
+  if (p.residual != nullptr) {
+    if (full) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.residual + row + n);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u = __ldg(src + q);
+        uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[8 * q + 2 * h] += bf16_lo(w[h]);
+          v[8 * q + 2 * h + 1] += bf16_hi(w[h]);
+        }
+      }
+    } else {
+      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] += __bfloat162float(p.residual[row + n + j]);
+    }
+  }
+  if (p.d_fp32) {
+    float* dst = reinterpret_cast<float*>(p.D) + row + n;
+    if (full) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if (p.accumulate) {
+          float4 old = d4[q];
+          o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+        }
+        d4[q] = o;
+      }
+    } else {
+      for (int j = 0; j < 32 && n + j < p.N; ++j) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
+    }
+  } else {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row + n;
+    if (full) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (p.accumulate) {
+          uint4 old = d4[q];
+          uint32_t w[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            v[8 * q + 2 * h] += bf16_lo(w[h]);
+            v[8 * q + 2 * h + 1] += bf16_hi(w[h]);
+          }
+        }
+        d4[q] = make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                           pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+      }
+    } else {
+      for (int j = 0; j < 32 && n + j < p.N; ++j) {
+        float o = v[j] + (p.accumulate ? __bfloat162float(dst[j]) : 0.f);
+        dst[j] = __float2bfloat16_rn(o);
+      }
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmParams p) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * kATileBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;      // [2]
+  uint64_t* drain_bar = tempty_bar + 2;      // [1]
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+  const int num_k = (p.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % p.num_m_tiles) * kBM;
+        const int n0 = (tile / p.num_m_tiles) * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          const int k0 = kb * kBK;
+          mbar_arrive_expect_tx(&full_bar[stage], kTx);
+          uint8_t* a_dst = smA + stage * kATileBytes;
+          uint8_t* b_dst = smB + stage * L::kBTileBytes;
+          if (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already in flight land before this CTA's shared memory goes away.
+        int s = stage, ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(&full_bar[s], ph, nullptr, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool any_mma = false;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, kErrGemmMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smA + stage * kATileBytes);
+          const uint32_t b_base = smem_u32(smB + stage * L::kBTileBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t a_desc = A_MN ? make_sdesc_sw128(a_base + k * 2048, 8192, 1024)
+                                         : make_sdesc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t b_desc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
+                                         : make_sdesc_sw128(b_base + k * 32, 16, 1024);
+            tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            any_mma = true;
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (!ok && any_mma) {
+        // Wait for every MMA this thread issued before the tensor memory is released.
+        tc_commit(drain_bar);
+        mbar_wait(drain_bar, 0, nullptr, nullptr, 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int lane_group = warp % 4;  // TMEM lanes 32*lane_group .. +31
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrGemmEpilogueWait)) break;
+      tc_fence_after();
+      const int m0 = (tile % p.num_m_tiles) * kBM;
+      const int n0 = (tile / p.num_m_tiles) * BN;
+      const int m = m0 + lane_group * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        epilogue_chunk(p, m, n0 + c * 32, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------ host
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr != nullptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major (rows x inner) matrix with row stride `ld` elements.
+static CUtensorMap make_map(const void* base, int64_t inner, int64_t rows, int64_t ld, int box_inner, int box_rows) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", (int)r);
+  return map;
+}
+
+static int num_sms(int device) {
+  static int cache[64] = {0};
+  if (cache[device] == 0) {
+    int v = 0;
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device));
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, int device, cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, STAGES>;
+  static bool configured[64] = {false};
+  if (!configured[device]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    configured[device] = true;
+  }
+  p.num_m_tiles = (p.M + kBM - 1) / kBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  p.num_tiles = p.num_m_tiles * num_n;
+  const int grid = std::min(p.num_tiles, num_sms(device));
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int BN>
+static void dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
+                            int device, cudaStream_t s) {
+  constexpr int ST = BN == 256 ? 4 : 6;
+  if (!a_mn && !b_mn) launch_gemm<BN, false, false, ST>(ta, tb, p, device, s);
+  else if (!a_mn && b_mn) launch_gemm<BN, false, true, ST>(ta, tb, p, device, s);
+  else if (a_mn && !b_mn) launch_gemm<BN, true, false, ST>(ta, tb, p, device, s);
+  else launch_gemm<BN, true, true, ST>(ta, tb, p, device, s);
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Picks the N tile: 256 unless 128 gives noticeably better wave quantisation over the SMs.
+static int choose_bn(int M, int N, int sms) {
+  if (N <= 128) return 128;
+  auto eff = [&](int bn) {
+    const long tiles = (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    const double useful = (double)M * N;
+    return useful / ((double)waves * sms * kBM * bn);
+  };
+  return eff(256) >= 0.85 * eff(128) ? 256 : 128;
+}
+
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> bias,
+          c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> gamma,
+          c10::optional<torch::Tensor> aux_out, bool a_kmajor, bool b_kmajor, int64_t act, bool accumulate) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && d.is_cuda(), "gemm: CUDA tensors expected");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && d.dim() == 2, "gemm: 2-D tensors expected");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && d.is_contiguous(), "gemm: row-major operands expected");
+  const int64_t M = a_kmajor ? a.size(0) : a.size(1);
+  const int64_t K = a_kmajor ? a.size(1) : a.size(0);
+  const int64_t N = b_kmajor ? b.size(0) : b.size(1);
+  const int64_t Kb = b_kmajor ? b.size(1) : b.size(0);
+  TORCH_CHECK(K == Kb, "gemm: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(d.size(0) == M && d.size(1) == N, "gemm: output shape mismatch");
+  TORCH_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "gemm: bf16 or fp32 output");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && M % 8 == 0, "gemm: M, N, K must be multiples of 8");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm: leading dimensions must be multiples of 8");
+  TORCH_CHECK(aligned16(a.data_ptr()) && aligned16(b.data_ptr()) && aligned16(d.data_ptr()),
+              "gemm: 16-byte aligned base addresses expected");
+  c10::cuda::CUDAGuard guard(a.device());
+  const int device = a.get_device();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.D = d.data_ptr();
+  p.d_fp32 = d.scalar_type() == at::kFloat;
+  p.act = (int)act;
+  p.accumulate = accumulate ? 1 : 0;
+  p.err = error_word(device);
+  auto check_vec = [&](const c10::optional<torch::Tensor>& t, const char* name) -> const float* {
+    if (!t.has_value()) return nullptr;
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == N, "gemm: ",
+                name, " must be a contiguous fp32 vector of length N");
+    return t->data_ptr<float>();
+  };
+  auto check_mat = [&](const c10::optional<torch::Tensor>& t, const char* name) -> __nv_bfloat16* {
+    if (!t.has_value()) return nullptr;
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->size(0) == M &&
+                    t->size(1) == N && aligned16(t->data_ptr()),
+                "gemm: ", name, " must be a contiguous, aligned bf16 (M, N) matrix");
+    return reinterpret_cast<__nv_bfloat16*>(t->data_ptr());
+  };
+  p.bias = check_vec(bias, "bias");
+  p.gamma = check_vec(gamma, "gamma");
+  p.residual = check_mat(residual, "residual");
+  p.aux = check_mat(aux, "aux");
+  p.aux_out = check_mat(aux_out, "aux_out");
+  TORCH_CHECK(act != kActDGelu || p.aux != nullptr, "gemm: GELU' needs aux");
+
+  const int bn = choose_bn((int)M, (int)N, num_sms(device));
+  // A tile: 128 rows x 64 K (K-major) or 64 M x 64 K per box, twice (M-major).
+  CUtensorMap ta = a_kmajor ? make_map(a.data_ptr(), K, M, a.stride(0), 64, kBM)
+                            : make_map(a.data_ptr(), M, K, a.stride(0), 64, 64);
+  CUtensorMap tb = b_kmajor ? make_map(b.data_ptr(), K, N, b.stride(0), 64, bn)
+                            : make_map(b.data_ptr(), N, K, b.stride(0), 64, 64);
+  if (bn == 256) dispatch_majors<256>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+  else dispatch_majors<128>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+}
+
+// -------------------------------------------------------------- column sums (bias gradients)
+// out[n] (+)= sum_m x[m, n]; x bf16 (M, N) row-major, N % 8 == 0. Each thread owns 8 adjacent
+// columns over a slab of rows; partial sums are combined with one fp32 atomic per column per CTA.
+__global__ void column_sum_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ out, int M, int N,
+                                  int rows_per_cta) {
+  const int col8 = blockIdx.x * blockDim.x + threadIdx.x;  // group of 8 columns
+  const int n = col8 * 8;
+  if (n >= N) return;
+  const int m_begin = blockIdx.y * rows_per_cta;
+  const int m_end = min(M, m_begin + rows_per_cta);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int m = m_begin; m < m_end; ++m) {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * N + n));
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      acc[2 * h] += bf16_lo(w[h]);
+      acc[2 * h + 1] += bf16_hi(w[h]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) atomicAdd(out + n + j, acc[j]);
+}
+
+void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
+              "column_sum: contiguous bf16 (M, N) expected");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == x.size(1),
+              "column_sum: fp32 (N,) output expected");
+  TORCH_CHECK(x.size(1) % 8 == 0, "column_sum: N must be a multiple of 8");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (!accumulate) C10_CUDA_CHECK(cudaMemsetAsync(out.data_ptr(), 0, out.numel() * 4, stream));
+  const int M = (int)x.size(0), N = (int)x.size(1);
+  if (M == 0) return;
+  const int threads = 128;
+  const int groups = N / 8;
+  dim3 grid((groups + threads - 1) / threads, std::max(1, std::min(256, (M + 63) / 64)));
+  const int rows = (M + grid.y - 1) / grid.y;
+  column_sum_kernel<<<grid, threads, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                                  out.data_ptr<float>(), M, N, rows);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mia

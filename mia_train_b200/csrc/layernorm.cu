@@ -1,0 +1,218 @@
+// LayerNorm / RMSNorm forward and backward, one warp per row, fp32 statistics.
+//
+// Forward writes y (input dtype), the row mean (0 for RMSNorm) and 1/sqrt(var + eps). Backward
+// recomputes xhat from them:
+//   g   = dy * w
+//   dx  = rstd * (g - mean(g) - xhat * mean(g * xhat))        (LayerNorm)
+//   dx  = rstd * (g - xhat * mean(g * xhat))                  (RMSNorm)
+//   dw += sum_rows dy * xhat,   db += sum_rows dy
+// The parameter gradients are reduced per CTA in shared memory and then added to global fp32
+// buffers with one atomic per column per CTA.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace mia {
+
+template <typename T>
+struct Vec8;
+template <>
+struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&v)[8]) {
+    uint4 u = *reinterpret_cast<const uint4*>(p);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      v[2 * h] = bf16_lo(w[h]);
+      v[2 * h + 1] = bf16_hi(w[h]);
+    }
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float (&v)[8]) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                              pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  }
+};
+template <>
+struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, float (&v)[8]) {
+    float4 a = *reinterpret_cast<const float4*>(p);
+    float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ void store(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T>
+__global__ void layernorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                                     T* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                     int rows, int n, float eps, int rms) {
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
+    const T* xr = x + (size_t)row * n;
+    float s = 0.f;
+    for (int c = lane * 8; c < n; c += 256) {
+      float v[8];
+      Vec8<T>::load(xr + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[j];
+    }
+    const float mean = rms ? 0.f : warp_sum(s) / n;
+    float ss = 0.f;
+    for (int c = lane * 8; c < n; c += 256) {
+      float v[8];
+      Vec8<T>::load(xr + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[j] - mean;
+        ss += d * d;
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(ss) / n + eps);
+    T* yr = y + (size_t)row * n;
+    for (int c = lane * 8; c < n; c += 256) {
+      float v[8];
+      Vec8<T>::load(xr + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float o = (v[j] - mean) * rstd;
+        if (w != nullptr) o *= __ldg(w + c + j);
+        if (b != nullptr) o += __ldg(b + c + j);
+        v[j] = o;
+      }
+      Vec8<T>::store(yr + c, v);
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+template <typename T>
+__global__ void layernorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
+                                     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                                     T* __restrict__ dx, float* __restrict__ dw, float* __restrict__ db, int rows,
+                                     int n, int rms) {
+  extern __shared__ float sacc[];  // [2 * n]: dw partials, db partials
+  const bool want_dw = dw != nullptr, want_db = db != nullptr;
+  for (int i = threadIdx.x; i < 2 * n; i += blockDim.x) sacc[i] = 0.f;
+  __syncthreads();
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
+    const T* xr = x + (size_t)row * n;
+    const T* gr = dy + (size_t)row * n;
+    const float mean = mean_in[row];
+    const float rstd = rstd_in[row];
+    float sum_g = 0.f, sum_gx = 0.f;
+    for (int c = lane * 8; c < n; c += 256) {
+      float xv[8], gv[8];
+      Vec8<T>::load(xr + c, xv);
+      Vec8<T>::load(gr + c, gv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = (xv[j] - mean) * rstd;
+        const float g = gv[j] * (w != nullptr ? __ldg(w + c + j) : 1.f);
+        sum_g += g;
+        sum_gx += g * xh;
+        if (want_dw) atomicAdd(&sacc[c + j], gv[j] * xh);
+        if (want_db) atomicAdd(&sacc[n + c + j], gv[j]);
+      }
+    }
+    const float mg = rms ? 0.f : warp_sum(sum_g) / n;
+    const float mgx = warp_sum(sum_gx) / n;
+    T* dr = dx + (size_t)row * n;
+    for (int c = lane * 8; c < n; c += 256) {
+      float xv[8], gv[8];
+      Vec8<T>::load(xr + c, xv);
+      Vec8<T>::load(gr + c, gv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = (xv[j] - mean) * rstd;
+        const float g = gv[j] * (w != nullptr ? __ldg(w + c + j) : 1.f);
+        xv[j] = rstd * (g - mg - xh * mgx);
+      }
+      Vec8<T>::store(dr + c, xv);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    if (want_dw) atomicAdd(dw + i, sacc[i]);
+    if (want_db) atomicAdd(db + i, sacc[n + i]);
+  }
+}
+
+static int sm_count(const torch::Tensor& t) {
+  int v = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, t.get_device()));
+  return v;
+}
+
+void layernorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> b, torch::Tensor y,
+                   torch::Tensor mean, torch::Tensor rstd, double eps, bool rms) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 2, "layernorm_fwd: contiguous 2-D CUDA input");
+  const int rows = (int)x.size(0), n = (int)x.size(1);
+  TORCH_CHECK(n % 8 == 0, "layernorm: hidden size must be a multiple of 8");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const float* wp = w.has_value() ? w->data_ptr<float>() : nullptr;
+  const float* bp = b.has_value() ? b->data_ptr<float>() : nullptr;
+  if (rows == 0) return;
+  const int threads = 256;
+  const int grid = std::min((rows + 7) / 8, sm_count(x) * 8);
+  if (x.scalar_type() == at::kBFloat16) {
+    layernorm_fwd_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), wp, bp, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+        mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, n, (float)eps, rms ? 1 : 0);
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kFloat, "layernorm: bf16 or fp32 input");
+    layernorm_fwd_kernel<float><<<grid, threads, 0, stream>>>(x.data_ptr<float>(), wp, bp, y.data_ptr<float>(),
+                                                              mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, n,
+                                                              (float)eps, rms ? 1 : 0);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void layernorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> w, torch::Tensor mean,
+                   torch::Tensor rstd, torch::Tensor dx, c10::optional<torch::Tensor> dw,
+                   c10::optional<torch::Tensor> db, bool rms) {
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.sizes() == x.sizes(), "layernorm_bwd: shapes");
+  const int rows = (int)x.size(0), n = (int)x.size(1);
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (rows == 0) return;
+  const float* wp = w.has_value() ? w->data_ptr<float>() : nullptr;
+  float* dwp = dw.has_value() ? dw->data_ptr<float>() : nullptr;
+  float* dbp = db.has_value() ? db->data_ptr<float>() : nullptr;
+  const int threads = 256;
+  const int grid = std::min((rows + 7) / 8, sm_count(x) * 2);
+  const size_t smem = 2 * (size_t)n * sizeof(float);
+  if (x.scalar_type() == at::kBFloat16) {
+    auto k = layernorm_bwd_kernel<__nv_bfloat16>;
+    if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<grid, threads, smem, stream>>>(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+                                      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), wp, mean.data_ptr<float>(),
+                                      rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dwp, dbp,
+                                      rows, n, rms ? 1 : 0);
+  } else {
+    auto k = layernorm_bwd_kernel<float>;
+    if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<grid, threads, smem, stream>>>(dy.data_ptr<float>(), x.data_ptr<float>(), wp, mean.data_ptr<float>(),
+                                      rstd.data_ptr<float>(), dx.data_ptr<float>(), dwp, dbp, rows, n, rms ? 1 : 0);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mia

@@ -1,0 +1,273 @@
+// Masked-autoencoding kernels: patch gather (the patch-embedding GEMM's A operand), mask-token
+// re-insertion and its backward, and the fused norm-pix MSE loss with its gradient.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace mia {
+
+typedef __nv_bfloat16 bf16;
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<bf16>(bf16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16_rn(v); }
+
+// One CTA per (b, kept patch). Row layout (channel, pd, ph, pw) = Conv3d weight flattening.
+template <typename Tin, typename Tout>
+__global__ void patch_gather_kernel(const Tin* __restrict__ vol, const int64_t* __restrict__ index,
+                                    Tout* __restrict__ out, int C, int D, int H, int W, int pd, int ph, int pw, int K) {
+  const int row = blockIdx.x;  // b * K + k
+  const int b = row / K;
+  const int gh = H / ph, gw = W / pw;
+  const int64_t p = index[row];
+  const int zd = (int)(p / ((int64_t)gh * gw));
+  const int zh = (int)((p / gw) % gh);
+  const int zw = (int)(p % gw);
+  const int vol_patch = pd * ph * pw;
+  const int len = C * vol_patch;
+  Tout* dst = out + (size_t)row * len;
+  for (int e = threadIdx.x; e < len; e += blockDim.x) {
+    const int c = e / vol_patch;
+    int r = e % vol_patch;
+    const int i = r / (ph * pw);
+    r %= ph * pw;
+    const int j = r / pw, l = r % pw;
+    const size_t src = ((((size_t)b * C + c) * D + (zd * pd + i)) * H + (zh * ph + j)) * W + (zw * pw + l);
+    dst[e] = from_f<Tout>(to_f<Tin>(vol[src]));
+  }
+}
+
+void patch_gather(torch::Tensor vol, torch::Tensor index, torch::Tensor out, int64_t pd, int64_t ph, int64_t pw) {
+  TORCH_CHECK(vol.is_contiguous() && vol.dim() == 5, "patch_gather: contiguous (B, C, D, H, W) volume");
+  TORCH_CHECK(index.scalar_type() == at::kLong && index.is_contiguous(), "patch_gather: int64 (B, K) index");
+  c10::cuda::CUDAGuard guard(vol.device());
+  const int B = (int)vol.size(0), C = (int)vol.size(1), D = (int)vol.size(2), H = (int)vol.size(3), W = (int)vol.size(4);
+  const int K = (int)index.size(1);
+  if (B * K == 0) return;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int threads = 256;
+  auto launch = [&](auto in_tag, auto out_tag) {
+    using Tin = decltype(in_tag);
+    using Tout = decltype(out_tag);
+    patch_gather_kernel<Tin, Tout><<<B * K, threads, 0, stream>>>(
+        reinterpret_cast<const Tin*>(vol.data_ptr()), index.data_ptr<int64_t>(), reinterpret_cast<Tout*>(out.data_ptr()),
+        C, D, H, W, (int)pd, (int)ph, (int)pw, K);
+  };
+  const bool in_f = vol.scalar_type() == at::kFloat;
+  const bool out_f = out.scalar_type() == at::kFloat;
+  if (in_f && out_f) launch(float{}, float{});
+  else if (in_f && !out_f) launch(float{}, bf16{});
+  else if (!in_f && out_f) launch(bf16{}, float{});
+  else launch(bf16{}, bf16{});
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// out[b, n, :] = restore[b, n] < K ? visible[b, restore[b, n], :] : token. One warp per row, 16 B
+// vectors (d % 8 == 0).
+__global__ void mae_restore_fwd_kernel(const bf16* __restrict__ visible, const bf16* __restrict__ token,
+                                       const int64_t* __restrict__ restore, bf16* __restrict__ out, int B, int N,
+                                       int K, int d) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= B * N) return;
+  const int b = row / N;
+  const int64_t r = restore[row];
+  const uint4* src = r < K ? reinterpret_cast<const uint4*>(visible + ((size_t)b * K + r) * d)
+                           : reinterpret_cast<const uint4*>(token);
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * d);
+  for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
+}
+
+// dvis[b, restore[b, n]] = dout[b, n] for visible rows; dtoken += sum of the others. Each CTA
+// reduces its masked rows in registers and shared memory, then one atomic per column.
+__global__ void mae_restore_bwd_kernel(const bf16* __restrict__ dout, const int64_t* __restrict__ restore,
+                                       bf16* __restrict__ dvis, float* __restrict__ dtok, int B, int N, int K, int d) {
+  extern __shared__ float part[];  // [d]
+  for (int i = threadIdx.x; i < d; i += blockDim.x) part[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x % 32;
+  const int warps = blockDim.x / 32;
+  constexpr int kMaxVec = 8;  // d <= 2048
+  float acc[kMaxVec * 8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec * 8; ++i) acc[i] = 0.f;
+  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < B * N; row += gridDim.x * warps) {
+    const int b = row / N;
+    const int64_t r = restore[row];
+    const uint4* src = reinterpret_cast<const uint4*>(dout + (size_t)row * d);
+    if (r < K) {
+      uint4* dst = reinterpret_cast<uint4*>(dvis + ((size_t)b * K + r) * d);
+      for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
+    } else {
+#pragma unroll
+      for (int vi = 0; vi < kMaxVec; ++vi) {
+        const int c = lane + 32 * vi;
+        if (c < d / 8) {
+          uint4 u = src[c];
+          uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            acc[vi * 8 + 2 * h] += bf16_lo(w[h]);
+            acc[vi * 8 + 2 * h + 1] += bf16_hi(w[h]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int vi = 0; vi < kMaxVec; ++vi) {
+    const int c = lane + 32 * vi;
+    if (c < d / 8)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) atomicAdd(&part[c * 8 + e], acc[vi * 8 + e]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x) atomicAdd(dtok + i, part[i]);
+}
+
+void mae_restore_fwd(torch::Tensor visible, torch::Tensor token, torch::Tensor restore, torch::Tensor out) {
+  TORCH_CHECK(visible.scalar_type() == at::kBFloat16 && visible.is_contiguous(), "mae_restore: bf16 visible");
+  const int B = (int)restore.size(0), N = (int)restore.size(1), K = (int)visible.size(1), d = (int)visible.size(2);
+  TORCH_CHECK(d % 8 == 0, "mae_restore: width must be a multiple of 8");
+  c10::cuda::CUDAGuard guard(visible.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const long rows = (long)B * N;
+  if (rows == 0) return;
+  mae_restore_fwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const bf16*>(visible.data_ptr()), reinterpret_cast<const bf16*>(token.data_ptr()),
+      restore.data_ptr<int64_t>(), reinterpret_cast<bf16*>(out.data_ptr()), B, N, K, d);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mae_restore_bwd(torch::Tensor dout, torch::Tensor restore, torch::Tensor dvis, torch::Tensor dtok) {
+  const int B = (int)restore.size(0), N = (int)restore.size(1), K = (int)dvis.size(1), d = (int)dvis.size(2);
+  TORCH_CHECK(d % 8 == 0 && d <= 2048, "mae_restore_bwd: width must be a multiple of 8 and at most 2048");
+  c10::cuda::CUDAGuard guard(dout.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dout.get_device()));
+  const int grid = std::max(1, std::min(sms, (B * N + 7) / 8));
+  mae_restore_bwd_kernel<<<grid, 256, d * sizeof(float), stream>>>(
+      reinterpret_cast<const bf16*>(dout.data_ptr()), restore.data_ptr<int64_t>(),
+      reinterpret_cast<bf16*>(dvis.data_ptr()), dtok.data_ptr<float>(), B, N, K, d);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// One CTA per (b, n) patch. Masked patches: target = (x - mean) / sqrt(var_unbiased + 1e-6) (or x
+// itself), loss += sum((pred - target)^2) / P / count, grad = 2 (pred - target) / P / count.
+// Visible patches: grad = 0. `count` = max(1, sum(mask)) is read from the device.
+template <typename TP, typename TV>
+__global__ void norm_pix_mse_kernel(const TP* __restrict__ pred, const TV* __restrict__ vol,
+                                    const float* __restrict__ mask, const float* __restrict__ count,
+                                    float* __restrict__ loss, TP* __restrict__ grad, int C, int D, int H, int W,
+                                    int pd, int ph, int pw, int N, int norm_pix) {
+  constexpr int kMaxPer = 64;  // P <= 256 * 64
+  const int row = blockIdx.x;
+  const int b = row / N, n = row % N;
+  const int vp = pd * ph * pw;
+  const int P = C * vp;
+  const TP* pr = pred + (size_t)row * P;
+  TP* gr = grad + (size_t)row * P;
+  const float mk = mask[row];
+  if (mk == 0.f) {
+    for (int e = threadIdx.x; e < P; e += blockDim.x) gr[e] = from_f<TP>(0.f);
+    return;
+  }
+  const int gh = H / ph, gw = W / pw;
+  const int zd = n / (gh * gw), zh = (n / gw) % gh, zw = n % gw;
+  float x[kMaxPer];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = threadIdx.x + i * blockDim.x;
+    x[i] = 0.f;
+    if (e < P) {
+      const int c = e / vp;
+      int r = e % vp;
+      const int a = r / (ph * pw);
+      r %= ph * pw;
+      const int j = r / pw, l = r % pw;
+      x[i] = to_f<TV>(vol[((((size_t)b * C + c) * D + (zd * pd + a)) * H + (zh * ph + j)) * W + (zw * pw + l)]);
+      s += x[i];
+    }
+  }
+  __shared__ float red[32];
+  auto block_sum = [&](float v) -> float {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < (int)blockDim.x / 32; ++w) tot += red[w];
+    return tot;
+  };
+  float mean = 0.f, inv = 1.f;
+  if (norm_pix) {
+    mean = block_sum(s) / P;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int e = threadIdx.x + i * blockDim.x;
+      if (e < P) ss += (x[i] - mean) * (x[i] - mean);
+    }
+    const float var = block_sum(ss) / (float)(P > 1 ? P - 1 : 1);
+    inv = rsqrtf(var + 1e-6f);
+  }
+  const float cnt = *count;
+  const float gscale = 2.f / (float)P / cnt;
+  float se = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = threadIdx.x + i * blockDim.x;
+    if (e < P) {
+      const float tgt = (x[i] - mean) * inv;
+      const float diff = to_f<TP>(pr[e]) - tgt;
+      se += diff * diff;
+      gr[e] = from_f<TP>(diff * gscale * mk);
+    }
+  }
+  const float tot = block_sum(se);
+  if (threadIdx.x == 0) atomicAdd(loss, tot * mk / (float)P / cnt);
+}
+
+void norm_pix_mse(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, torch::Tensor loss, torch::Tensor grad,
+                  int64_t pd, int64_t ph, int64_t pw, bool norm_pix) {
+  TORCH_CHECK(pred.is_contiguous() && vol.is_contiguous() && mask.is_contiguous(), "norm_pix_mse: contiguous inputs");
+  const int B = (int)vol.size(0), C = (int)vol.size(1), D = (int)vol.size(2), H = (int)vol.size(3), W = (int)vol.size(4);
+  const int N = (int)pred.size(1);
+  const int P = (int)pred.size(2);
+  TORCH_CHECK(P == C * pd * ph * pw && P <= 256 * 64, "norm_pix_mse: patch width mismatch or too large");
+  c10::cuda::CUDAGuard guard(pred.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  auto count = mask.sum().clamp_min(1.0);
+  C10_CUDA_CHECK(cudaMemsetAsync(loss.data_ptr(), 0, sizeof(float), stream));
+  auto launch = [&](auto p_tag, auto v_tag) {
+    using TP = decltype(p_tag);
+    using TV = decltype(v_tag);
+    norm_pix_mse_kernel<TP, TV><<<B * N, 256, 0, stream>>>(
+        reinterpret_cast<const TP*>(pred.data_ptr()), reinterpret_cast<const TV*>(vol.data_ptr()), mask.data_ptr<float>(),
+        count.data_ptr<float>(), loss.data_ptr<float>(), reinterpret_cast<TP*>(grad.data_ptr()), C, D, H, W, (int)pd,
+        (int)ph, (int)pw, N, norm_pix ? 1 : 0);
+  };
+  const bool pf = pred.scalar_type() == at::kFloat, vf = vol.scalar_type() == at::kFloat;
+  if (pf && vf) launch(float{}, float{});
+  else if (pf && !vf) launch(float{}, bf16{});
+  else if (!pf && vf) launch(bf16{}, float{});
+  else launch(bf16{}, bf16{});
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mia

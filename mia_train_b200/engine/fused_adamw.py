@@ -8,7 +8,9 @@ checkpoints interchange with the stock optimizer, and the same param-group field
 Per step it issues one host->device copy of the per-group (lr, weight_decay, beta1, beta2) table
 and one kernel launch over every parameter; `step` counters live on the device. An optional
 device-side `grad_scale` (the grad-clip coefficient) is applied as gradients are read. Parameters
-whose grad is None are skipped, and their step does not advance, as in torch.
+whose grad is None are skipped, and their step does not advance, as in torch. A parameter with a
+`main_grad` buffer (see `ops/_params.py`) is updated from it, and one with a `_mia_shadow` bf16
+copy gets that copy rewritten by the same kernel.
 """
 
 from __future__ import annotations
@@ -47,6 +49,9 @@ class FusedAdamW(Optimizer):
         return state
 
     def _hyper(self, device: torch.device) -> torch.Tensor:
+        external = getattr(self, "external_hyper", None)
+        if external is not None:  # a device-side schedule (see engine/graph_step.py)
+            return external
         g = len(self.param_groups)
         if self._hyper_host is None or self._hyper_host.shape[0] != g:
             self._hyper_host = torch.empty((g, 4), dtype=torch.float32, pin_memory=torch.cuda.is_available())
@@ -64,17 +69,22 @@ class FusedAdamW(Optimizer):
     @torch.no_grad()
     def step(self, closure: Any = None) -> Any:  # type: ignore[override]
         loss = closure() if closure is not None else None
-        params, grads, m, v, steps, gidx = [], [], [], [], [], []
+        params, grads, m, v, steps, gidx, shadows = [], [], [], [], [], [], []
         eps = None
+        have_shadow = False
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
-                if p.grad is None:
+                grad = p.grad if p.grad is not None else getattr(p, "main_grad", None)
+                if grad is None:
                     continue
-                if p.grad.is_sparse:
+                if grad.is_sparse:
                     raise RuntimeError("FusedAdamW does not support sparse gradients")
                 state = self._init_state(p)
                 params.append(p)
-                grads.append(p.grad)
+                grads.append(grad)
+                shadow = getattr(p, "_mia_shadow", None)
+                have_shadow = have_shadow or shadow is not None
+                shadows.append(shadow if shadow is not None else self._empty(p.device))
                 m.append(state["exp_avg"])
                 v.append(state["exp_avg_sq"])
                 steps.append(state["step"])
@@ -90,5 +100,14 @@ class FusedAdamW(Optimizer):
         cached = getattr(self, "_gidx_cache", None)
         if cached is None or cached[0] != key:
             self._gidx_cache = (key, torch.tensor(gidx, dtype=torch.int32, device=device))
-        adamw_step(params, grads, m, v, steps, self._gidx_cache[1], hyper, float(eps), self.grad_scale)
+        adamw_step(
+            params, grads, m, v, steps, self._gidx_cache[1], hyper, float(eps), self.grad_scale,
+            shadows if have_shadow else None,
+        )
         return loss
+
+    def _empty(self, device: torch.device) -> torch.Tensor:
+        cache = self.__dict__.setdefault("_empty_cache", {})
+        if device not in cache:
+            cache[device] = torch.empty(0, device=device, dtype=torch.bfloat16)
+        return cache[device]

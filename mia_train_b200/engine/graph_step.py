@@ -1,0 +1,261 @@
+"""A whole training step (forward, backward, grad clip, AdamW, schedule) captured in one CUDA graph.
+
+The reference runs every step eagerly from Python: ~800 kernel launches per ViT-L MAE step, each
+with autograd and dispatcher overhead on the host. Here the step is recorded once and replayed, so
+the host issues a single graph launch per step and the device never waits for Python.
+
+What makes the step capturable:
+
+* `FlatParameters` packs every trainable parameter into one flat fp32 buffer (64-element aligned
+  slots) with a flat fp32 gradient buffer. Each parameter gets `main_grad` (its slice of the
+  gradient buffer) and, for matrices, `_mia_shadow` (a bf16 copy). Native backward kernels
+  accumulate weight gradients straight into `main_grad`; gradients that arrive through autograd
+  (parameters no native kernel owns) are folded in by a post-accumulate hook. The fused AdamW
+  updates params and rewrites the bf16 shadows in the same pass, so GEMMs never cast weights.
+* The learning-rate / weight-decay schedule is precomputed per step into a device table indexed by
+  a device step counter, so nothing host-side changes between replays.
+* Gradient clipping computes the global norm on the device and hands the clip coefficient to the
+  AdamW kernel (no host synchronisation).
+* Inputs are copied into static device buffers before each replay (from pinned host memory when
+  the caller passes host tensors).
+
+The first `eager_steps` calls run eagerly (they are real training steps and settle the allocator
+and every lazily built table), the next call captures and replays. Metrics come back as static
+device tensors; reading them is the caller's only synchronisation.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable, Mapping
+from typing import Any
+
+import torch
+import torch.nn as nn
+
+from ..ops.optim import clip_coefficient, grad_sumsq
+from .config import TrainerConfig
+from .optimizer import lr_multiplier, weight_decay_at
+
+_ALIGN = 64
+
+
+class FlatParameters:
+    """Every trainable parameter of `module` as a view into flat fp32 param/grad buffers."""
+
+    def __init__(self, module: nn.Module, shadow_min_dim: int = 2) -> None:
+        seen: set[int] = set()
+        params: list[nn.Parameter] = []
+        for p in module.parameters():
+            if p.requires_grad and id(p) not in seen:
+                seen.add(id(p))
+                params.append(p)
+        if not params:
+            raise ValueError("FlatParameters: nothing requires grad")
+        device = params[0].device
+        offsets, total = [], 0
+        shadow_offsets, shadow_total = [], 0
+        for p in params:
+            offsets.append(total)
+            total += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
+            if p.ndim >= shadow_min_dim:
+                shadow_offsets.append(shadow_total)
+                shadow_total += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
+            else:
+                shadow_offsets.append(None)
+        self.params = params
+        self.data = torch.zeros(total, dtype=torch.float32, device=device)
+        self.grad = torch.zeros(total, dtype=torch.float32, device=device)
+        self.shadow = torch.zeros(max(shadow_total, 1), dtype=torch.bfloat16, device=device)
+        self._hooks = []
+        with torch.no_grad():
+            for p, off, soff in zip(params, offsets, shadow_offsets, strict=True):
+                n = p.numel()
+                view = self.data[off:off + n].view_as(p)
+                view.copy_(p.data)
+                p.data = view
+                p.main_grad = self.grad[off:off + n].view_as(p)  # type: ignore[attr-defined]
+                if soff is not None:
+                    sview = self.shadow[soff:soff + n].view_as(p)
+                    sview.copy_(view)
+                    p._mia_shadow = sview  # type: ignore[attr-defined]
+                self._hooks.append(p.register_post_accumulate_grad_hook(_fold_into_main_grad))
+        self.numel = sum(p.numel() for p in params)
+
+    def zero_grad(self) -> None:
+        self.grad.zero_()
+
+    @torch.no_grad()
+    def refresh_shadows(self) -> None:
+        """Re-derive the bf16 copies from the fp32 params (after loading weights)."""
+        for p in self.params:
+            shadow = getattr(p, "_mia_shadow", None)
+            if shadow is not None:
+                shadow.copy_(p.data)
+
+    def release(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        for p in self.params:
+            for attr in ("main_grad", "_mia_shadow"):
+                if hasattr(p, attr):
+                    delattr(p, attr)
+
+
+def _fold_into_main_grad(p: torch.Tensor) -> None:
+    if p.grad is not None and getattr(p, "main_grad", None) is not None:
+        p.main_grad.add_(p.grad)  # type: ignore[attr-defined]
+        p.grad = None
+
+
+class DeviceSchedule:
+    """Per-step (lr, weight_decay, beta1, beta2) for every param group, as a device table."""
+
+    def __init__(self, optimizer: torch.optim.Optimizer, config: TrainerConfig, start_step: int = 0) -> None:
+        device = next(p.device for g in optimizer.param_groups for p in g["params"])
+        steps = config.max_steps + 1
+        table = torch.empty((steps, len(optimizer.param_groups), 4), dtype=torch.float32)
+        for s in range(steps):
+            mult = lr_multiplier(s, config)
+            wd = weight_decay_at(s, config)
+            for gi, group in enumerate(optimizer.param_groups):
+                base_lr = group.get("initial_lr", group["lr"])
+                b1, b2 = group["betas"]
+                table[s, gi, 0] = base_lr * mult
+                table[s, gi, 1] = wd * group.get("wd_multiplier", 1.0)
+                table[s, gi, 2] = b1
+                table[s, gi, 3] = b2
+        self.table = table.to(device)
+        self.counter = torch.tensor([start_step], dtype=torch.int64, device=device)
+        self.current = torch.empty((len(optimizer.param_groups), 4), dtype=torch.float32, device=device)
+        self.last_index = steps - 1
+
+    def advance(self) -> torch.Tensor:
+        """Load this step's row into `current`, then move the counter on (clamped at the end)."""
+        idx = self.counter.clamp(max=self.last_index)
+        self.current.copy_(self.table.index_select(0, idx)[0])
+        self.counter.add_(1)
+        return self.current
+
+
+def _to_static(batch: Any, device: torch.device) -> Any:
+    if isinstance(batch, torch.Tensor):
+        return torch.empty(batch.shape, dtype=batch.dtype, device=device)
+    if isinstance(batch, Mapping):
+        return {k: _to_static(v, device) for k, v in batch.items()}
+    if isinstance(batch, (list, tuple)):
+        return type(batch)(_to_static(v, device) for v in batch)
+    return batch
+
+
+def _copy_into(static: Any, batch: Any) -> None:
+    if isinstance(static, torch.Tensor):
+        static.copy_(batch, non_blocking=True)
+    elif isinstance(static, Mapping):
+        for k in static:
+            _copy_into(static[k], batch[k])
+    elif isinstance(static, (list, tuple)):
+        for s, b in zip(static, batch, strict=True):
+            _copy_into(s, b)
+
+
+class CapturedStep:
+    """`step(batch) -> metrics` for one training step, replayed from a CUDA graph after warm-up."""
+
+    def __init__(
+        self,
+        algorithm: nn.Module,
+        optimizer: torch.optim.Optimizer,
+        config: TrainerConfig,
+        example_batch: Any,
+        *,
+        eager_steps: int = 2,
+        start_step: int = 0,
+        capture: bool = True,
+        forward: Callable[[Any], dict[str, torch.Tensor]] | None = None,
+        process_group: Any = None,
+    ) -> None:
+        if not hasattr(optimizer, "grad_scale"):
+            raise TypeError("CapturedStep needs the fused optimizer (FusedAdamW)")
+        self.algorithm = algorithm
+        self.optimizer = optimizer
+        self.config = config
+        self.device = next(algorithm.parameters()).device
+        self.flat = FlatParameters(algorithm)
+        self.schedule = DeviceSchedule(optimizer, config, start_step)
+        optimizer.external_hyper = self.schedule.current  # type: ignore[attr-defined]
+        self.static_batch = _to_static(example_batch, self.device)
+        self.static_metrics: dict[str, torch.Tensor] = {}
+        self.eager_steps = eager_steps
+        self.capture = capture
+        self.calls = 0
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self._forward = forward or algorithm
+        self._autocast_dtype = torch.bfloat16 if config.precision == "bf16" else None
+        self.process_group = process_group
+        self.world = 1
+        if process_group is not None:
+            import torch.distributed as dist
+
+            self.world = dist.get_world_size(process_group)
+
+    def _body(self) -> dict[str, torch.Tensor]:
+        self.flat.zero_grad()
+        self.schedule.advance()
+        if self._autocast_dtype is not None:
+            with torch.autocast("cuda", dtype=self._autocast_dtype):
+                metrics = self._forward(self.static_batch)
+        else:
+            metrics = self._forward(self.static_batch)
+        metrics["loss"].backward()
+        out = {k: v.detach() for k, v in metrics.items()}
+        if self.world > 1:
+            import torch.distributed as dist
+
+            # Data parallel: sum the flat gradient over ranks (NCCL, captured in the graph); the
+            # 1/world average is folded into the scale the AdamW kernel applies.
+            dist.all_reduce(self.flat.grad, group=self.process_group)
+        inv_world = 1.0 / self.world
+        if self.config.grad_clip_norm is not None:
+            norm = grad_sumsq([self.flat.grad]).sqrt() * inv_world
+            self.optimizer.grad_scale = clip_coefficient(norm, float(self.config.grad_clip_norm)) * inv_world
+            out["grad_norm"] = norm
+        elif self.world > 1:
+            self.optimizer.grad_scale = torch.full((), inv_world, device=self.device)
+        self.optimizer.step()
+        return out
+
+    def _store(self, out: dict[str, torch.Tensor]) -> None:
+        for k, v in out.items():
+            v = v.float().reshape(())
+            if k not in self.static_metrics:
+                self.static_metrics[k] = torch.zeros((), dtype=torch.float32, device=self.device)
+            self.static_metrics[k].copy_(v)
+
+    def _capture(self) -> None:
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._store(self._body())
+        self.graph = graph
+
+    def load_batch(self, batch: Any) -> None:
+        _copy_into(self.static_batch, batch)
+
+    def __call__(self, batch: Any | None = None) -> dict[str, torch.Tensor]:
+        """Run one step on `batch` (host tensors are copied in; None reuses the static batch)."""
+        if batch is not None:
+            self.load_batch(batch)
+        self.calls += 1
+        if not self.capture or self.calls <= self.eager_steps:
+            self._store(self._body())
+            return self.static_metrics
+        if self.graph is None:
+            self._capture()
+        self.graph.replay()
+        return self.static_metrics
+
+    def release(self) -> None:
+        self.graph = None
+        self.flat.release()
+        if hasattr(self.optimizer, "external_hyper"):
+            del self.optimizer.external_hyper

@@ -153,8 +153,7 @@ class ViT3D(BaseModel):
             )
         cdtype = compute_dtype(x) if x.is_cuda else x.dtype
         rows = patchify_op(x, self.patch_size, index, out_dtype=cdtype)
-        weight = self.patch_embed.weight.reshape(self.embed_dim, -1)
-        tokens = linear(rows, weight, self.patch_embed.bias)
+        tokens = linear(rows, self.patch_embed.weight, self.patch_embed.bias)
         coords = self.patch_coords(x.shape[0], x.device)
         if index is not None:
             coords = torch.gather(coords, 1, index.unsqueeze(-1).expand(-1, -1, SPATIAL_RANK))

@@ -69,16 +69,12 @@ class _NativeRopeAttention(torch.autograd.Function):
     def backward(ctx, do):  # type: ignore[override]
         q, k, v, o, lse, ang, pairs = ctx.saved_tensors
         do = do.to(q.dtype).contiguous()
-        dq = torch.empty_like(q)
-        dk = torch.empty_like(k)
-        dv = torch.empty_like(v)
-        native().attention_bwd(q, k, v, o, do, lse, dq, dk, dv, float(ctx.scale))
         b, h, n, d = q.shape
         dqkv = torch.empty((b, n, 3, h, d), device=q.device, dtype=q.dtype)
         dang = None
         if ang is not None:
-            dang = torch.zeros((b, n, pairs.shape[0]), device=q.device, dtype=torch.float32)
-        native().rope_split_bwd(dq, dk, dv, q, k, ang, pairs, dqkv, dang)
+            dang = torch.zeros((ang.shape[0] if ang.shape[0] == b else b, n, pairs.shape[0]), device=q.device, dtype=torch.float32)
+        native().rope_attention_bwd(q, k, v, o, do, lse, ang, pairs, dqkv, dang, float(ctx.scale))
         if dang is not None and ctx.angles_shape[0] == 1 and b != 1:
             dang = dang.sum(0, keepdim=True)
         if dang is not None:

@@ -23,6 +23,7 @@ import torch
 import torch.nn.functional as F
 
 from ._native import native, use_native
+from ._params import compute_weight, grad_sink
 
 ACT_NONE, ACT_GELU, ACT_DGELU = 0, 1, 2
 _ACTS = {None: ACT_NONE, "none": ACT_NONE, "gelu": ACT_GELU}
@@ -112,10 +113,6 @@ def column_sum(x: torch.Tensor, out: torch.Tensor | None = None, accumulate: boo
     return out
 
 
-def _accumulate_grad(param: torch.Tensor, grad: torch.Tensor) -> torch.Tensor:
-    return grad if grad.dtype == param.dtype else grad.to(param.dtype)
-
-
 class _NativeLinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias, residual, gamma, act, cdtype):  # type: ignore[override]
@@ -124,7 +121,7 @@ class _NativeLinear(torch.autograd.Function):
         if x2.dtype != cdtype:
             x2 = x2.to(cdtype)
         x2 = x2.contiguous()
-        w = weight.to(cdtype).contiguous()
+        w = compute_weight(weight, cdtype).reshape(weight.shape[0], -1).contiguous()
         res2 = None
         if residual is not None:
             res2 = residual.reshape(-1, weight.shape[0])
@@ -137,6 +134,8 @@ class _NativeLinear(torch.autograd.Function):
         y = gemm(x2, w, out_dtype=cdtype, bias=bf, residual=res2, gamma=g, act=act, aux_out=pre)
         ctx.save_for_backward(x2, w, pre, g, bf)
         ctx.meta = (shape, act, bias is not None, residual is not None, gamma is not None, weight.dtype)
+        ctx.weight_shape = weight.shape
+        ctx.sinks = (grad_sink(weight), grad_sink(bias))
         return y.reshape(*shape[:-1], weight.shape[0])
 
     @staticmethod
@@ -161,11 +160,20 @@ class _NativeLinear(torch.autograd.Function):
         dx = None
         if ctx.needs_input_grad[0]:
             dx = gemm(dz, w, b_kmajor=False, out_dtype=x2.dtype).reshape(shape)
+        w_sink, b_sink = ctx.sinks
         dw = None
         if ctx.needs_input_grad[1]:
-            dw = gemm(dz, x2, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32)
-            dw = _accumulate_grad(w, dw) if wdtype != torch.float32 else dw
-        db = column_sum(dz).to(wdtype) if (has_bias and ctx.needs_input_grad[2]) else None
+            if w_sink is not None:
+                gemm(dz, x2, a_kmajor=False, b_kmajor=False, out=w_sink.view(w.shape), accumulate=True)
+            else:
+                dw = gemm(dz, x2, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32)
+                dw = dw.to(wdtype).view(ctx.weight_shape)
+        db = None
+        if has_bias and ctx.needs_input_grad[2]:
+            if b_sink is not None:
+                column_sum(dz, out=b_sink, accumulate=True)
+            else:
+                db = column_sum(dz).to(wdtype)
         return dx, dw, db, dres, dgamma, None, None
 
 
@@ -177,12 +185,16 @@ def linear(
     residual: torch.Tensor | None = None,
     gamma: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """`residual + gamma * act(x @ weight.T + bias)`; see the module docstring."""
+    """`residual + gamma * act(x @ weight.T + bias)`; see the module docstring.
+
+    `weight` may have more than two dims (a kernel == stride convolution's weight): its trailing
+    dims are flattened, in the convolution's own order.
+    """
     act = _ACTS[activation]
     cdtype = compute_dtype(x)
     if cdtype == torch.bfloat16 and use_native(x) and x.shape[-1] % 8 == 0 and weight.shape[0] % 8 == 0:
         return _NativeLinear.apply(x, weight, bias, residual, gamma, act, cdtype)
-    y = F.linear(x, weight, bias)
+    y = F.linear(x, weight.reshape(weight.shape[0], -1), bias)
     if act == ACT_GELU:
         y = F.gelu(y)
     if gamma is not None:

@@ -13,6 +13,7 @@ import torch
 import torch.nn.functional as F
 
 from ._native import native, use_native
+from ._params import grad_sink
 
 
 class _NativeLayerNorm(torch.autograd.Function):
@@ -28,6 +29,7 @@ class _NativeLayerNorm(torch.autograd.Function):
         b = bias.float().contiguous() if bias is not None else None
         native().layernorm_fwd(x2, w, b, y, mean, rstd, float(eps), bool(rms))
         ctx.save_for_backward(x2, w, mean, rstd)
+        ctx.sinks = (grad_sink(weight), grad_sink(bias))
         ctx.meta = (shape, weight is not None, bias is not None, rms,
                     weight.dtype if weight is not None else None, bias.dtype if bias is not None else None)
         return y.reshape(shape)
@@ -39,13 +41,14 @@ class _NativeLayerNorm(torch.autograd.Function):
         dy2 = dy.reshape(x2.shape).to(x2.dtype).contiguous()
         dx = torch.empty_like(x2)
         n = x2.shape[1]
-        dw = torch.zeros(n, device=x2.device, dtype=torch.float32) if has_w else None
-        db = torch.zeros(n, device=x2.device, dtype=torch.float32) if has_b else None
+        w_sink, b_sink = ctx.sinks
+        dw = (w_sink if w_sink is not None else torch.zeros(n, device=x2.device, dtype=torch.float32)) if has_w else None
+        db = (b_sink if b_sink is not None else torch.zeros(n, device=x2.device, dtype=torch.float32)) if has_b else None
         native().layernorm_bwd(dy2, x2, w, mean, rstd, dx, dw, db, bool(rms))
         return (
             dx.reshape(shape),
-            dw.to(wdtype) if dw is not None else None,
-            db.to(bdtype) if db is not None else None,
+            dw.to(wdtype) if (dw is not None and w_sink is None) else None,
+            db.to(bdtype) if (db is not None and b_sink is None) else None,
             None,
             None,
         )

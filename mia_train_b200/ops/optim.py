@@ -41,13 +41,17 @@ def adamw_step(
     hyper: torch.Tensor,
     eps: float,
     grad_scale: torch.Tensor | None,
+    shadows: list[torch.Tensor] | None = None,
 ) -> None:
     """One AdamW update for every tensor; `hyper[g] = (lr, weight_decay, beta1, beta2)` per group.
 
     Steps are incremented in the kernel; bias corrections use the incremented step, as
-    `torch.optim.AdamW` does.
+    `torch.optim.AdamW` does. `shadows[i]` (an empty tensor for none) receives the updated
+    parameter in bf16.
     """
-    native().adamw_step(params, grads, exp_avgs, exp_avg_sqs, steps, group_index, hyper, float(eps), grad_scale)
+    native().adamw_step(
+        params, grads, exp_avgs, exp_avg_sqs, steps, group_index, hyper, float(eps), grad_scale, shadows or []
+    )
 
 
 def adamw_reference(

@@ -1,0 +1,268 @@
+"""Numerics of every native kernel against a plain fp32 PyTorch version of the same op.
+
+Run on a B200: `python -m pytest tests -m gpu`. Each test also checks that no kernel recorded a
+bounded-wait timeout in the device error word.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover - collected on CPU, skipped there
+    pytest.skip("needs CUDA", allow_module_level=True)
+
+from mia_train_b200.ops import _native  # noqa: E402
+from mia_train_b200.ops.linear import ACT_DGELU, ACT_GELU, gelu_grad_reference, gemm  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def _no_errors():
+    torch.cuda.synchronize()
+    assert _native.native().check_errors(0) == 0
+
+
+def _close(actual, expected, rel=2e-2, atol=2e-2):
+    a, e = actual.float(), expected.float()
+    err = (a - e).abs().max().item()
+    scale = e.abs().max().item() + 1e-6
+    assert err <= atol + rel * scale, f"max error {err:.4g} vs scale {scale:.4g}"
+
+
+@pytest.mark.parametrize("a_k,b_k", [(True, True), (True, False), (False, True), (False, False)])
+@pytest.mark.parametrize("mnk", [(256, 256, 128), (384, 648, 200), (128, 136, 64), (2048, 3072, 1024), (1000, 512, 4096)])
+def test_gemm_layouts(a_k, b_k, mnk):
+    m, n, k = mnk
+    torch.manual_seed(0)
+    a = torch.randn(m, k, device=DEV).bfloat16()
+    b = torch.randn(n, k, device=DEV).bfloat16()
+    ref = a.float() @ b.float().t()
+    a_in = a if a_k else a.t().contiguous()
+    b_in = b if b_k else b.t().contiguous()
+    out = gemm(a_in, b_in, a_kmajor=a_k, b_kmajor=b_k, out_dtype=torch.float32)
+    _close(out, ref, rel=1e-2, atol=1e-2 * math.sqrt(k))
+    _no_errors()
+
+
+def test_gemm_epilogues():
+    torch.manual_seed(1)
+    m, n, k = 512, 768, 320
+    a = torch.randn(m, k, device=DEV).bfloat16()
+    b = (torch.randn(n, k, device=DEV) * 0.05).bfloat16()
+    bias = torch.randn(n, device=DEV)
+    gamma = torch.rand(n, device=DEV)
+    res = torch.randn(m, n, device=DEV).bfloat16()
+    acc = a.float() @ b.float().t() + bias
+    pre = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    y = gemm(a, b, bias=bias, act=ACT_GELU, aux_out=pre)
+    _close(pre, acc, rel=1e-2, atol=5e-2)
+    _close(y, F.gelu(acc), rel=1e-2, atol=5e-2)
+    y2 = gemm(a, b, bias=bias, gamma=gamma, residual=res)
+    _close(y2, res.float() + gamma * acc, rel=1e-2, atol=5e-2)
+    y3 = gemm(a, b, act=ACT_DGELU, aux=res)
+    _close(y3, (a.float() @ b.float().t()) * gelu_grad_reference(res.float()), rel=1e-2, atol=5e-2)
+    out = torch.randn(m, n, device=DEV)
+    base = out.clone()
+    gemm(a, b, out=out, accumulate=True)
+    _close(out, base + a.float() @ b.float().t(), rel=1e-2, atol=5e-2)
+    _no_errors()
+
+
+def test_column_sum():
+    from mia_train_b200.ops.linear import column_sum
+
+    x = torch.randn(3000, 520, device=DEV).bfloat16()
+    _close(column_sum(x), x.float().sum(0), rel=1e-3, atol=1e-2)
+    _no_errors()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rms", [False, True])
+def test_layernorm(dtype, rms):
+    from mia_train_b200.ops.norm import layer_norm, rms_norm
+
+    torch.manual_seed(2)
+    x = (torch.randn(777, 1024, device=DEV) * 3 + 1).to(dtype).requires_grad_(True)
+    w = torch.randn(1024, device=DEV, requires_grad=True)
+    b = torch.randn(1024, device=DEV, requires_grad=True)
+    dy = torch.randn(777, 1024, device=DEV).to(dtype)
+    if rms:
+        y = rms_norm(x, w, 1e-6)
+        xf = x.detach().float().requires_grad_(True)
+        wf = w.detach().clone().requires_grad_(True)
+        ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * wf
+        params, ref_params = (w,), (wf,)
+    else:
+        y = layer_norm(x, w, b, 1e-5)
+        xf = x.detach().float().requires_grad_(True)
+        wf = w.detach().clone().requires_grad_(True)
+        bf = b.detach().clone().requires_grad_(True)
+        ref = F.layer_norm(xf, (1024,), wf, bf, 1e-5)
+        params, ref_params = (w, b), (wf, bf)
+    _close(y, ref)
+    y.backward(dy)
+    ref.backward(dy.float())
+    _close(x.grad, xf.grad, rel=2e-2, atol=5e-2)
+    for p, rp in zip(params, ref_params, strict=True):
+        _close(p.grad, rp.grad, rel=1e-2, atol=1e-1)
+    _no_errors()
+
+
+@pytest.mark.parametrize("shape", [(2, 4, 128, 64), (2, 3, 200, 32), (1, 2, 512, 32), (1, 2, 96, 128)])
+def test_attention_fwd_bwd(shape):
+    from mia_train_b200.ops.attention import attention
+
+    torch.manual_seed(3)
+    b, h, n, d = shape
+    q = torch.randn(b, n, h, d, device=DEV).bfloat16().requires_grad_(True)
+    k = torch.randn(b, n, h, d, device=DEV).bfloat16().requires_grad_(True)
+    v = torch.randn(b, n, h, d, device=DEV).bfloat16().requires_grad_(True)
+    scale = d**-0.5
+    out = attention(q, k, v, scale)
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ref = F.scaled_dot_product_attention(qf.transpose(1, 2), kf.transpose(1, 2), vf.transpose(1, 2), scale=scale).transpose(1, 2)
+    _close(out, ref)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    ref.backward(dout.float())
+    for g, rg in ((q.grad, qf.grad), (k.grad, kf.grad), (v.grad, vf.grad)):
+        _close(g, rg, rel=3e-2, atol=3e-2)
+    _no_errors()
+
+
+def test_rope_attention_matches_reference():
+    from mia_train_b200.layers.common.rope import AxialRotaryEmbedding
+    from mia_train_b200.ops import attention as attn_ops
+
+    torch.manual_seed(4)
+    b, n, h, d = 2, 128, 4, 64
+    rot = AxialRotaryEmbedding(d, 3).to(DEV)
+    coords = torch.randint(0, 8, (b, n, 3), device=DEV).float()
+    qkv = torch.randn(b, n, 3, h, d, device=DEV).bfloat16().requires_grad_(True)
+    tables = rot(coords)
+    out = attn_ops.rope_attention(qkv, tables.angles, tables.pairs, d**-0.5)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    g_native = qkv.grad.clone()
+    f_native = [f.grad.clone() for f in rot.inv_freqs]
+    qkv.grad = None
+    for f in rot.inv_freqs:
+        f.grad = None
+    with _native.reference_math():
+        qkv32 = qkv.detach().float().requires_grad_(True)
+        tables = rot(coords)
+        ref = attn_ops.rope_attention(qkv32, tables.angles, tables.pairs, d**-0.5)
+        ref.backward(dout.float())
+    _close(out, ref)
+    _close(g_native, qkv32.grad, rel=3e-2, atol=3e-2)
+    for fn, f in zip(f_native, rot.inv_freqs, strict=True):
+        _close(fn, f.grad, rel=5e-2, atol=5e-2)
+    _no_errors()
+
+
+def test_fused_adamw_matches_torch():
+    from mia_train_b200.engine.fused_adamw import FusedAdamW
+
+    torch.manual_seed(5)
+    shapes = [(300, 70), (1000,), (64, 64, 3), (5,)]
+    params = [torch.randn(s, device=DEV, requires_grad=True) for s in shapes]
+    ref_params = [p.detach().clone().requires_grad_(True) for p in params]
+    groups = [{"params": params[:2], "weight_decay": 0.1}, {"params": params[2:], "weight_decay": 0.0, "lr": 3e-3}]
+    ref_groups = [{"params": ref_params[:2], "weight_decay": 0.1}, {"params": ref_params[2:], "weight_decay": 0.0, "lr": 3e-3}]
+    opt = FusedAdamW(groups, lr=1e-3, betas=(0.9, 0.95))
+    ref = torch.optim.AdamW(ref_groups, lr=1e-3, betas=(0.9, 0.95))
+    for _ in range(5):
+        for p, rp in zip(params, ref_params, strict=True):
+            g = torch.randn_like(p)
+            p.grad = g.clone()
+            rp.grad = g.clone()
+        opt.step()
+        ref.step()
+    for p, rp in zip(params, ref_params, strict=True):
+        torch.testing.assert_close(p, rp, rtol=1e-5, atol=1e-6)
+    assert float(opt.state[params[0]]["step"]) == 5.0
+    _no_errors()
+
+
+def test_clip_grad_norm_native():
+    from mia_train_b200.ops.optim import clip_grad_norm_native
+
+    params = [torch.nn.Parameter(torch.randn(s, device=DEV)) for s in [(100, 10), (7,), (33, 33)]]
+    for p in params:
+        p.grad = torch.randn_like(p) * 3
+    expected = [p.grad.clone() for p in params]
+    total = torch.sqrt(sum((g**2).sum() for g in expected))
+    coef = min(1.0, 1.0 / (total.item() + 1e-6))
+    norm = clip_grad_norm_native(params, 1.0)
+    assert abs(norm.item() - total.item()) < 1e-3 * total.item()
+    for p, e in zip(params, expected, strict=True):
+        torch.testing.assert_close(p.grad, e * coef, rtol=1e-5, atol=1e-6)
+    _no_errors()
+
+
+def test_mae_ops():
+    from mia_train_b200.ops import mae as mae_ops
+    from mia_train_b200.ops.patch import patchify, patchify_reference
+
+    torch.manual_seed(6)
+    vol = torch.randn(2, 1, 32, 32, 32, device=DEV)
+    idx = torch.argsort(torch.rand(2, 64, device=DEV), dim=1)[:, :16]
+    rows = patchify(vol, (8, 8, 8), idx, out_dtype=torch.bfloat16)
+    ref_rows = torch.gather(patchify_reference(vol, (8, 8, 8)), 1, idx.unsqueeze(-1).expand(-1, -1, 512))
+    _close(rows, ref_rows, rel=1e-2, atol=1e-2)
+    vis = torch.randn(2, 16, 64, device=DEV).bfloat16().requires_grad_(True)
+    tok = torch.randn(1, 1, 64, device=DEV, requires_grad=True)
+    restore = torch.argsort(torch.rand(2, 64, device=DEV), dim=1)
+    out = mae_ops.restore_with_mask_token(vis, tok, restore)
+    ref = mae_ops.restore_reference(vis.detach().float(), tok.detach(), restore)
+    _close(out, ref)
+    g = torch.randn_like(out)
+    out.backward(g)
+    vis32 = vis.detach().float().requires_grad_(True)
+    tok32 = tok.detach().clone().requires_grad_(True)
+    mae_ops.restore_reference(vis32, tok32, restore).backward(g.float())
+    _close(vis.grad, vis32.grad)
+    _close(tok.grad, tok32.grad, rel=1e-2, atol=1e-1)
+    pred = torch.randn(2, 64, 512, device=DEV).bfloat16().requires_grad_(True)
+    mask = (torch.rand(2, 64, device=DEV) < 0.75).float()
+    loss = mae_ops.norm_pix_mse(pred, vol, mask, (8, 8, 8))
+    loss.backward()
+    pred32 = pred.detach().float().requires_grad_(True)
+    ref_loss = mae_ops.norm_pix_mse_reference(pred32, vol, mask, (8, 8, 8))
+    ref_loss.backward()
+    assert abs(loss.item() - ref_loss.item()) < 1e-3 * max(1.0, ref_loss.item())
+    _close(pred.grad, pred32.grad, rel=2e-2, atol=1e-5)
+    _no_errors()
+
+
+def test_mae_step_native_vs_reference_math():
+    """One vit3d+MAE training step: native kernels vs PyTorch math on the same weights and batch."""
+    import copy
+
+    from mia_train_b200.algorithms.mae import MAE
+    from mia_train_b200.models.vit import ViT3D
+
+    torch.manual_seed(7)
+    model = ViT3D(img_size=(32, 32, 32), patch_size=(8, 8, 8), embed_dim=128, depth=2, num_heads=2)
+    alg = MAE(model, input_axes="lcxyz", decoder_embed_dim=64, decoder_depth=1, decoder_num_heads=2).to(DEV)
+    alg_ref = copy.deepcopy(alg)
+    batch = {"img": torch.randn(2, 1, 1, 32, 32, 32, device=DEV)}
+    torch.manual_seed(8)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = alg(batch)
+    out["loss"].backward()
+    torch.manual_seed(8)
+    with _native.reference_math(), torch.autocast("cuda", dtype=torch.bfloat16):
+        out_ref = alg_ref(batch)
+    out_ref["loss"].backward()
+    assert abs(out["loss"].item() - out_ref["loss"].item()) < 2e-2 * abs(out_ref["loss"].item())
+    for (name, p), (_, pr) in zip(alg.named_parameters(), alg_ref.named_parameters(), strict=True):
+        assert p.grad is not None, name
+        _close(p.grad, pr.grad, rel=1e-1, atol=1e-3)
+    _no_errors()
