@@ -685,3 +685,101 @@ void rope_attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch
 }
 
 }  // namespace mia
+
+// ------------------------------------------------------------------ allocation-free entry point
+// See attention_noalloc.h for the contract. The scratch lives in a fixed device array: an fp32
+// dQ accumulator followed by the per-row delta = rowsum(dO * O).
+#include <cstdio>
+#include <mutex>
+
+#include "attention_noalloc.h"
+
+// The scratch array: file scope, internal linkage, one instance per GPU that loads the library.
+static __device__ __align__(256) float g_attn_noalloc_scratch[MIA_ATTN_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_lock;
+float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Resolves the device address of the scratch array for the current device (first call only).
+float* noalloc_scratch_for_current_device(int* device_out) {
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kNoAllocMaxDevices) return nullptr;
+  *device_out = device;
+  std::lock_guard<std::mutex> guard(g_noalloc_lock);
+  if (g_noalloc_scratch_ptr[device] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&ptr, g_attn_noalloc_scratch);
+    if (rc != cudaSuccess || ptr == nullptr) {
+      std::fprintf(stderr, "mia_attention_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", device,
+                   cudaGetErrorString(rc));
+      return nullptr;
+    }
+    g_noalloc_scratch_ptr[device] = static_cast<float*>(ptr);
+  }
+  return g_noalloc_scratch_ptr[device];
+}
+
+template <int D>
+int noalloc_launch(const mia::bf16* q, const mia::bf16* k, const mia::bf16* v, const mia::bf16* o,
+                   const mia::bf16* dout, const float* lse, mia::bf16* dq, mia::bf16* dk, mia::bf16* dv, int B, int H,
+                   int Nq, int Nk, float scale, float* scratch, cudaStream_t stream) {
+  using namespace mia;
+  const size_t dq_elems = (size_t)B * H * Nq * D;
+  float* dq_acc = scratch;
+  float* delta = scratch + dq_elems;
+  if (cudaMemsetAsync(dq_acc, 0, dq_elems * sizeof(float), stream) != cudaSuccess) return MIA_NOALLOC_ERR_CUDA;
+  const int rows = B * H * Nq;
+  attn_delta_kernel<D><<<(rows * 32 + 255) / 256, 256, 0, stream>>>(o, dout, delta, H, Nq, rows);
+  constexpr int S = D + 8;
+  const size_t smem = (size_t)(2 * kAttnBlockN + 2 * kAttnBlockM) * S * 2 + (size_t)kAttnBlockN * (kAttnBlockM + 8) * 2 +
+                      2 * kAttnBlockM * 4;
+  if (cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return MIA_NOALLOC_ERR_CUDA;
+  dim3 grid((Nk + kAttnBlockN - 1) / kAttnBlockN, B * H);
+  attn_bwd_kernel<D><<<grid, kAttnThreads, smem, stream>>>(q, k, v, dout, lse, delta, dq_acc, dk, dv, H, Nq, Nk, scale,
+                                                          scale * kLog2e);
+  f32_to_bf16_kernel<<<(unsigned)((dq_elems / 2 + 255) / 256 + 1), 256, 0, stream>>>(dq_acc, dq, dq_elems);
+  return cudaGetLastError() == cudaSuccess ? MIA_NOALLOC_OK : MIA_NOALLOC_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int mia_attention_bwd_noalloc(
+    const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse, void* dq, void* dk,
+    void* dv, int batch, int heads, int seq_q, int seq_k, int head_dim, float scale, void* stream) {
+  if (batch <= 0 || heads <= 0 || seq_q <= 0 || seq_k <= 0) {
+    std::fprintf(stderr, "mia_attention_bwd_noalloc: sizes must be positive\n");
+    return MIA_NOALLOC_ERR_ARGS;
+  }
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128) {
+    std::fprintf(stderr, "mia_attention_bwd_noalloc: head_dim must be 32, 64 or 128, got %d\n", head_dim);
+    return MIA_NOALLOC_ERR_ARGS;
+  }
+  const unsigned long long need = (unsigned long long)batch * heads * seq_q * (head_dim + 1);
+  if (need > (unsigned long long)MIA_ATTN_NOALLOC_SCRATCH_FLOATS) {
+    std::fprintf(stderr,
+                 "mia_attention_bwd_noalloc: batch*heads*seq_q*(head_dim+1) = %llu floats of scratch exceeds the "
+                 "fixed maximum of %d floats; split the batch or use the allocating entry point\n",
+                 need, MIA_ATTN_NOALLOC_SCRATCH_FLOATS);
+    return MIA_NOALLOC_ERR_TOO_LARGE;
+  }
+  int device = -1;
+  float* scratch = noalloc_scratch_for_current_device(&device);
+  if (scratch == nullptr) return MIA_NOALLOC_ERR_CUDA;
+  using mia::bf16;
+  auto s = static_cast<cudaStream_t>(stream);
+  auto cq = static_cast<const bf16*>(q);
+  auto ck = static_cast<const bf16*>(k);
+  auto cv = static_cast<const bf16*>(v);
+  auto co = static_cast<const bf16*>(o);
+  auto cd = static_cast<const bf16*>(dout);
+  auto oq = static_cast<bf16*>(dq);
+  auto ok = static_cast<bf16*>(dk);
+  auto ov = static_cast<bf16*>(dv);
+  if (head_dim == 32) return noalloc_launch<32>(cq, ck, cv, co, cd, lse, oq, ok, ov, batch, heads, seq_q, seq_k, scale, scratch, s);
+  if (head_dim == 64) return noalloc_launch<64>(cq, ck, cv, co, cd, lse, oq, ok, ov, batch, heads, seq_q, seq_k, scale, scratch, s);
+  return noalloc_launch<128>(cq, ck, cv, co, cd, lse, oq, ok, ov, batch, heads, seq_q, seq_k, scale, scratch, s);
+}
