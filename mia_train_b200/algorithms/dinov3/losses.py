@@ -1,0 +1,112 @@
+"""DINOv3 losses: Sinkhorn-Knopp centring, DINO, iBOT and KoLeo (reference
+`src/algorithms/dinov3/losses.py:48-206`).
+
+* `sinkhorn_knopp(logits, T, n_iter)`: Q = exp(logits / T)^T in fp32, normalised by its global sum
+  (all-reduced), then `n_iter` rounds of: rows summed globally (all-reduced) and divided by K,
+  columns summed locally and divided by the global batch; finally scaled by the batch. The
+  exponent is not clamped, as in the reference.
+* `DINOLoss`: cross-entropy of the student's temperature-softened log-softmax against the teacher
+  probabilities over all (student, teacher) view pairs, optionally ignoring same-view pairs.
+* `IBOTPatchLoss`: the same on masked patches, each sample's patches weighted by 1 / its count; the
+  global masked-patch count is all-reduced.
+* `KoLeoLoss`: -mean log distance to the nearest neighbour of L2-normalised features, outside
+  autocast.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+def _world_size() -> int:
+    return dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+
+
+def _all_reduce(t: torch.Tensor) -> torch.Tensor:
+    if dist.is_available() and dist.is_initialized():
+        dist.all_reduce(t)
+    return t
+
+
+def sinkhorn_knopp(
+    logits: torch.Tensor, temperature: float, n_iterations: int = 3, batch_size: float | None = None
+) -> torch.Tensor:
+    q = torch.exp(logits.float() / temperature).t()  # (K, B_local)
+    k, b_local = q.shape
+    total = float(b_local * _world_size()) if batch_size is None else float(batch_size)
+    q /= _all_reduce(torch.sum(q))
+    for _ in range(n_iterations):
+        q /= _all_reduce(torch.sum(q, dim=1, keepdim=True))
+        q /= k
+        q /= torch.sum(q, dim=0, keepdim=True)
+        q /= total
+    q *= total
+    return q.t()
+
+
+class DINOLoss(nn.Module):
+    def __init__(self, out_dim: int, student_temp: float = 0.1) -> None:
+        super().__init__()
+        self.out_dim = out_dim
+        self.student_temp = student_temp
+
+    def sinkhorn_knopp_teacher(self, teacher_logits: torch.Tensor, teacher_temp: float, n_iterations: int = 3):
+        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations)
+
+    def forward(self, student_logits: torch.Tensor, teacher_probs: torch.Tensor, ignore_diagonal: bool = False):
+        log_probs = F.log_softmax(student_logits.float() / self.student_temp, dim=-1)
+        n_s, b, _ = log_probs.shape
+        n_t = teacher_probs.shape[0]
+        if not ignore_diagonal:
+            return -torch.einsum("sbk,tbk->", log_probs, teacher_probs) / (b * n_s * n_t)
+        pairwise = -torch.einsum("sbk,tbk->st", log_probs, teacher_probs)
+        diag = min(n_s, n_t)
+        pairwise = torch.diagonal_scatter(pairwise, torch.zeros(diag, device=pairwise.device, dtype=pairwise.dtype))
+        return pairwise.sum() / (b * n_s * n_t - b * diag)
+
+
+class IBOTPatchLoss(nn.Module):
+    def __init__(self, patch_out_dim: int, student_temp: float = 0.1) -> None:
+        super().__init__()
+        self.patch_out_dim = patch_out_dim
+        self.student_temp = student_temp
+
+    def sinkhorn_knopp_teacher(self, teacher_logits, teacher_temp, n_masked_patches=None, n_iterations=3):
+        if n_masked_patches is None:
+            n_masked_patches = teacher_logits.shape[0]
+        total = torch.tensor(float(n_masked_patches), device=teacher_logits.device, dtype=torch.float32)
+        _all_reduce(total)
+        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations, batch_size=float(total.item()))
+
+    def forward_masked(self, student_logits, teacher_probs, student_masks_flat, n_masked_patches=None,
+                       masks_weight=None):
+        loss = torch.sum(teacher_probs * F.log_softmax(student_logits.float() / self.student_temp, dim=-1), dim=-1)
+        if masks_weight is None:
+            masks_weight = (
+                (1 / student_masks_flat.sum(-1).clamp(min=1.0)).unsqueeze(-1).expand_as(student_masks_flat)[student_masks_flat]
+            )
+        if n_masked_patches is not None:
+            loss = loss[:n_masked_patches]
+        return -(loss * masks_weight).sum() / student_masks_flat.shape[0]
+
+
+class KoLeoLoss(nn.Module):
+    def __init__(self, eps: float = 1e-8) -> None:
+        super().__init__()
+        self.eps = eps
+        self.pdist = nn.PairwiseDistance(2, eps=eps)
+
+    def _pairwise_nearest(self, x: torch.Tensor) -> torch.Tensor:
+        dots = torch.mm(x, x.t())
+        n = x.shape[0]
+        dots.view(-1)[:: n + 1].fill_(-1)
+        return torch.argmax(dots, dim=1)
+
+    def forward(self, student_output: torch.Tensor) -> torch.Tensor:
+        with torch.autocast("cuda", enabled=False), torch.autocast("cpu", enabled=False):
+            x = F.normalize(student_output.float(), eps=self.eps, p=2, dim=-1)
+            nearest = self._pairwise_nearest(x)
+            return -torch.log(self.pdist(x, x[nearest]) + self.eps).mean()

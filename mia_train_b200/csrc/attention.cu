@@ -461,91 +461,146 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restri
 }
 
 // ------------------------------------------------------------------------------------ RoPE
+// One CTA per token (b, n). The token's packed projection (3*H*D bf16) is staged in shared memory
+// with 16-byte loads; per-element rotation roles are built once per CTA from the pair list, and
+// cos/sin of the token's P angles are computed once and shared by every head of q and k.
+struct RopeRoles {
+  int16_t partner;  // -1: channel not rotated
+  int16_t pair;
+  int8_t second;    // 0: first channel of its pair, 1: second
+};
+
+__device__ __forceinline__ void rope_build_roles(RopeRoles* roles, const int* __restrict__ pairs, int P, int D,
+                                                 float* cs, float* sn, const float* ang) {
+  for (int d = threadIdx.x; d < D; d += blockDim.x) roles[d] = RopeRoles{-1, 0, 0};
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
+    roles[i1] = RopeRoles{(int16_t)i2, (int16_t)p, 0};
+    roles[i2] = RopeRoles{(int16_t)i1, (int16_t)p, 1};
+    float a = ang != nullptr ? ang[p] : 0.f;
+    sincosf(a, &sn[p], &cs[p]);
+  }
+  __syncthreads();
+}
+
 // qkv (B, N, 3, H, D) -> q, k, v (B, H, N, D); pairs (P, 2) int32; angles (B or 1, N, P) fp32.
-template <int D>
 __global__ void rope_split_fwd_kernel(const bf16* __restrict__ qkv, const float* __restrict__ angles,
                                       const int* __restrict__ pairs, int P, int angle_bstride, bf16* __restrict__ q,
-                                      bf16* __restrict__ k, bf16* __restrict__ v, int B, int N, int H) {
-  // one warp per (b, n, h)
-  const int item = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-  const int lane = threadIdx.x % 32;
-  if (item >= B * N * H) return;
-  const int h = item % H;
-  const int n = (item / H) % N;
-  const int b = item / (H * N);
-  const size_t in_base = (((size_t)b * N + n) * 3) * H * D + (size_t)h * D;
-  const size_t out_off = (((size_t)b * H + h) * N + n) * D;
-  const float* ang = angles != nullptr ? angles + (size_t)b * angle_bstride + (size_t)n * P : nullptr;
-  // copy straight through, then rotate pairs
-  for (int which = 0; which < 3; ++which) {
-    const bf16* src = qkv + in_base + (size_t)which * H * D;
-    bf16* dst = (which == 0 ? q : which == 1 ? k : v) + out_off;
-    for (int d = lane; d < D; d += 32) dst[d] = src[d];
-  }
-  if (ang == nullptr) return;
-  __syncwarp();
-  for (int p = lane; p < P; p += 32) {
-    const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
-    float sn, cs;
-    sincosf(ang[p], &sn, &cs);
-    for (int which = 0; which < 2; ++which) {
-      const bf16* src = qkv + in_base + (size_t)which * H * D;
-      bf16* dst = (which == 0 ? q : k) + out_off;
-      const float x1 = __bfloat162float(src[i1]);
-      const float x2 = __bfloat162float(src[i2]);
-      dst[i1] = __float2bfloat16_rn(x1 * cs - x2 * sn);
-      dst[i2] = __float2bfloat16_rn(x2 * cs + x1 * sn);
+                                      bf16* __restrict__ k, bf16* __restrict__ v, int N, int H, int D) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int HD = H * D;
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);                          // [3 * HD]
+  float* cs = reinterpret_cast<float*>(smem_raw + 3 * HD * 2);           // [P]
+  float* sn = cs + P;                                                    // [P]
+  RopeRoles* roles = reinterpret_cast<RopeRoles*>(sn + P);               // [D]
+  const int token = blockIdx.x;  // b * N + n
+  const int b = token / N, n = token % N;
+  const uint4* src = reinterpret_cast<const uint4*>(qkv + (size_t)token * 3 * HD);
+  for (int c = threadIdx.x; c < 3 * HD / 8; c += blockDim.x) reinterpret_cast<uint4*>(xs)[c] = src[c];
+  const float* ang = (angles != nullptr && P > 0) ? angles + (size_t)b * angle_bstride + (size_t)n * P : nullptr;
+  rope_build_roles(roles, pairs, P, D, cs, sn, ang);
+  const int chunks_per_head = D / 8;
+  for (int c = threadIdx.x; c < 3 * HD / 8; c += blockDim.x) {
+    const int which = c / (HD / 8);
+    const int rem = c % (HD / 8);
+    const int h = rem / chunks_per_head;
+    const int d0 = (rem % chunks_per_head) * 8;
+    const bf16* x = xs + which * HD + h * D;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = d0 + j;
+      const float xi = __bfloat162float(x[d]);
+      const RopeRoles r = roles[d];
+      if (which < 2 && r.partner >= 0 && ang != nullptr) {
+        const float xp = __bfloat162float(x[r.partner]);
+        o[j] = r.second ? xi * cs[r.pair] + xp * sn[r.pair] : xi * cs[r.pair] - xp * sn[r.pair];
+      } else {
+        o[j] = xi;
+      }
     }
+    bf16* dst = (which == 0 ? q : which == 1 ? k : v) + (((size_t)b * H + h) * N + n) * D + d0;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
   }
 }
 
-// Backward: dqkv (B, N, 3, H, D) from dq (fp32 accumulator), dk, dv (B, H, N, D); dangles (B, N, P)
-// accumulated: d(theta) = g2 * y1 - g1 * y2 summed over heads and over q and k, where y is the
-// rotated value (the attention input) and g its gradient.
-template <int D>
+// Backward: dqkv (B, N, 3, H, D) from dq (fp32), dk, dv (B, H, N, D); dangles (B, N, P): the CTA
+// owns its token, so d(theta_p) = sum over heads and over q, k of (g2 * y1 - g1 * y2) is written
+// without atomics (y is the rotated value the attention saw, g its gradient).
 __global__ void rope_split_bwd_kernel(const float* __restrict__ dq, const bf16* __restrict__ dk,
                                       const bf16* __restrict__ dv, const bf16* __restrict__ qr,
                                       const bf16* __restrict__ kr, const float* __restrict__ angles,
                                       const int* __restrict__ pairs, int P, int angle_bstride, bf16* __restrict__ dqkv,
-                                      float* __restrict__ dangles, int B, int N, int H) {
-  const int item = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-  const int lane = threadIdx.x % 32;
-  if (item >= B * N * H) return;
-  const int h = item % H;
-  const int n = (item / H) % N;
-  const int b = item / (H * N);
-  const size_t out_base = (((size_t)b * N + n) * 3) * H * D + (size_t)h * D;
-  const size_t in_off = (((size_t)b * H + h) * N + n) * D;
-  for (int d = lane; d < D; d += 32) {
-    dqkv[out_base + d] = __float2bfloat16_rn(dq[in_off + d]);
-    dqkv[out_base + (size_t)H * D + d] = dk[in_off + d];
-    dqkv[out_base + 2 * (size_t)H * D + d] = dv[in_off + d];
+                                      float* __restrict__ dangles, int N, int H, int D) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int HD = H * D;
+  float* gq = reinterpret_cast<float*>(smem_raw);                 // [HD]
+  float* gk = gq + HD;                                            // [HD]
+  float* yq = gk + HD;                                            // [HD]
+  float* yk = yq + HD;                                            // [HD]
+  float* cs = yk + HD;                                            // [P]
+  float* sn = cs + P;                                             // [P]
+  RopeRoles* roles = reinterpret_cast<RopeRoles*>(sn + P);        // [D]
+  const int token = blockIdx.x;
+  const int b = token / N, n = token % N;
+  const float* ang = (angles != nullptr && P > 0) ? angles + (size_t)b * angle_bstride + (size_t)n * P : nullptr;
+  for (int c = threadIdx.x; c < HD / 8; c += blockDim.x) {
+    const int h = c / (D / 8), d0 = (c % (D / 8)) * 8;
+    const size_t off = (((size_t)b * H + h) * N + n) * D + d0;
+    const float4 a = *reinterpret_cast<const float4*>(dq + off);
+    const float4 a2 = *reinterpret_cast<const float4*>(dq + off + 4);
+    float* gqd = gq + h * D + d0;
+    gqd[0] = a.x; gqd[1] = a.y; gqd[2] = a.z; gqd[3] = a.w; gqd[4] = a2.x; gqd[5] = a2.y; gqd[6] = a2.z; gqd[7] = a2.w;
+    const uint4 ukv = *reinterpret_cast<const uint4*>(dk + off);
+    const uint4 uq = *reinterpret_cast<const uint4*>(qr + off);
+    const uint4 uk = *reinterpret_cast<const uint4*>(kr + off);
+    const uint32_t w1[4] = {ukv.x, ukv.y, ukv.z, ukv.w}, w2[4] = {uq.x, uq.y, uq.z, uq.w}, w3[4] = {uk.x, uk.y, uk.z, uk.w};
+#pragma unroll
+    for (int hh = 0; hh < 4; ++hh) {
+      gk[h * D + d0 + 2 * hh] = bf16_lo(w1[hh]);
+      gk[h * D + d0 + 2 * hh + 1] = bf16_hi(w1[hh]);
+      yq[h * D + d0 + 2 * hh] = bf16_lo(w2[hh]);
+      yq[h * D + d0 + 2 * hh + 1] = bf16_hi(w2[hh]);
+      yk[h * D + d0 + 2 * hh] = bf16_lo(w3[hh]);
+      yk[h * D + d0 + 2 * hh + 1] = bf16_hi(w3[hh]);
+    }
+    // dv passes straight through
+    *reinterpret_cast<uint4*>(dqkv + (size_t)token * 3 * HD + 2 * HD + h * D + d0) =
+        *reinterpret_cast<const uint4*>(dv + off);
   }
-  if (angles == nullptr) return;
-  __syncwarp();
-  const float* ang = angles + (size_t)b * angle_bstride + (size_t)n * P;
-  for (int p = lane; p < P; p += 32) {
-    const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
-    float sn, cs;
-    sincosf(ang[p], &sn, &cs);
-    float dtheta = 0.f;
-    // q
-    {
-      const float g1 = dq[in_off + i1], g2 = dq[in_off + i2];
-      const float y1 = __bfloat162float(qr[in_off + i1]), y2 = __bfloat162float(qr[in_off + i2]);
-      dtheta += g2 * y1 - g1 * y2;
-      dqkv[out_base + i1] = __float2bfloat16_rn(g1 * cs + g2 * sn);
-      dqkv[out_base + i2] = __float2bfloat16_rn(g2 * cs - g1 * sn);
+  rope_build_roles(roles, pairs, P, D, cs, sn, ang);
+  for (int c = threadIdx.x; c < 2 * HD / 8; c += blockDim.x) {
+    const int which = c / (HD / 8);
+    const int rem = c % (HD / 8);
+    const int h = rem / (D / 8), d0 = (rem % (D / 8)) * 8;
+    const float* g = (which == 0 ? gq : gk) + h * D;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = d0 + j;
+      const RopeRoles r = roles[d];
+      if (r.partner >= 0 && ang != nullptr) {
+        const float gi = g[d], gp = g[r.partner];
+        o[j] = r.second ? gi * cs[r.pair] - gp * sn[r.pair] : gi * cs[r.pair] + gp * sn[r.pair];
+      } else {
+        o[j] = g[d];
+      }
     }
-    // k
-    {
-      const float g1 = __bfloat162float(dk[in_off + i1]), g2 = __bfloat162float(dk[in_off + i2]);
-      const float y1 = __bfloat162float(kr[in_off + i1]), y2 = __bfloat162float(kr[in_off + i2]);
-      dtheta += g2 * y1 - g1 * y2;
-      dqkv[out_base + (size_t)H * D + i1] = __float2bfloat16_rn(g1 * cs + g2 * sn);
-      dqkv[out_base + (size_t)H * D + i2] = __float2bfloat16_rn(g2 * cs - g1 * sn);
+    *reinterpret_cast<uint4*>(dqkv + (size_t)token * 3 * HD + which * HD + h * D + d0) =
+        make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  }
+  if (dangles != nullptr && ang != nullptr) {
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+      const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
+      float acc = 0.f;
+      for (int h = 0; h < H; ++h) {
+        acc += gq[h * D + i2] * yq[h * D + i1] - gq[h * D + i1] * yq[h * D + i2];
+        acc += gk[h * D + i2] * yk[h * D + i1] - gk[h * D + i1] * yk[h * D + i2];
+      }
+      dangles[(size_t)token * P + p] = acc;
     }
-    if (dangles != nullptr) atomicAdd(dangles + ((size_t)b * N + n) * P + p, dtheta);
   }
 }
 
@@ -642,15 +697,15 @@ void rope_split_fwd(torch::Tensor qkv, c10::optional<torch::Tensor> angles, torc
     ang = angles->data_ptr<float>();
     bstride = angles->size(0) == 1 ? 0 : N * P;
   }
-  const long items = (long)B * N * H;
-  if (items == 0) return;
-  DISPATCH_HEAD_DIM(D, [&] {
-    rope_split_fwd_kernel<HD><<<(unsigned)((items * 32 + 255) / 256), 256, 0, stream>>>(
-        reinterpret_cast<const bf16*>(qkv.data_ptr()), ang, pairs.data_ptr<int>(), P, bstride,
-        reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()),
-        reinterpret_cast<bf16*>(v.data_ptr()), B, N, H);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  });
+  TORCH_CHECK(D % 8 == 0 && D <= 256, "rope_split_fwd: head_dim must be a multiple of 8, at most 256");
+  if ((long)B * N == 0) return;
+  const size_t smem = (size_t)3 * H * D * 2 + 2 * (size_t)P * 4 + (size_t)D * sizeof(RopeRoles) + 16;
+  if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(rope_split_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rope_split_fwd_kernel<<<B * N, 128, smem, stream>>>(
+      reinterpret_cast<const bf16*>(qkv.data_ptr()), ang, pairs.data_ptr<int>(), P, bstride,
+      reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()), reinterpret_cast<bf16*>(v.data_ptr()),
+      N, H, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // Fused backward of rope_split + attention: attention backward into an fp32 dq, then the RoPE
@@ -673,15 +728,14 @@ void rope_attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch
     bstride = angles->size(0) == 1 ? 0 : N * P;
   }
   float* dang = (dangles.has_value() && ang != nullptr) ? dangles->data_ptr<float>() : nullptr;
-  const long items = (long)B * N * H;
-  DISPATCH_HEAD_DIM(D, [&] {
-    rope_split_bwd_kernel<HD><<<(unsigned)((items * 32 + 255) / 256), 256, 0, stream>>>(
-        dq_acc.data_ptr<float>(), reinterpret_cast<const bf16*>(dk.data_ptr()),
-        reinterpret_cast<const bf16*>(dv.data_ptr()), reinterpret_cast<const bf16*>(q.data_ptr()),
-        reinterpret_cast<const bf16*>(k.data_ptr()), ang, pairs.data_ptr<int>(), P, bstride,
-        reinterpret_cast<bf16*>(dqkv.data_ptr()), dang, B, N, H);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  });
+  TORCH_CHECK(D % 8 == 0 && D <= 256, "rope_attention_bwd: head_dim must be a multiple of 8, at most 256");
+  const size_t smem = (size_t)4 * H * D * 4 + 2 * (size_t)P * 4 + (size_t)D * sizeof(RopeRoles) + 16;
+  if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(rope_split_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rope_split_bwd_kernel<<<B * N, 128, smem, stream>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<const bf16*>(dk.data_ptr()), reinterpret_cast<const bf16*>(dv.data_ptr()),
+      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()), ang,
+      pairs.data_ptr<int>(), P, bstride, reinterpret_cast<bf16*>(dqkv.data_ptr()), dang, N, H, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace mia

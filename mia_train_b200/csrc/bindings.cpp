@@ -23,6 +23,7 @@ void rope_attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch
                         torch::Tensor dqkv, c10::optional<torch::Tensor> dangles, double scale);
 void multi_tensor_sumsq(std::vector<at::Tensor> tensors, at::Tensor out);
 void multi_tensor_scale(std::vector<at::Tensor> tensors, at::Tensor coef);
+void ema_update(std::vector<at::Tensor> teacher, std::vector<at::Tensor> student, double momentum);
 void adamw_step(std::vector<at::Tensor> params, std::vector<at::Tensor> grads, std::vector<at::Tensor> exp_avgs,
                 std::vector<at::Tensor> exp_avg_sqs, std::vector<at::Tensor> steps, at::Tensor group_index,
                 at::Tensor hyper, double eps, c10::optional<at::Tensor> grad_scale, std::vector<at::Tensor> shadows);
@@ -45,6 +46,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_attention_bwd", &mia::rope_attention_bwd);
   m.def("multi_tensor_sumsq", &mia::multi_tensor_sumsq);
   m.def("multi_tensor_scale", &mia::multi_tensor_scale);
+  m.def("ema_update", &mia::ema_update, "teacher = m * teacher + (1 - m) * student over tensor lists");
   m.def("adamw_step", &mia::adamw_step);
   m.def("patch_gather", &mia::patch_gather);
   m.def("mae_restore_fwd", &mia::mae_restore_fwd);

@@ -12,10 +12,12 @@
 //   warp 1      MMA issuer: allocates 2*BN TMEM columns (two fp32 accumulators), one thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) per 16-wide K slice and commits each consumed stage
 //               back to the producer and each finished tile to the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32*(w%4)..+31,
-//               i.e. output rows), bias / GELU (keeping the pre-activation) / GELU' / LayerScale /
-//               residual / accumulate-into-output, then 16-byte stores. While they drain one
-//               accumulator the MMA warp fills the other.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32*(w%4)..+31,
+//               i.e. output rows; warps 2-5 take the first half of the tile's columns, 6-9 the
+//               second), bias / GELU (keeping the pre-activation) / GELU' / LayerScale / residual /
+//               accumulate-into-output, then 16-byte stores. TMEM loads are double-buffered so the
+//               next 32 columns are in flight while the current ones are processed. While the
+//               epilogue drains one accumulator the MMA warp fills the other.
 //
 // All waits are bounded (see common.cuh); on a timeout the kernel records an error code, drains
 // the copies and MMAs it issued, frees its tensor memory and returns.
@@ -33,7 +35,7 @@ namespace mia {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer warp, MMA warp, 8 epilogue warps
 constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
 
 enum Act : int { kActNone = 0, kActGelu = 1, kActDGelu = 2 };
@@ -50,9 +52,27 @@ struct GemmParams {
   int act;
   int accumulate;
   int num_m_tiles;
-  int num_tiles;
+  int num_n_tiles;
+  int num_tiles;   // num_m_tiles * num_n_tiles * splits
+  int splits;      // split-K factor (> 1: partial sums added atomically into an fp32 output)
+  int k_blocks_per_split;
   int* err;
 };
+
+// Tile index -> (m tile, n tile, K-split); m fastest so concurrently running CTAs share B tiles.
+struct TileCoord {
+  int m0, n0, kb_begin, kb_end;
+};
+__device__ __forceinline__ TileCoord tile_coord(const GemmParams& p, int tile, int bn, int num_k) {
+  const int mn = tile % (p.num_m_tiles * p.num_n_tiles);
+  const int split = tile / (p.num_m_tiles * p.num_n_tiles);
+  TileCoord c;
+  c.m0 = (mn % p.num_m_tiles) * 128;
+  c.n0 = (mn / p.num_m_tiles) * bn;
+  c.kb_begin = split * p.k_blocks_per_split;
+  c.kb_end = min(num_k, c.kb_begin + p.k_blocks_per_split);
+  return c;
+}
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -66,12 +86,30 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (p.splits > 1) {  // split-K partial: atomically added into the fp32 output
+    float* dst = reinterpret_cast<float*>(p.D) + (size_t)m * p.N + n;
+    if (n + 32 <= p.N) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        atomicAdd(reinterpret_cast<float4*>(dst) + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+    } else {
+      for (int j = 0; j < 32 && n + j < p.N; ++j) atomicAdd(dst + j, v[j]);
+    }
+    return;
+  }
   const bool full = (n + 32 <= p.N);
   const size_t row = (size_t)m * p.N;
   if (p.bias != nullptr) {
+    if (full) {
+      const float4* b4 = reinterpret_cast<const float4*>(p.bias + n);
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || n + j < p.N) v[j] += __ldg(p.bias + n + j);
+      for (int q = 0; q < 8; ++q) {
+        const float4 bb = __ldg(b4 + q);
+        v[4 * q] += bb.x; v[4 * q + 1] += bb.y; v[4 * q + 2] += bb.z; v[4 * q + 3] += bb.w;
+      }
+    } else {
+      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] += __ldg(p.bias + n + j);
+    }
   }
   if (p.act == kActGelu) {
     if (p.aux_out != nullptr) {
@@ -105,9 +143,16 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
     }
   }
   if (p.gamma != nullptr) {
+    if (full) {
+      const float4* g4 = reinterpret_cast<const float4*>(p.gamma + n);
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || n + j < p.N) v[j] *= __ldg(p.gamma + n + j);
+      for (int q = 0; q < 8; ++q) {
+        const float4 gg = __ldg(g4 + q);
+        v[4 * q] *= gg.x; v[4 * q + 1] *= gg.y; v[4 * q + 2] *= gg.z; v[4 * q + 3] *= gg.w;
+      }
+    } else {
+      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] *= __ldg(p.gamma + n + j);
+    }
   }
   if (p.residual != nullptr) {
     if (full) {
@@ -197,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 256);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -224,9 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % p.num_m_tiles) * kBM;
-        const int n0 = (tile / p.num_m_tiles) * BN;
-        for (int kb = 0; kb < num_k; ++kb) {
+        const TileCoord tc = tile_coord(p, tile, BN, num_k);
+        const int m0 = tc.m0, n0 = tc.n0;
+        for (int kb = tc.kb_begin; kb < tc.kb_end; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
             ok = false;
             break;
@@ -283,7 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_k; ++kb) {
+        const TileCoord tc = tile_coord(p, tile, BN, num_k);
+        for (int kb = tc.kb_begin; kb < tc.kb_end; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrGemmMmaWait)) {
             ok = false;
             break;
@@ -297,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          : make_sdesc_sw128(a_base + k * 32, 16, 1024);
             const uint64_t b_desc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
                                          : make_sdesc_sw128(b_base + k * 32, 16, 1024);
-            tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > tc.kb_begin || k > 0) ? 1u : 0u);
             any_mma = true;
           }
           tc_commit(&empty_bar[stage]);
@@ -318,23 +364,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5
-    const int lane_group = warp % 4;  // TMEM lanes 32*lane_group .. +31
+    // ---------------- epilogue warps 2..9
+    const int lane_group = warp % 4;         // TMEM lanes 32*lane_group .. +31
+    const int col_half = (warp - 2) / 4;     // which half of the tile's columns
+    constexpr int kChunks = BN / 64;         // 32-column chunks per half
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrGemmEpilogueWait)) break;
       tc_fence_after();
-      const int m0 = (tile % p.num_m_tiles) * kBM;
-      const int n0 = (tile / p.num_m_tiles) * BN;
+      const TileCoord tc = tile_coord(p, tile, BN, (p.K + kBK - 1) / kBK);
+      const int m0 = tc.m0;
+      const int n0 = tc.n0 + col_half * (BN / 2);
       const int m = m0 + lane_group * 32 + lane;
-      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        epilogue_chunk(p, m, n0 + c * 32, r);
+      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_half * (BN / 2);
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(t_row, r[0]);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        tmem_ld_wait_regs(r[c & 1]);
+        if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, r[(c + 1) & 1]);
+        epilogue_chunk(p, m, n0 + c * 32, r[c & 1]);
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -399,8 +449,14 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams
     configured[device] = true;
   }
   p.num_m_tiles = (p.M + kBM - 1) / kBM;
-  const int num_n = (p.N + BN - 1) / BN;
-  p.num_tiles = p.num_m_tiles * num_n;
+  p.num_n_tiles = (p.N + BN - 1) / BN;
+  const int num_k = (p.K + kBK - 1) / kBK;
+  if (p.splits < 1) p.splits = 1;
+  p.k_blocks_per_split = (num_k + p.splits - 1) / p.splits;
+  p.splits = (num_k + p.k_blocks_per_split - 1) / p.k_blocks_per_split;  // no empty split
+  p.num_tiles = p.num_m_tiles * p.num_n_tiles * p.splits;
+  if (p.splits > 1 && !p.accumulate)
+    C10_CUDA_CHECK(cudaMemsetAsync(p.D, 0, (size_t)p.M * p.N * sizeof(float), stream));
   const int grid = std::min(p.num_tiles, num_sms(device));
   kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -482,6 +538,16 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   TORCH_CHECK(act != kActDGelu || p.aux != nullptr, "gemm: GELU' needs aux");
 
   const int bn = choose_bn((int)M, (int)N, num_sms(device));
+  // Split K when the output alone cannot fill the SMs and nothing in the epilogue needs the full
+  // sum (the weight-gradient GEMMs: tokens are K, the output is a small fp32 matrix).
+  p.splits = 1;
+  const bool plain_fp32 = p.d_fp32 && !p.bias && !p.gamma && !p.residual && !p.aux && !p.aux_out && act == kActNone;
+  if (plain_fp32) {
+    const long tiles = (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+    const int sms = num_sms(device);
+    const int k_blocks = (int)((K + kBK - 1) / kBK);
+    if (2 * tiles <= sms) p.splits = (int)std::max(1L, std::min<long>(k_blocks / 4, sms / tiles));
+  }
   // A tile: 128 rows x 64 K (K-major) or 64 M x 64 K per box, twice (M-major).
   CUtensorMap ta = a_kmajor ? make_map(a.data_ptr(), K, M, a.stride(0), 64, kBM)
                             : make_map(a.data_ptr(), M, K, a.stride(0), 64, 64);
@@ -492,27 +558,54 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
 }
 
 // -------------------------------------------------------------- column sums (bias gradients)
-// out[n] (+)= sum_m x[m, n]; x bf16 (M, N) row-major, N % 8 == 0. Each thread owns 8 adjacent
-// columns over a slab of rows; partial sums are combined with one fp32 atomic per column per CTA.
-__global__ void column_sum_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ out, int M, int N,
-                                  int rows_per_cta) {
-  const int col8 = blockIdx.x * blockDim.x + threadIdx.x;  // group of 8 columns
-  const int n = col8 * 8;
-  if (n >= N) return;
+// out[n] (+)= sum_m x[m, n]; x bf16 (M, N) row-major, N % 8 == 0. A CTA owns 256 columns (8 per
+// lane) and a slab of rows split across its 8 warps; the warps are combined in shared memory and
+// the CTA adds one partial per column. The slab height keeps the CTA count near the SM count, so
+// each column sees only a few dozen atomics.
+__global__ void __launch_bounds__(256) column_sum_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ out,
+                                                         int M, int N, int rows_per_cta) {
+  __shared__ float part[8][256];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int n = blockIdx.x * 256 + lane * 8;
   const int m_begin = blockIdx.y * rows_per_cta;
   const int m_end = min(M, m_begin + rows_per_cta);
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int m = m_begin; m < m_end; ++m) {
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * N + n));
-    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  if (n < N) {
+    int m = m_begin + warp;
+    for (; m + 24 < m_end; m += 32) {
+      uint4 u[4];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      acc[2 * h] += bf16_lo(w[h]);
-      acc[2 * h + 1] += bf16_hi(w[h]);
+      for (int r = 0; r < 4; ++r) u[r] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(m + 8 * r) * N + n));
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const uint32_t w[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          acc[2 * h] += bf16_lo(w[h]);
+          acc[2 * h + 1] += bf16_hi(w[h]);
+        }
+      }
+    }
+    for (; m < m_end; m += 8) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * N + n));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        acc[2 * h] += bf16_lo(w[h]);
+        acc[2 * h + 1] += bf16_hi(w[h]);
+      }
     }
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) atomicAdd(out + n + j, acc[j]);
+  for (int j = 0; j < 8; ++j) part[warp][lane * 8 + j] = acc[j];
+  __syncthreads();
+  const int c = threadIdx.x;  // one column of this CTA's 256
+  if (blockIdx.x * 256 + c < N) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w][c];
+    atomicAdd(out + blockIdx.x * 256 + c, s);
+  }
 }
 
 void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate) {
@@ -526,12 +619,11 @@ void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate) {
   if (!accumulate) C10_CUDA_CHECK(cudaMemsetAsync(out.data_ptr(), 0, out.numel() * 4, stream));
   const int M = (int)x.size(0), N = (int)x.size(1);
   if (M == 0) return;
-  const int threads = 128;
-  const int groups = N / 8;
-  dim3 grid((groups + threads - 1) / threads, std::max(1, std::min(256, (M + 63) / 64)));
-  const int rows = (M + grid.y - 1) / grid.y;
-  column_sum_kernel<<<grid, threads, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-                                                  out.data_ptr<float>(), M, N, rows);
+  const int gx = (N + 255) / 256;
+  const int gy = std::max(1, std::min((M + 63) / 64, (num_sms(x.get_device()) + gx - 1) / gx));
+  const int rows = (M + gy - 1) / gy;
+  column_sum_kernel<<<dim3(gx, gy), 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                                      out.data_ptr<float>(), M, N, rows);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -6,11 +6,13 @@
 //   dx  = rstd * (g - mean(g) - xhat * mean(g * xhat))        (LayerNorm)
 //   dx  = rstd * (g - xhat * mean(g * xhat))                  (RMSNorm)
 //   dw += sum_rows dy * xhat,   db += sum_rows dy
-// The parameter gradients are reduced per CTA in shared memory and then added to global fp32
-// buffers with one atomic per column per CTA.
+// Backward runs as two kernels: dX with one warp per row, and the weight/bias gradients as a column
+// reduction over row slabs (one atomic per column per CTA, about one CTA per SM).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -100,15 +102,11 @@ __global__ void layernorm_fwd_kernel(const T* __restrict__ x, const float* __res
   }
 }
 
-template <typename T>
-__global__ void layernorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
-                                     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
-                                     T* __restrict__ dx, float* __restrict__ dw, float* __restrict__ db, int rows,
-                                     int n, int rms) {
-  extern __shared__ float sacc[];  // [2 * n]: dw partials, db partials
-  const bool want_dw = dw != nullptr, want_db = db != nullptr;
-  for (int i = threadIdx.x; i < 2 * n; i += blockDim.x) sacc[i] = 0.f;
-  __syncthreads();
+// dX: one warp per row, the row held in registers (NCH chunks of 8 columns per lane).
+template <typename T, int NCH>
+__global__ void layernorm_bwd_dx_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
+                                        const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                                        T* __restrict__ dx, int rows, int n, int rms) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
@@ -116,41 +114,84 @@ __global__ void layernorm_bwd_kernel(const T* __restrict__ dy, const T* __restri
     const T* gr = dy + (size_t)row * n;
     const float mean = mean_in[row];
     const float rstd = rstd_in[row];
+    float xh[NCH][8], g[NCH][8];
     float sum_g = 0.f, sum_gx = 0.f;
-    for (int c = lane * 8; c < n; c += 256) {
-      float xv[8], gv[8];
-      Vec8<T>::load(xr + c, xv);
-      Vec8<T>::load(gr + c, gv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float xh = (xv[j] - mean) * rstd;
-        const float g = gv[j] * (w != nullptr ? __ldg(w + c + j) : 1.f);
-        sum_g += g;
-        sum_gx += g * xh;
-        if (want_dw) atomicAdd(&sacc[c + j], gv[j] * xh);
-        if (want_db) atomicAdd(&sacc[n + c + j], gv[j]);
+    for (int ch = 0; ch < NCH; ++ch) {
+      const int c = lane * 8 + ch * 256;
+      if (c < n) {
+        float xv[8], gv[8];
+        Vec8<T>::load(xr + c, xv);
+        Vec8<T>::load(gr + c, gv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[ch][j] = (xv[j] - mean) * rstd;
+          g[ch][j] = gv[j] * (w != nullptr ? __ldg(w + c + j) : 1.f);
+          sum_g += g[ch][j];
+          sum_gx += g[ch][j] * xh[ch][j];
+        }
       }
     }
     const float mg = rms ? 0.f : warp_sum(sum_g) / n;
     const float mgx = warp_sum(sum_gx) / n;
     T* dr = dx + (size_t)row * n;
-    for (int c = lane * 8; c < n; c += 256) {
-      float xv[8], gv[8];
-      Vec8<T>::load(xr + c, xv);
-      Vec8<T>::load(gr + c, gv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float xh = (xv[j] - mean) * rstd;
-        const float g = gv[j] * (w != nullptr ? __ldg(w + c + j) : 1.f);
-        xv[j] = rstd * (g - mg - xh * mgx);
+    for (int ch = 0; ch < NCH; ++ch) {
+      const int c = lane * 8 + ch * 256;
+      if (c < n) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = rstd * (g[ch][j] - mg - xh[ch][j] * mgx);
+        Vec8<T>::store(dr + c, o);
       }
-      Vec8<T>::store(dr + c, xv);
     }
   }
+}
+
+// dw[c] += sum_r dy[r, c] * xhat[r, c], db[c] += sum_r dy[r, c]. A CTA owns 256 columns (8 per lane)
+// and a slab of rows split over its 8 warps; warps are combined in shared memory and the CTA adds one
+// value per column (the slab height keeps the CTA count near the SM count).
+template <typename T>
+__global__ void __launch_bounds__(256) layernorm_bwd_param_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                                  const float* __restrict__ mean_in,
+                                                                  const float* __restrict__ rstd_in,
+                                                                  float* __restrict__ dw, float* __restrict__ db,
+                                                                  int rows, int n, int rows_per_cta) {
+  __shared__ float part[2][8][256];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c = blockIdx.x * 256 + lane * 8;
+  const int r_begin = blockIdx.y * rows_per_cta;
+  const int r_end = min(rows, r_begin + rows_per_cta);
+  float aw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ab[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c < n) {
+    for (int r = r_begin + warp; r < r_end; r += 8) {
+      float xv[8], gv[8];
+      Vec8<T>::load(x + (size_t)r * n + c, xv);
+      Vec8<T>::load(dy + (size_t)r * n + c, gv);
+      const float mean = mean_in[r], rstd = rstd_in[r];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        aw[j] += gv[j] * (xv[j] - mean) * rstd;
+        ab[j] += gv[j];
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    part[0][warp][lane * 8 + j] = aw[j];
+    part[1][warp][lane * 8 + j] = ab[j];
+  }
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    if (want_dw) atomicAdd(dw + i, sacc[i]);
-    if (want_db) atomicAdd(db + i, sacc[n + i]);
+  const int col = blockIdx.x * 256 + threadIdx.x;
+  if (col < n) {
+    float sw = 0.f, sb = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      sw += part[0][k][threadIdx.x];
+      sb += part[1][k][threadIdx.x];
+    }
+    if (dw != nullptr) atomicAdd(dw + col, sw);
+    if (db != nullptr) atomicAdd(db + col, sb);
   }
 }
 
@@ -193,26 +234,37 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tenso
   c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (rows == 0) return;
+  TORCH_CHECK(n <= 256 * 8, "layernorm_bwd: hidden size above 2048 is not supported");
   const float* wp = w.has_value() ? w->data_ptr<float>() : nullptr;
   float* dwp = dw.has_value() ? dw->data_ptr<float>() : nullptr;
   float* dbp = db.has_value() ? db->data_ptr<float>() : nullptr;
-  const int threads = 256;
-  const int grid = std::min((rows + 7) / 8, sm_count(x) * 2);
-  const size_t smem = 2 * (size_t)n * sizeof(float);
-  if (x.scalar_type() == at::kBFloat16) {
-    auto k = layernorm_bwd_kernel<__nv_bfloat16>;
-    if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<grid, threads, smem, stream>>>(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
-                                      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), wp, mean.data_ptr<float>(),
-                                      rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dwp, dbp,
-                                      rows, n, rms ? 1 : 0);
-  } else {
-    auto k = layernorm_bwd_kernel<float>;
-    if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<grid, threads, smem, stream>>>(dy.data_ptr<float>(), x.data_ptr<float>(), wp, mean.data_ptr<float>(),
-                                      rstd.data_ptr<float>(), dx.data_ptr<float>(), dwp, dbp, rows, n, rms ? 1 : 0);
-  }
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int sms = sm_count(x);
+  const int dx_grid = std::max(1, std::min(8 * sms, (rows + 7) / 8));
+  const int gx = (n + 255) / 256;
+  const int gy = std::max(1, std::min((rows + 31) / 32, (sms + gx - 1) / gx));
+  const int rows_per_cta = (rows + gy - 1) / gy;
+  auto run = [&](auto tag, auto nch) {
+    using T = decltype(tag);
+    constexpr int NCH = decltype(nch)::value;
+    layernorm_bwd_dx_kernel<T, NCH><<<dx_grid, 256, 0, stream>>>(
+        reinterpret_cast<const T*>(dy.data_ptr()), reinterpret_cast<const T*>(x.data_ptr()), wp, mean.data_ptr<float>(),
+        rstd.data_ptr<float>(), reinterpret_cast<T*>(dx.data_ptr()), rows, n, rms ? 1 : 0);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    if (dwp != nullptr || dbp != nullptr) {
+      layernorm_bwd_param_kernel<T><<<dim3(gx, gy), 256, 0, stream>>>(
+          reinterpret_cast<const T*>(dy.data_ptr()), reinterpret_cast<const T*>(x.data_ptr()), mean.data_ptr<float>(),
+          rstd.data_ptr<float>(), dwp, dbp, rows, n, rows_per_cta);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+    }
+  };
+  auto by_width = [&](auto tag) {
+    if (n <= 256) run(tag, std::integral_constant<int, 1>{});
+    else if (n <= 512) run(tag, std::integral_constant<int, 2>{});
+    else if (n <= 1024) run(tag, std::integral_constant<int, 4>{});
+    else run(tag, std::integral_constant<int, 8>{});
+  };
+  if (x.scalar_type() == at::kBFloat16) by_width(__nv_bfloat16{});
+  else by_width(float{});
 }
 
 }  // namespace mia

@@ -165,45 +165,77 @@ void mae_restore_bwd(torch::Tensor dout, torch::Tensor restore, torch::Tensor dv
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// One CTA per (b, n) patch. Masked patches: target = (x - mean) / sqrt(var_unbiased + 1e-6) (or x
-// itself), loss += sum((pred - target)^2) / P / count, grad = 2 (pred - target) / P / count.
+// One CTA per (b, n) patch. The patch is read as runs of 8 voxels along W (pw % 8 == 0), so every
+// load is 16 B (bf16) or 32 B (fp32). Pass 1: shifted sum and sum of squares (shift = the patch's
+// first voxel, which keeps the variance well conditioned); pass 2 re-reads the runs (L1/L2 hits),
+// forms the normalised target and writes the loss contribution and the gradient.
+// Masked patches: target = (x - mean) / sqrt(var_unbiased + 1e-6) (or x itself);
+// loss += sum((pred - target)^2) / P / count; grad = 2 (pred - target) / P / count.
 // Visible patches: grad = 0. `count` = max(1, sum(mask)) is read from the device.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<bf16>(const bf16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    v[2 * h] = bf16_lo(w[h]);
+    v[2 * h + 1] = bf16_hi(w[h]);
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store8<bf16>(bf16* p, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                                            pack_bf16x2(v[6], v[7]));
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
 template <typename TP, typename TV>
 __global__ void norm_pix_mse_kernel(const TP* __restrict__ pred, const TV* __restrict__ vol,
                                     const float* __restrict__ mask, const float* __restrict__ count,
                                     float* __restrict__ loss, TP* __restrict__ grad, int C, int D, int H, int W,
                                     int pd, int ph, int pw, int N, int norm_pix) {
-  constexpr int kMaxPer = 64;  // P <= 256 * 64
   const int row = blockIdx.x;
   const int b = row / N, n = row % N;
   const int vp = pd * ph * pw;
   const int P = C * vp;
+  const int runs = P / 8;
   const TP* pr = pred + (size_t)row * P;
   TP* gr = grad + (size_t)row * P;
   const float mk = mask[row];
   if (mk == 0.f) {
-    for (int e = threadIdx.x; e < P; e += blockDim.x) gr[e] = from_f<TP>(0.f);
+    const float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int u = threadIdx.x; u < runs; u += blockDim.x) store8<TP>(gr + u * 8, z);
     return;
   }
   const int gh = H / ph, gw = W / pw;
   const int zd = n / (gh * gw), zh = (n / gw) % gh, zw = n % gw;
-  float x[kMaxPer];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    const int e = threadIdx.x + i * blockDim.x;
-    x[i] = 0.f;
-    if (e < P) {
-      const int c = e / vp;
-      int r = e % vp;
-      const int a = r / (ph * pw);
-      r %= ph * pw;
-      const int j = r / pw, l = r % pw;
-      x[i] = to_f<TV>(vol[((((size_t)b * C + c) * D + (zd * pd + a)) * H + (zh * ph + j)) * W + (zw * pw + l)]);
-      s += x[i];
-    }
-  }
+  const int runs_per_row = pw / 8;
+  auto run_ptr = [&](int u) -> const TV* {
+    const int e = u * 8;
+    const int c = e / vp;
+    int r = e % vp;
+    const int a = r / (ph * pw);
+    r %= ph * pw;
+    const int j = r / pw, l = r % pw;
+    return vol + ((((size_t)b * C + c) * D + (zd * pd + a)) * H + (zh * ph + j)) * W + (zw * pw + l);
+  };
+  (void)runs_per_row;
   __shared__ float red[32];
+  __shared__ float shift_s;
   auto block_sum = [&](float v) -> float {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -216,28 +248,41 @@ __global__ void norm_pix_mse_kernel(const TP* __restrict__ pred, const TV* __res
   };
   float mean = 0.f, inv = 1.f;
   if (norm_pix) {
-    mean = block_sum(s) / P;
-    float ss = 0.f;
+    if (threadIdx.x == 0) shift_s = to_f<TV>(*run_ptr(0));
+    __syncthreads();
+    const float shift = shift_s;
+    float s = 0.f, ss = 0.f;
+    for (int u = threadIdx.x; u < runs; u += blockDim.x) {
+      float x[8];
+      load8<TV>(run_ptr(u), x);
 #pragma unroll
-    for (int i = 0; i < kMaxPer; ++i) {
-      const int e = threadIdx.x + i * blockDim.x;
-      if (e < P) ss += (x[i] - mean) * (x[i] - mean);
+      for (int j = 0; j < 8; ++j) {
+        const float d = x[j] - shift;
+        s += d;
+        ss += d * d;
+      }
     }
-    const float var = block_sum(ss) / (float)(P > 1 ? P - 1 : 1);
+    const float tot_s = block_sum(s);
+    const float tot_ss = block_sum(ss);
+    const float m_shifted = tot_s / P;
+    mean = shift + m_shifted;
+    const float var = fmaxf(tot_ss - tot_s * m_shifted, 0.f) / (float)(P > 1 ? P - 1 : 1);
     inv = rsqrtf(var + 1e-6f);
   }
   const float cnt = *count;
-  const float gscale = 2.f / (float)P / cnt;
+  const float gscale = 2.f / (float)P / cnt * mk;
   float se = 0.f;
+  for (int u = threadIdx.x; u < runs; u += blockDim.x) {
+    float x[8], p[8], g[8];
+    load8<TV>(run_ptr(u), x);
+    load8<TP>(pr + u * 8, p);
 #pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    const int e = threadIdx.x + i * blockDim.x;
-    if (e < P) {
-      const float tgt = (x[i] - mean) * inv;
-      const float diff = to_f<TP>(pr[e]) - tgt;
+    for (int j = 0; j < 8; ++j) {
+      const float diff = p[j] - (x[j] - mean) * inv;
       se += diff * diff;
-      gr[e] = from_f<TP>(diff * gscale * mk);
+      g[j] = diff * gscale;
     }
+    store8<TP>(gr + u * 8, g);
   }
   const float tot = block_sum(se);
   if (threadIdx.x == 0) atomicAdd(loss, tot * mk / (float)P / cnt);
@@ -249,7 +294,8 @@ void norm_pix_mse(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, tor
   const int B = (int)vol.size(0), C = (int)vol.size(1), D = (int)vol.size(2), H = (int)vol.size(3), W = (int)vol.size(4);
   const int N = (int)pred.size(1);
   const int P = (int)pred.size(2);
-  TORCH_CHECK(P == C * pd * ph * pw && P <= 256 * 64, "norm_pix_mse: patch width mismatch or too large");
+  TORCH_CHECK(P == C * pd * ph * pw, "norm_pix_mse: patch width mismatch");
+  TORCH_CHECK(pw % 8 == 0 && W % 8 == 0, "norm_pix_mse: the W extent of a patch must be a multiple of 8");
   c10::cuda::CUDAGuard guard(pred.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   auto count = mask.sum().clamp_min(1.0);

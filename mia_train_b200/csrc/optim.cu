@@ -155,7 +155,34 @@ __global__ void adamw_kernel(const TensorEntry* __restrict__ entries, const int2
   __nv_bfloat16* shadow = reinterpret_cast<__nv_bfloat16*>(e.ptr[5]);
   const int64_t start = (int64_t)ch.y * kChunk;
   const int64_t end = min(e.numel, start + kChunk);
-  for (int64_t i = start + threadIdx.x; i < end; i += blockDim.x) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(gr) | reinterpret_cast<uintptr_t>(m) |
+                     reinterpret_cast<uintptr_t>(v)) & 15) == 0 &&
+                   (shadow == nullptr || (reinterpret_cast<uintptr_t>(shadow) & 7) == 0);
+  int64_t vec_end = start;
+  if (vec) {
+    vec_end = start + ((end - start) / 4) * 4;
+    for (int64_t i = start + 4 * threadIdx.x; i < vec_end; i += 4 * blockDim.x) {
+      float4 g4 = *reinterpret_cast<const float4*>(gr + i);
+      float4 p4 = *reinterpret_cast<const float4*>(p + i);
+      float4 m4 = *reinterpret_cast<const float4*>(m + i);
+      float4 v4 = *reinterpret_cast<const float4*>(v + i);
+      float gg[4] = {g4.x, g4.y, g4.z, g4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
+      float mm[4] = {m4.x, m4.y, m4.z, m4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float g = gg[j] * gs;
+        mm[j] = mm[j] + (1.0f - b1) * (g - mm[j]);
+        vv[j] = vv[j] * b2 + (1.0f - b2) * g * g;
+        pp[j] = pp[j] * decay - step_size * (mm[j] / (sqrtf(vv[j]) / bc2_sqrt + eps));
+      }
+      *reinterpret_cast<float4*>(p + i) = make_float4(pp[0], pp[1], pp[2], pp[3]);
+      *reinterpret_cast<float4*>(m + i) = make_float4(mm[0], mm[1], mm[2], mm[3]);
+      *reinterpret_cast<float4*>(v + i) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      if (shadow != nullptr)
+        *reinterpret_cast<uint2*>(shadow + i) = make_uint2(pack_bf16x2(pp[0], pp[1]), pack_bf16x2(pp[2], pp[3]));
+    }
+  }
+  for (int64_t i = vec_end + threadIdx.x; i < end; i += blockDim.x) {
     const float g = gr[i] * gs;
     float pi = p[i] * decay;
     float mi = m[i];
@@ -167,6 +194,32 @@ __global__ void adamw_kernel(const TensorEntry* __restrict__ entries, const int2
     m[i] = mi;
     v[i] = vi;
     if (shadow != nullptr) shadow[i] = __float2bfloat16_rn(pi);
+  }
+}
+
+// teacher = momentum * teacher + (1 - momentum) * student; entries: ptr = {teacher, student}.
+__global__ void ema_kernel(const TensorEntry* __restrict__ entries, const int2* __restrict__ chunks, float momentum) {
+  const int2 ch = chunks[blockIdx.x];
+  const TensorEntry e = entries[ch.x];
+  float* t = reinterpret_cast<float*>(e.ptr[0]);
+  const float* s = reinterpret_cast<const float*>(e.ptr[1]);
+  const int64_t start = (int64_t)ch.y * kChunk;
+  const int64_t end = min(e.numel, start + kChunk);
+  const float a = 1.0f - momentum;
+  if (((reinterpret_cast<uintptr_t>(t) | reinterpret_cast<uintptr_t>(s)) & 15) == 0) {
+    const int64_t vend = start + ((end - start) / 4) * 4;
+    for (int64_t i = start + 4 * threadIdx.x; i < vend; i += 4 * blockDim.x) {
+      float4 tv = *reinterpret_cast<float4*>(t + i);
+      const float4 sv = *reinterpret_cast<const float4*>(s + i);
+      tv.x = momentum * tv.x + a * sv.x;
+      tv.y = momentum * tv.y + a * sv.y;
+      tv.z = momentum * tv.z + a * sv.z;
+      tv.w = momentum * tv.w + a * sv.w;
+      *reinterpret_cast<float4*>(t + i) = tv;
+    }
+    for (int64_t i = vend + threadIdx.x; i < end; i += blockDim.x) t[i] = momentum * t[i] + a * s[i];
+  } else {
+    for (int64_t i = start + threadIdx.x; i < end; i += blockDim.x) t[i] = momentum * t[i] + a * s[i];
   }
 }
 
@@ -186,6 +239,21 @@ void multi_tensor_sumsq(std::vector<at::Tensor> tensors, at::Tensor out) {
   sumsq_kernel<<<tab.num_chunks, 256, 0, stream>>>(reinterpret_cast<const TensorEntry*>(tab.entries.data_ptr()),
                                                    reinterpret_cast<const int2*>(tab.chunks.data_ptr()),
                                                    out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ema_update(std::vector<at::Tensor> teacher, std::vector<at::Tensor> student, double momentum) {
+  if (teacher.empty()) return;
+  TORCH_CHECK(teacher.size() == student.size(), "ema_update: list lengths differ");
+  for (size_t i = 0; i < teacher.size(); ++i)
+    TORCH_CHECK(teacher[i].scalar_type() == at::kFloat && student[i].scalar_type() == at::kFloat &&
+                    teacher[i].numel() == student[i].numel() && teacher[i].is_contiguous() && student[i].is_contiguous(),
+                "ema_update: matching contiguous fp32 tensors expected");
+  c10::cuda::CUDAGuard guard(teacher[0].device());
+  const Table& tab = get_table({teacher, student}, nullptr);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  ema_kernel<<<tab.num_chunks, 256, 0, stream>>>(reinterpret_cast<const TensorEntry*>(tab.entries.data_ptr()),
+                                                 reinterpret_cast<const int2*>(tab.chunks.data_ptr()), (float)momentum);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

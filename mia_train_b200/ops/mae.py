@@ -98,9 +98,11 @@ def norm_pix_mse(
     patch: tuple[int, int, int],
     norm_pix: bool = True,
 ) -> torch.Tensor:
-    if use_native(prediction) and prediction.dtype in (torch.bfloat16, torch.float32) and volumes.dtype in (
-        torch.float32,
-        torch.bfloat16,
+    if (
+        use_native(prediction)
+        and prediction.dtype in (torch.bfloat16, torch.float32)
+        and volumes.dtype in (torch.float32, torch.bfloat16)
+        and patch[2] % 8 == 0
     ):
         return _NativeNormPixMSE.apply(prediction, volumes, mask, tuple(patch), norm_pix)
     return norm_pix_mse_reference(prediction.float(), volumes.float(), mask.float(), patch, norm_pix)

@@ -57,13 +57,13 @@ class _NativeLayerNorm(torch.autograd.Function):
 def layer_norm(
     x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None, eps: float = 1e-5
 ) -> torch.Tensor:
-    if use_native(x) and x.dtype in (torch.bfloat16, torch.float32) and x.shape[-1] % 8 == 0 and x.shape[-1] <= 8192:
+    if use_native(x) and x.dtype in (torch.bfloat16, torch.float32) and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048:
         return _NativeLayerNorm.apply(x, weight, bias, eps, False)
     return F.layer_norm(x, (x.shape[-1],), weight, bias, eps)
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor | None, eps: float = 1e-6) -> torch.Tensor:
-    if use_native(x) and x.dtype in (torch.bfloat16, torch.float32) and x.shape[-1] % 8 == 0 and x.shape[-1] <= 8192:
+    if use_native(x) and x.dtype in (torch.bfloat16, torch.float32) and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048:
         return _NativeLayerNorm.apply(x, weight, None, eps, True)
     xf = x.float()
     y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)

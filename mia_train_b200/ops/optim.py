@@ -74,3 +74,18 @@ def adamw_reference(
     bc2 = 1 - beta2**step
     denom = (exp_avg_sq.sqrt() / (bc2**0.5)).add_(eps)
     param.addcdiv_(exp_avg, denom, value=-lr / bc1)
+
+
+@torch.no_grad()
+def ema_update(teacher: list[torch.Tensor], student: list[torch.Tensor], momentum: float) -> None:
+    """teacher <- momentum * teacher + (1 - momentum) * student, one launch for all tensors on CUDA."""
+    if not teacher:
+        return
+    from ._native import use_native
+
+    plain = all(type(t) is torch.Tensor and t.dtype == torch.float32 and t.is_contiguous() for t in teacher + student)
+    if plain and use_native(teacher[0]):
+        native().ema_update(teacher, student, float(momentum))
+        return
+    torch._foreach_mul_(teacher, momentum)
+    torch._foreach_add_(teacher, student, alpha=1 - momentum)

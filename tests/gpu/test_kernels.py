@@ -266,3 +266,19 @@ def test_mae_step_native_vs_reference_math():
         assert p.grad is not None, name
         _close(p.grad, pr.grad, rel=1e-1, atol=1e-3)
     _no_errors()
+
+
+@pytest.mark.parametrize("mnk", [(512, 512, 8192), (1536, 512, 8192), (1024, 1024, 2048)])
+def test_gemm_split_k_weight_gradient(mnk):
+    """dW-shaped GEMMs (small output, long K, fp32 accumulate) take the split-K path."""
+    m, n, k = mnk
+    torch.manual_seed(9)
+    dy = torch.randn(k, m, device=DEV).bfloat16()  # (tokens, out) -> A read M-major
+    x = torch.randn(k, n, device=DEV).bfloat16()   # (tokens, in)  -> B read N-major
+    out = torch.randn(m, n, device=DEV)
+    base = out.clone()
+    gemm(dy, x, a_kmajor=False, b_kmajor=False, out=out, accumulate=True)
+    _close(out, base + dy.float().t() @ x.float(), rel=1e-2, atol=1e-2 * math.sqrt(k))
+    fresh = gemm(dy, x, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32)
+    _close(fresh, dy.float().t() @ x.float(), rel=1e-2, atol=1e-2 * math.sqrt(k))
+    _no_errors()
