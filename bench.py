@@ -210,8 +210,10 @@ def native_arm(args: argparse.Namespace, rank: int, world: int, local: int) -> d
 
     # count this framework's kernel launches in one eager step (the replayed graph holds the same)
     launches = count_native_launches(lambda: step._body() and None, alg)
-    if args.profile_kernels and rank == 0:
-        print(kernel_table(lambda: step._body() and None, args.profile_kernels), flush=True)
+    if args.profile_kernels:  # every rank runs the profiled steps (they hold collectives)
+        table = kernel_table(lambda: step._body() and None, args.profile_kernels)
+        if rank == 0:
+            print(table, flush=True)
 
     for i in range(args.warmup):
         step(device_batch(i))

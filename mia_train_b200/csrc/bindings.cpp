@@ -32,6 +32,14 @@ void mae_restore_fwd(torch::Tensor visible, torch::Tensor token, torch::Tensor r
 void mae_restore_bwd(torch::Tensor dout, torch::Tensor restore, torch::Tensor dvis, torch::Tensor dtok);
 void norm_pix_mse(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, torch::Tensor loss, torch::Tensor grad,
                   int64_t pd, int64_t ph, int64_t pw, bool norm_pix);
+at::Tensor affinity_bce_fwd(at::Tensor logits, at::Tensor labels, std::vector<int64_t> offsets, int64_t ignore_index);
+at::Tensor affinity_bce_bwd(at::Tensor logits, at::Tensor labels, std::vector<int64_t> offsets, int64_t ignore_index,
+                            at::Tensor sums, at::Tensor grad_out);
+std::vector<at::Tensor> semantic_ce_fwd(at::Tensor logits, at::Tensor labels, c10::optional<at::Tensor> weights,
+                                        int64_t ignore_index);
+at::Tensor semantic_ce_bwd(at::Tensor logits, at::Tensor labels, c10::optional<at::Tensor> weights, int64_t ignore_index,
+                           at::Tensor stats, at::Tensor grad_out);
+at::Tensor connected_components_cpu(at::Tensor labels);
 }  // namespace mia
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -52,5 +60,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mae_restore_fwd", &mia::mae_restore_fwd);
   m.def("mae_restore_bwd", &mia::mae_restore_bwd);
   m.def("norm_pix_mse", &mia::norm_pix_mse);
+  m.def("affinity_bce_fwd", &mia::affinity_bce_fwd, "fused affinity targets + masked BCE statistics");
+  m.def("affinity_bce_bwd", &mia::affinity_bce_bwd, "gradient of the fused affinity BCE");
+  m.def("semantic_ce_fwd", &mia::semantic_ce_fwd, "fused softmax CE + confusion histogram");
+  m.def("semantic_ce_bwd", &mia::semantic_ce_bwd, "gradient of the fused softmax CE");
+  m.def("connected_components_cpu", &mia::connected_components_cpu, "connected components of equal positive labels (host)");
   m.def("check_errors", &mia::read_and_clear_errors, "read and clear the device error word");
 }
