@@ -172,6 +172,8 @@ def build_trainer(
 
 
 def run(config_path: Path, output_root: Path | None = None, resume: str | None = None) -> Path:
+    from .. import components  # noqa: F401  (populates the registries the config names)
+
     config = load_run_config(Path(config_path))
     root = Path(output_root) if output_root is not None else checkpoint_dir()
     rank, _, local_rank = init_distributed()

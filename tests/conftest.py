@@ -44,10 +44,13 @@ def _worker(rank: int, world_size: int, init_file: str, fn, args, queue) -> None
 def run_distributed(tmp_path):
     """run_distributed(fn, world_size, *args) -> {rank: result}; fn(rank, world_size, *args)."""
 
+    calls = [0]
+
     def launch(fn, world_size: int = 2, *args, timeout: float = 240.0):
         ctx = mp.get_context("spawn")
         queue = ctx.Queue()
-        init_file = str(tmp_path / f"pg_init_{os.getpid()}_{id(fn)}")
+        calls[0] += 1  # a fresh rendezvous file per launch: a used one holds the last group's state
+        init_file = str(tmp_path / f"pg_init_{os.getpid()}_{calls[0]}")
         procs = [
             ctx.Process(target=_worker, args=(r, world_size, init_file, fn, args, queue), daemon=True)
             for r in range(world_size)

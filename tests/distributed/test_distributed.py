@@ -1,0 +1,134 @@
+"""Multi-process CPU tests over Gloo: parallel wrappers, the training loop, run orchestration."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.cpu_dist
+
+CONFIG = """
+experiment_name = "dist"
+
+[model]
+name = "vit3d"
+img_size = [16, 16, 16]
+patch_size = [8, 8, 8]
+embed_dim = 32
+depth = 2
+num_heads = 2
+
+[algorithm]
+name = "mae"
+mask_ratio = 0.5
+decoder_embed_dim = 16
+decoder_depth = 1
+decoder_num_heads = 2
+
+[data]
+name = "synthetic_volumes"
+shape = [16, 16, 16]
+samples_per_epoch = 16
+
+[trainer]
+max_steps = {steps}
+batch_size = 2
+lr = 1e-3
+warmup_steps = 1
+precision = "fp32"
+log_every = 2
+checkpoint_every = 3
+seed = 0
+
+[parallelism]
+{parallelism}
+"""
+
+
+def _all_reduce(rank, world):
+    import torch.distributed as dist
+
+    t = torch.tensor([float(rank + 1)])
+    dist.all_reduce(t)
+    return float(t)
+
+
+def test_harness(run_distributed):
+    out = run_distributed(_all_reduce, 2)
+    assert out == {0: 3.0, 1: 3.0}
+
+
+def _wrapped_step(rank, world, layout):
+    import torch.distributed as dist
+
+    from mia_train_b200.algorithms.mae import MAE
+    from mia_train_b200.models.vit import ViT3D
+    from mia_train_b200.parallel.parallel_dims import ParallelDims
+    from mia_train_b200.parallel.parallelize import parallelize_algorithm
+
+    dims = ParallelDims(**layout)
+    mesh = dims.build_mesh("cpu")
+    torch.manual_seed(0)
+    model = ViT3D(img_size=(16, 16, 16), patch_size=(8, 8, 8), embed_dim=32, depth=2, num_heads=2)
+    alg = MAE(model, input_axes="lcxyz", decoder_embed_dim=16, decoder_depth=1, decoder_num_heads=2)
+    alg = parallelize_algorithm(alg, mesh, dims)
+    torch.manual_seed(100 + rank)
+    out = alg({"img": torch.randn(2, 1, 1, 16, 16, 16)})
+    out["loss"].backward()
+    # the gradient of one shared parameter, reassembled, must agree across ranks
+    g = alg.model.blocks[0].attn.qkv.weight.grad
+    full = g.full_tensor() if hasattr(g, "full_tensor") else g
+    gathered = [torch.zeros_like(full) for _ in range(world)]
+    dist.all_gather(gathered, full.contiguous())
+    return float(max((x - gathered[0]).abs().max() for x in gathered)), float(out["loss"])
+
+
+@pytest.mark.parametrize("layout,world", [
+    ({"dp_replicate": 2}, 2),
+    ({"dp_shard": 2}, 2),
+    ({"dp_shard": 2, "fsdp_unit": "model", "param_dtype": "fp32"}, 2),
+    ({"dp_replicate": 2, "dp_shard": 2}, 4),
+])
+def test_data_parallel_layouts_agree(run_distributed, layout, world):
+    out = run_distributed(_wrapped_step, world, layout)
+    for diff, loss in out.values():
+        assert diff < 1e-6 and loss == loss
+
+
+def _run_training(rank, world, root, config_path, resume):
+    from mia_train_b200.engine.run import run
+
+    return str(run(Path(config_path), output_root=Path(root), resume=resume))
+
+
+def test_run_then_resume(run_distributed, tmp_path):
+    cfg = tmp_path / "dist.toml"
+    cfg.write_text(CONFIG.format(steps=4, parallelism="dp_shard = 2"))
+    root = tmp_path / "runs"
+    out = run_distributed(_run_training, 2, str(root), str(cfg), None)
+    assert len(set(out.values())) == 1  # every rank agreed on one run directory
+    run_dir = Path(out[0])
+    assert (run_dir / "checkpoints" / "step_4").is_dir() or any((run_dir / "checkpoints").glob("step_*"))
+    assert (run_dir / "resolved_config.json").is_file()
+    cfg.write_text(CONFIG.format(steps=6, parallelism="dp_shard = 2"))
+    out2 = run_distributed(_run_training, 2, str(root), str(cfg), "latest")
+    assert out2[0] == out[0]
+    steps = sorted(int(p.name.split("_")[1]) for p in (run_dir / "checkpoints").glob("step_*") if "tmp" not in p.name)
+    assert steps[-1] == 6
+
+
+def _prep_failure(rank, world, root):
+    from mia_train_b200.engine.run import prepare_run_dir
+
+    try:
+        prepare_run_dir(Path(root) / "x", Path(root) / "does_not_exist.toml", {}, rank)
+    except RuntimeError as error:
+        return str(error)
+    return "no error"
+
+
+def test_prep_failure_reaches_every_rank(run_distributed, tmp_path):
+    out = run_distributed(_prep_failure, 2, str(tmp_path), timeout=120)
+    assert all("could not prepare" in v for v in out.values())
