@@ -58,6 +58,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--batch", type=int, default=CONFIG["per_rank_batch"])
     ap.add_argument("--depth", type=int, default=24, help="encoder depth (24 = the named config)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--dp-impl", choices=("p2p", "nccl", "allreduce"), default="p2p",
+                    help="data-parallel gradient path for N > 1 (sharded optimizer over peer memory by default)")
     ap.add_argument("--profile-kernels", type=int, default=0, metavar="STEPS",
                     help="also profile STEPS eager steps and print the per-kernel device-time table")
     return ap.parse_args()
@@ -198,7 +200,7 @@ def native_arm(args: argparse.Namespace, rank: int, world: int, local: int) -> d
                                     lambda: torch.autocast("cuda", dtype=torch.bfloat16))
 
     step = CapturedStep(alg, opt, tcfg, {"img": pool_dev[: args.batch]}, eager_steps=2, forward=forward,
-                        process_group=dist.group.WORLD if world > 1 else None)
+                        process_group=dist.group.WORLD if world > 1 else None, dp_impl=args.dp_impl)
 
     def device_batch(i: int) -> dict:
         j = (i * args.batch) % pool_dev.shape[0]
@@ -425,7 +427,7 @@ def main() -> None:
                     "model": CONFIG["model"] if args.depth == 24 else CONFIG["model"] + f" (depth {args.depth})",
                     "global_batch": args.batch * world,
                     "seq_len": CONFIG["seq_len"],
-                    "parallelism": f"dp{world}",
+                    "parallelism": f"dp{world}" + (f" (sharded optimizer, {args.dp_impl})" if world > 1 and args.impl == "native" else ""),
                     "l2": "inputs and weights larger than L2 (no flush)",
                 },
                 "mfu": round(mfu, 4),

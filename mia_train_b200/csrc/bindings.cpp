@@ -40,6 +40,20 @@ std::vector<at::Tensor> semantic_ce_fwd(at::Tensor logits, at::Tensor labels, c1
 at::Tensor semantic_ce_bwd(at::Tensor logits, at::Tensor labels, c10::optional<at::Tensor> weights, int64_t ignore_index,
                            at::Tensor stats, at::Tensor grad_out);
 at::Tensor connected_components_cpu(at::Tensor labels);
+std::vector<at::Tensor> ipc_export(int64_t nbytes, int64_t device);
+std::vector<int64_t> ipc_open(at::Tensor handles, int64_t rank, int64_t local_ptr, int64_t device);
+void ipc_close(std::vector<int64_t> peers, int64_t rank, int64_t device);
+void ipc_free(int64_t local_ptr, int64_t device);
+int64_t comm_flag_bytes();
+int64_t comm_max_blocks();
+void zero_reduce_scatter(std::vector<int64_t> grad_peers, std::vector<int64_t> flag_peers, int64_t shard_off,
+                         int64_t shard_len, at::Tensor partial, at::Tensor epoch, int64_t rank, double timeout_ms);
+void zero_norm_exchange(std::vector<int64_t> flag_peers, at::Tensor partial, at::Tensor epoch, int64_t rank,
+                        double max_norm, at::Tensor grad_scale, at::Tensor grad_norm, double timeout_ms);
+void zero_all_gather(std::vector<int64_t> data_peers, std::vector<int64_t> shadow_peers, std::vector<int64_t> flag_peers,
+                     int64_t shard_len, int64_t bf16_begin, int64_t total, at::Tensor epoch, int64_t rank, int64_t blocks,
+                     double timeout_ms);
+void zero_advance_epoch(at::Tensor epoch);
 }  // namespace mia
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -65,5 +79,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("semantic_ce_fwd", &mia::semantic_ce_fwd, "fused softmax CE + confusion histogram");
   m.def("semantic_ce_bwd", &mia::semantic_ce_bwd, "gradient of the fused softmax CE");
   m.def("connected_components_cpu", &mia::connected_components_cpu, "connected components of equal positive labels (host)");
+  m.def("ipc_export", &mia::ipc_export, "cudaMalloc + IPC handle: (local uint8 tensor, handle bytes, address)");
+  m.def("ipc_open", &mia::ipc_open, "open every peer's IPC handle -> device pointers (own pointer at own rank)");
+  m.def("ipc_close", &mia::ipc_close);
+  m.def("ipc_free", &mia::ipc_free);
+  m.def("comm_flag_bytes", &mia::comm_flag_bytes);
+  m.def("comm_max_blocks", &mia::comm_max_blocks);
+  m.def("zero_reduce_scatter", &mia::zero_reduce_scatter, "peer-memory gradient reduce-scatter + sum of squares");
+  m.def("zero_norm_exchange", &mia::zero_norm_exchange, "cross-rank grad norm -> clip scale");
+  m.def("zero_all_gather", &mia::zero_all_gather, "peer-memory parameter all-gather + local refresh");
+  m.def("zero_advance_epoch", &mia::zero_advance_epoch);
   m.def("check_errors", &mia::read_and_clear_errors, "read and clear the device error word");
 }

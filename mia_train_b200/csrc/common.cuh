@@ -28,6 +28,9 @@ enum ErrorCode : int {
   kErrGemmEpilogueWait = 103,
   kErrAttnWait = 201,
   kErrCommWait = 301,
+  kErrZeroReduceScatterWait = 401,
+  kErrZeroNormWait = 402,
+  kErrZeroAllGatherWait = 403,
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

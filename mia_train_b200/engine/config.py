@@ -1,9 +1,10 @@
 """Strict dataclasses for the `[init]`, `[lora]`, `[augment]` and `[trainer]` TOML sections.
 
 Field names, defaults and validation follow the reference's `src/engine/config.py:17-417`, so a
-config written for the reference loads here unchanged. Three `[trainer]` keys are new: `fused_optimizer` (this
-framework's CUDA AdamW over fp32 master weights), `nan_guard` (stop on a non-finite loss) and
-`watchdog_seconds` (dump stacks when a step hangs).
+config written for the reference loads here unchanged. New `[trainer]` keys: `fused_optimizer` (this
+framework's CUDA AdamW over fp32 master weights), `nan_guard` (stop on a non-finite loss),
+`watchdog_seconds` (dump stacks when a step hangs), `step_mode` (`"graph"` replays the whole step
+from one CUDA graph) and `graph_dp` (the data-parallel gradient path of the graph step).
 """
 
 from __future__ import annotations
@@ -163,6 +164,13 @@ class TrainerConfig:
     nan_guard: bool = True
     # Seconds a step may take before the watchdog thread dumps every thread's stack (0 = off).
     watchdog_seconds: float = 0.0
+    # "eager" runs the reference loop; "graph" captures forward, backward, clip, AdamW and the
+    # schedule into one CUDA graph (engine/graph_step.py). The algorithm's step must then be free
+    # of host synchronisation and shape changes (mae, simmim; not dinov3's variable mask counts).
+    step_mode: str = "eager"
+    # Data parallelism of the graph step across the dp ranks: "p2p" (sharded optimizer over peer
+    # memory), "nccl" (the same over NCCL collectives) or "allreduce" (replicated optimizer).
+    graph_dp: str = "p2p"
 
     def __post_init__(self) -> None:
         checks = [
@@ -229,6 +237,11 @@ class TrainerConfig:
                 f"fused_optimizer must be 'auto', 'on' or 'off', got {self.fused_optimizer!r}",
             ),
             (self.watchdog_seconds >= 0.0, f"watchdog_seconds must be >= 0, got {self.watchdog_seconds}"),
+            (self.step_mode in ("eager", "graph"), f"step_mode must be 'eager' or 'graph', got {self.step_mode!r}"),
+            (
+                self.graph_dp in ("p2p", "nccl", "allreduce"),
+                f"graph_dp must be 'p2p', 'nccl' or 'allreduce', got {self.graph_dp!r}",
+            ),
         ]
         for ok, message in checks:
             if not ok:

@@ -37,12 +37,33 @@ from .config import TrainerConfig
 from .optimizer import lr_multiplier, weight_decay_at
 
 _ALIGN = 64
+# Data-parallel gradient paths: "allreduce" (NCCL all-reduce of the whole flat gradient, replicated
+# AdamW), "p2p" (sharded optimizer over peer memory, engine/zero.py) and "nccl" (the same sharded
+# layout over NCCL collectives).
+DP_IMPLS = ("allreduce", "p2p", "nccl")
 
 
 class FlatParameters:
-    """Every trainable parameter of `module` as a view into flat fp32 param/grad buffers."""
+    """Every trainable parameter of `module` as a view into flat fp32 param/grad buffers.
 
-    def __init__(self, module: nn.Module, shadow_min_dim: int = 2) -> None:
+    Slots are `_ALIGN`-element aligned and the total is padded to a multiple of `world * _ALIGN`,
+    so a sharded optimizer can split the buffer into equal, aligned, contiguous slices. With
+    `bf16_region=True` the weights of Linear and convolution modules (whose only consumers run in
+    bf16) are placed after everything else, starting at `bf16_begin`. The bf16 shadow buffer
+    mirrors the fp32 layout element for element; parameters with `ndim >= shadow_min_dim` expose
+    their slice of it as `_mia_shadow`. `allocate(numel, dtype) -> (tensor, peer pointers)` lets
+    the caller place the buffers in peer-mapped memory.
+    """
+
+    def __init__(
+        self,
+        module: nn.Module,
+        shadow_min_dim: int = 2,
+        *,
+        world: int = 1,
+        bf16_region: bool = False,
+        allocate: Callable[[int, torch.dtype], tuple[torch.Tensor, list[int] | None]] | None = None,
+    ) -> None:
         seen: set[int] = set()
         params: list[nn.Parameter] = []
         for p in module.parameters():
@@ -51,32 +72,50 @@ class FlatParameters:
                 params.append(p)
         if not params:
             raise ValueError("FlatParameters: nothing requires grad")
+        gemm_weights: set[int] = set()
+        if bf16_region:
+            for m in module.modules():
+                if isinstance(m, (nn.Linear, nn.modules.conv._ConvNd)) and isinstance(m.weight, nn.Parameter):
+                    gemm_weights.add(id(m.weight))
+        params = [p for p in params if id(p) not in gemm_weights] + [p for p in params if id(p) in gemm_weights]
         device = params[0].device
         offsets, total = [], 0
-        shadow_offsets, shadow_total = [], 0
+        self.bf16_begin = -1
         for p in params:
+            if self.bf16_begin < 0 and id(p) in gemm_weights:
+                self.bf16_begin = total
             offsets.append(total)
             total += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
-            if p.ndim >= shadow_min_dim:
-                shadow_offsets.append(shadow_total)
-                shadow_total += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
-            else:
-                shadow_offsets.append(None)
+        unit = _ALIGN * world
+        total = (total + unit - 1) // unit * unit
+        if self.bf16_begin < 0:
+            self.bf16_begin = total
         self.params = params
-        self.data = torch.zeros(total, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(total, dtype=torch.float32, device=device)
-        self.shadow = torch.zeros(max(shadow_total, 1), dtype=torch.bfloat16, device=device)
+        self.offsets = offsets
+        self.total = total
+        self.world = world
+        self.peers: dict[str, list[int]] | None = None
+        if allocate is None:
+            self.data = torch.zeros(total, dtype=torch.float32, device=device)
+            self.grad = torch.zeros(total, dtype=torch.float32, device=device)
+            self.shadow = torch.zeros(total, dtype=torch.bfloat16, device=device)
+        else:
+            self.data, pd = allocate(total, torch.float32)
+            self.grad, pg = allocate(total, torch.float32)
+            self.shadow, ps = allocate(total, torch.bfloat16)
+            if pd is not None:
+                self.peers = {"data": pd, "grad": pg, "shadow": ps}
         self._hooks = []
         with torch.no_grad():
-            for p, off, soff in zip(params, offsets, shadow_offsets, strict=True):
+            for p, off in zip(params, offsets, strict=True):
                 n = p.numel()
                 view = self.data[off:off + n].view_as(p)
                 view.copy_(p.data)
                 p.data = view
                 p.main_grad = self.grad[off:off + n].view_as(p)  # type: ignore[attr-defined]
-                if soff is not None:
-                    sview = self.shadow[soff:soff + n].view_as(p)
-                    sview.copy_(view)
+                sview = self.shadow[off:off + n].view_as(p)
+                sview.copy_(view)
+                if p.ndim >= shadow_min_dim:
                     p._mia_shadow = sview  # type: ignore[attr-defined]
                 self._hooks.append(p.register_post_accumulate_grad_hook(_fold_into_main_grad))
         self.numel = sum(p.numel() for p in params)
@@ -87,10 +126,7 @@ class FlatParameters:
     @torch.no_grad()
     def refresh_shadows(self) -> None:
         """Re-derive the bf16 copies from the fp32 params (after loading weights)."""
-        for p in self.params:
-            shadow = getattr(p, "_mia_shadow", None)
-            if shadow is not None:
-                shadow.copy_(p.data)
+        self.shadow.copy_(self.data)
 
     def release(self) -> None:
         for h in self._hooks:
@@ -99,6 +135,10 @@ class FlatParameters:
             for attr in ("main_grad", "_mia_shadow"):
                 if hasattr(p, attr):
                     delattr(p, attr)
+        if self.peers is not None:  # peer-mapped buffers are about to be freed: give params their own memory
+            with torch.no_grad():
+                for p in self.params:
+                    p.data = p.data.clone()
 
 
 def _fold_into_main_grad(p: torch.Tensor) -> None:
@@ -173,16 +213,42 @@ class CapturedStep:
         capture: bool = True,
         forward: Callable[[Any], dict[str, torch.Tensor]] | None = None,
         process_group: Any = None,
+        dp_impl: str = "p2p",
+        comm_timeout_ms: float = 10_000.0,
     ) -> None:
         if not hasattr(optimizer, "grad_scale"):
             raise TypeError("CapturedStep needs the fused optimizer (FusedAdamW)")
+        if dp_impl not in DP_IMPLS:
+            raise ValueError(f"dp_impl must be one of {DP_IMPLS}, got {dp_impl!r}")
         self.algorithm = algorithm
         self.optimizer = optimizer
         self.config = config
         self.device = next(algorithm.parameters()).device
-        self.flat = FlatParameters(algorithm)
+        self.process_group = process_group
+        self.world = 1
+        if process_group is not None:
+            import torch.distributed as dist
+
+            self.world = dist.get_world_size(process_group)
+        self.dp_impl = dp_impl if self.world > 1 else "allreduce"
+        self.zero: Any = None
+        if self.dp_impl == "allreduce":
+            self.flat = FlatParameters(algorithm)
+        else:
+            from .zero import IpcBuffers, ShardedStep
+
+            ipc = IpcBuffers(process_group, self.device) if self.dp_impl == "p2p" else None
+            self.flat = FlatParameters(
+                algorithm, world=self.world, bf16_region=config.precision == "bf16",
+                allocate=ipc.allocate if ipc is not None else None,
+            )
         self.schedule = DeviceSchedule(optimizer, config, start_step)
         optimizer.external_hyper = self.schedule.current  # type: ignore[attr-defined]
+        if self.dp_impl != "allreduce":
+            self.zero = ShardedStep(
+                self.flat, optimizer, process_group, "p2p" if self.dp_impl == "p2p" else "nccl",
+                config.grad_clip_norm, self.schedule.current, ipc=ipc, timeout_ms=comm_timeout_ms,
+            )
         self.static_batch = _to_static(example_batch, self.device)
         self.static_metrics: dict[str, torch.Tensor] = {}
         self.eager_steps = eager_steps
@@ -191,12 +257,6 @@ class CapturedStep:
         self.graph: torch.cuda.CUDAGraph | None = None
         self._forward = forward or algorithm
         self._autocast_dtype = torch.bfloat16 if config.precision == "bf16" else None
-        self.process_group = process_group
-        self.world = 1
-        if process_group is not None:
-            import torch.distributed as dist
-
-            self.world = dist.get_world_size(process_group)
 
     def _body(self) -> dict[str, torch.Tensor]:
         self.flat.zero_grad()
@@ -208,6 +268,11 @@ class CapturedStep:
             metrics = self._forward(self.static_batch)
         metrics["loss"].backward()
         out = {k: v.detach() for k, v in metrics.items()}
+        if self.zero is not None:
+            norm = self.zero.step()
+            if self.config.grad_clip_norm is not None:
+                out["grad_norm"] = norm
+            return out
         if self.world > 1:
             import torch.distributed as dist
 
@@ -256,6 +321,10 @@ class CapturedStep:
 
     def release(self) -> None:
         self.graph = None
+        if self.zero is not None:
+            self.zero.gather_masters()
         self.flat.release()
+        if self.zero is not None:
+            self.zero.release()
         if hasattr(self.optimizer, "external_hyper"):
             del self.optimizer.external_hyper

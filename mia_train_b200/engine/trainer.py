@@ -110,8 +110,15 @@ class Trainer:
         if config.activation_checkpointing:
             apply_activation_checkpointing(algorithm)
         algorithm = algorithm.to(self.device)
-        if mesh is not None:
+        self.graph_mode = config.step_mode == "graph"
+        if self.graph_mode:
+            self._check_graph_mode()
+        if mesh is not None and not self.graph_mode:
             parallelize_algorithm(algorithm, mesh, self.dims)
+        elif self.graph_mode and dist.is_initialized() and dist.get_world_size() > 1:
+            for t in list(algorithm.parameters()) + list(algorithm.buffers()):  # identical replicas
+                dist.broadcast(t.data, src=0)
+        self.graph_step: Any = None
         self.algorithm = algorithm
         self.optimizer = build_optimizer(self.algorithm, config)
         self.scheduler = build_lr_scheduler(self.optimizer, config)
@@ -129,6 +136,36 @@ class Trainer:
         self.val_loader = val_dataset.build_dataloader(shuffle=False, **loader_args) if val_dataset else None
         self.is_primary = not dist.is_initialized() or dist.get_rank() == 0
         self.logger = MetricLogger(log_dir=self.output_dir / "tensorboard", is_primary=self.is_primary)
+
+    def _check_graph_mode(self) -> None:
+        problems = []
+        if self.device.type != "cuda":
+            problems.append("a CUDA device")
+        if self.config.fused_optimizer == "off":
+            problems.append("the fused optimizer (fused_optimizer != 'off')")
+        if self.dims.tp > 1:
+            problems.append("tp = 1 (tensor parallelism runs eagerly)")
+        if self.config.freeze_backbone_steps > 0:
+            problems.append("no backbone freeze (the captured step cannot change requires_grad)")
+        if problems:
+            raise ValueError("step_mode = 'graph' needs " + ", ".join(problems))
+
+    def _build_graph_step(self, example: Any, start_step: int) -> Any:
+        from .graph_step import CapturedStep
+
+        group = dist.group.WORLD if dist.is_initialized() and dist.get_world_size() > 1 else None
+        step = CapturedStep(self.algorithm, self.optimizer, self.config, example, start_step=start_step,
+                            process_group=group, dp_impl=self.config.graph_dp)
+        if step.zero is not None:
+            step.zero.import_state(self.optimizer)
+        return step
+
+    def _save(self, step: int) -> None:
+        if self.graph_step is not None and self.graph_step.zero is not None:
+            self.graph_step.zero.export_state(self.optimizer)
+        self.checkpoints.save(step)
+        if self.graph_step is not None and self.graph_step.zero is not None:
+            self.optimizer.state.clear()
 
     def _autocast(self) -> Any:
         dtype = _AUTOCAST.get(self.config.precision)
@@ -220,19 +257,26 @@ class Trainer:
                 with annotate("data_wait"):
                     raw = next(batches)
                 data_seconds += time.perf_counter() - t0
-                with annotate("h2d"):
-                    batch = move_to_device(raw, self.device)
-                with annotate("forward"), self._autocast():
-                    metrics = self.algorithm(batch)
-                with annotate("backward"):
-                    metrics["loss"].backward()
-                if self.config.grad_clip_norm is not None:
-                    with annotate("grad_clip"):
-                        metrics["grad_norm"] = self._clip()
-                with annotate("optimizer"):
-                    self.optimizer.step()
+                if self.graph_mode:
+                    if self.graph_step is None:
+                        self.graph_step = self._build_graph_step(raw, step)
+                    with annotate("graph_step"):
+                        metrics = dict(self.graph_step(raw))
                     self.scheduler.step()
-                    self.optimizer.zero_grad(set_to_none=True)
+                else:
+                    with annotate("h2d"):
+                        batch = move_to_device(raw, self.device)
+                    with annotate("forward"), self._autocast():
+                        metrics = self.algorithm(batch)
+                    with annotate("backward"):
+                        metrics["loss"].backward()
+                    if self.config.grad_clip_norm is not None:
+                        with annotate("grad_clip"):
+                            metrics["grad_norm"] = self._clip()
+                    with annotate("optimizer"):
+                        self.optimizer.step()
+                        self.scheduler.step()
+                        self.optimizer.zero_grad(set_to_none=True)
                 step += 1
                 self.algorithm.after_optimizer_step(step)
                 if frozen and step >= self.config.freeze_backbone_steps:
@@ -258,14 +302,17 @@ class Trainer:
                     logged_at = step
                     self.logger.log(step, logged)
                 if self.config.checkpoint_every and step % self.config.checkpoint_every == 0:
-                    self.checkpoints.save(step)
+                    self._save(step)
                 if self.config.val_every and step % self.config.val_every == 0:
                     self.logger.log(step, self.validate(), prefix="val")
                     self.algorithm.train()
                     data_seconds, window_start = 0.0, time.perf_counter()
                 profiler.step()
         if self.config.checkpoint_every and step > resumed_from and step % self.config.checkpoint_every != 0:
-            self.checkpoints.save(step)
+            self._save(step)
+        if self.graph_step is not None:
+            self.graph_step.release()
+            self.graph_step = None
         self.logger.close()
         return step
 

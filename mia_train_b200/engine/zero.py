@@ -1,0 +1,234 @@
+"""Sharded data-parallel optimizer step (gradients reduce-scattered, AdamW on a shard, params gathered).
+
+Every rank keeps the whole model (a ViT-L is 1.3 GB of fp32 parameters against 180 GB of HBM), so
+forward and backward need no parameter collectives at all. After backward, rank r owns the r-th
+contiguous slice of the flat parameter buffer:
+
+1. reduce-scatter: rank r sums slice r of every rank's flat gradient,
+2. the global gradient norm is exchanged and turned into the clip coefficient (times 1/world),
+3. AdamW updates slice r only (exp_avg / exp_avg_sq exist only for the owned slice, so optimizer
+   memory is 1/world of the unsharded optimizer),
+4. all-gather: every rank receives the other slices. Matrices consumed by GEMMs and convolutions
+   (the bf16 region of `FlatParameters`) travel as their bf16 values -- under bf16 compute that is
+   all any consumer reads -- and the receiver rebuilds its fp32 copy from them; everything else
+   travels in fp32. The owner keeps the exact fp32 master of its slice.
+
+Two implementations of the same layout:
+
+* `"p2p"` -- three native kernels over CUDA-IPC peer memory (`csrc/comm.cu`): the
+  reduce-scatter reads every peer's gradient slice over NVLink with 16-byte loads, the norm
+  exchange is one CTA, the all-gather pushes the owned slice into every peer with 16-byte stores
+  and refreshes the received slices locally; barriers are flag words with bounded waits.
+* `"nccl"` -- `reduce_scatter_tensor` / `all_reduce` / `all_gather_into_tensor` on the same flat
+  buffers (fp32 all-gather of the whole slice), kept as the baseline the fused path is compared to.
+
+The reference reaches the same end through FSDP2 (`src/distributed/parallelize.py:29-57`), which
+all-gathers fp32 parameters per unit in forward and backward and reduce-scatters fp32 gradients.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from ..ops._native import native
+from ..ops.optim import adamw_step, clip_coefficient, grad_sumsq
+
+IMPLS = ("p2p", "nccl")
+
+
+class IpcBuffers:
+    """Device buffers allocated with cudaMalloc and mapped into every peer through CUDA IPC."""
+
+    def __init__(self, group: Any, device: torch.device) -> None:
+        self.group = group
+        self.device = device
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self._owned: list[tuple[list[int], int]] = []
+
+    def allocate(self, numel: int, dtype: torch.dtype) -> tuple[torch.Tensor, list[int]]:
+        """(local tensor, [device pointer of every rank's copy]) -- a collective call."""
+        elem = torch.empty((), dtype=dtype).element_size()
+        nbytes = max(numel * elem, 256)
+        local, handle, addr = native().ipc_export(nbytes, self.device.index)
+        handles = [torch.empty_like(handle) for _ in range(self.world)]
+        gathered = _all_gather_cpu(handle, self.group)
+        for h, g in zip(handles, gathered, strict=True):
+            h.copy_(g)
+        peers = native().ipc_open(torch.stack(handles), self.rank, int(addr[0]), self.device.index)
+        self._owned.append((peers, int(addr[0])))
+        return local.view(dtype)[:numel], peers
+
+    def release(self) -> None:
+        if not self._owned:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every peer stopped using our memory
+        for peers, _ in self._owned:
+            native().ipc_close(peers, self.rank, self.device.index)
+        dist.barrier(group=self.group)  # every peer closed its mapping of ours
+        for _, addr in self._owned:
+            native().ipc_free(addr, self.device.index)
+        self._owned = []
+
+
+def _all_gather_cpu(t: torch.Tensor, group: Any) -> list[torch.Tensor]:
+    """All-gather a small CPU byte tensor through whatever backend the group uses."""
+    if dist.get_backend(group) == "nccl":
+        dev = torch.device("cuda", torch.cuda.current_device())
+        src = t.to(dev)
+        out = [torch.empty_like(src) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(out, src, group=group)
+        return [o.cpu() for o in out]
+    out = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(out, t, group=group)
+    return out
+
+
+class ShardedStep:
+    """Steps 1-4 above for a `FlatParameters` built with `world` and matching buffers."""
+
+    def __init__(
+        self,
+        flat: Any,
+        optimizer: torch.optim.Optimizer,
+        group: Any,
+        impl: str,
+        max_norm: float | None,
+        hyper: torch.Tensor,
+        ipc: IpcBuffers | None = None,
+        timeout_ms: float = 10_000.0,
+    ) -> None:
+        if impl not in IMPLS:
+            raise ValueError(f"sharded step impl must be one of {IMPLS}, got {impl!r}")
+        self.flat = flat
+        self.group = group
+        self.impl = impl
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.max_norm = float(max_norm) if max_norm is not None else 0.0
+        self.timeout_ms = timeout_ms
+        self.hyper = hyper
+        dev = flat.data.device
+        self.shard_len = flat.total // self.world
+        self.shard_off = self.rank * self.shard_len
+        lo, hi = self.shard_off, self.shard_off + self.shard_len
+        group_of = {id(p): gi for gi, g in enumerate(optimizer.param_groups) for p in g["params"]}
+        eps = {g["eps"] for g in optimizer.param_groups}
+        if len(eps) != 1:
+            raise ValueError("the sharded AdamW needs one eps for all param groups")
+        self.eps = float(eps.pop())
+        self.exp_avg = torch.zeros(self.shard_len, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(self.shard_len, dtype=torch.float32, device=dev)
+        params, grads, m, v, steps, gidx, shadows = [], [], [], [], [], [], []
+        self.slices: list[tuple[Any, int, int]] = []
+        for p, off in zip(flat.params, flat.offsets, strict=True):
+            a, b = max(off, lo), min(off + p.numel(), hi)
+            if a >= b:
+                continue
+            if id(p) not in group_of:
+                raise ValueError("every flat parameter must belong to an optimizer param group")
+            params.append(flat.data[a:b])
+            grads.append(flat.grad[a:b])
+            m.append(self.exp_avg[a - lo:b - lo])
+            v.append(self.exp_avg_sq[a - lo:b - lo])
+            steps.append(torch.zeros((), dtype=torch.float32, device=dev))
+            gidx.append(group_of[id(p)])
+            shadows.append(flat.shadow[a:b])
+            self.slices.append((p, a, b))
+        self._lists = (params, grads, m, v, steps, shadows)
+        self._gidx = torch.tensor(gidx, dtype=torch.int32, device=dev)
+        self.grad_scale = torch.ones((), dtype=torch.float32, device=dev)
+        self.grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
+        if impl == "p2p":
+            if ipc is None or flat.peers is None:
+                raise ValueError("the p2p implementation needs FlatParameters allocated through IpcBuffers")
+            self.ipc = ipc
+            self.blocks = min(2 * torch.cuda.get_device_properties(dev).multi_processor_count,
+                              int(native().comm_max_blocks()))
+            self.partial = torch.zeros(self.blocks, dtype=torch.float32, device=dev)
+            self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+            _, self.flag_peers = ipc.allocate(int(native().comm_flag_bytes()) // 4, torch.int32)
+        self.grad_shard = flat.grad[lo:hi]
+
+    def step(self) -> torch.Tensor:
+        """Run after backward on every rank; returns the (device) global gradient norm."""
+        params, grads, m, v, steps, shadows = self._lists
+        if self.impl == "p2p":
+            n = native()
+            n.zero_reduce_scatter(self.flat.peers["grad"], self.flag_peers, self.shard_off, self.shard_len,
+                                  self.partial, self.epoch, self.rank, self.timeout_ms)
+            n.zero_norm_exchange(self.flag_peers, self.partial, self.epoch, self.rank, self.max_norm,
+                                 self.grad_scale, self.grad_norm, self.timeout_ms)
+            if params:
+                adamw_step(params, grads, m, v, steps, self._gidx, self.hyper, self.eps, self.grad_scale, shadows)
+            n.zero_all_gather(self.flat.peers["data"], self.flat.peers["shadow"], self.flag_peers, self.shard_len,
+                              self.flat.bf16_begin, self.flat.total, self.epoch, self.rank, self.blocks, self.timeout_ms)
+            n.zero_advance_epoch(self.epoch)
+            return self.grad_norm
+        # NCCL baseline on the same layout (in-place reduce-scatter into the owned slice)
+        dist.reduce_scatter_tensor(self.grad_shard, self.flat.grad, group=self.group)
+        sumsq = grad_sumsq([self.grad_shard])
+        dist.all_reduce(sumsq, group=self.group)
+        norm = sumsq.sqrt() / self.world
+        coef = clip_coefficient(norm, self.max_norm) if self.max_norm > 0 else torch.ones_like(norm)
+        self.grad_scale.copy_(coef / self.world)
+        self.grad_norm.copy_(norm)
+        if params:
+            adamw_step(params, grads, m, v, steps, self._gidx, self.hyper, self.eps, self.grad_scale, shadows)
+        dist.all_gather_into_tensor(self.flat.data, self.flat.data[self.shard_off:self.shard_off + self.shard_len],
+                                    group=self.group)
+        self.flat.shadow.copy_(self.flat.data)
+        return self.grad_norm
+
+    @torch.no_grad()
+    def gather_masters(self) -> None:
+        """Make every rank's fp32 copy exact (the bf16 region is bf16-rounded off the owner)."""
+        dist.all_gather_into_tensor(self.flat.data, self.flat.data[self.shard_off:self.shard_off + self.shard_len].clone(),
+                                    group=self.group)
+
+    @torch.no_grad()
+    def export_state(self, optimizer: torch.optim.Optimizer) -> None:
+        """Write whole-parameter AdamW state (torch layout) into `optimizer.state` on every rank."""
+        self.gather_masters()
+        dev = self.flat.data.device
+        full = {}
+        for name, shard in (("exp_avg", self.exp_avg), ("exp_avg_sq", self.exp_avg_sq)):
+            buf = torch.empty(self.flat.total, dtype=torch.float32, device=dev)
+            dist.all_gather_into_tensor(buf, shard, group=self.group)
+            full[name] = buf
+        step = self._lists[4][0].detach().clone() if self._lists[4] else torch.zeros((), device=dev)
+        dist.broadcast(step, src=dist.get_global_rank(self.group, 0) if self.group is not None else 0, group=self.group)
+        for p, off in zip(self.flat.params, self.flat.offsets, strict=True):
+            n = p.numel()
+            optimizer.state[p] = {
+                "step": step.clone(),
+                "exp_avg": full["exp_avg"][off:off + n].view_as(p).clone(),
+                "exp_avg_sq": full["exp_avg_sq"][off:off + n].view_as(p).clone(),
+            }
+
+    @torch.no_grad()
+    def import_state(self, optimizer: torch.optim.Optimizer) -> bool:
+        """Load the owned slice's moments from whole-parameter state in `optimizer.state` (if any)."""
+        offsets = {id(p): off for p, off in zip(self.flat.params, self.flat.offsets, strict=True)}
+        found = False
+        steps = self._lists[4]
+        for i, (p, a, b) in enumerate(self.slices):
+            state = optimizer.state.get(p)
+            if not state or "exp_avg" not in state:
+                continue
+            found = True
+            off = offsets[id(p)]
+            lo = self.shard_off
+            self.exp_avg[a - lo:b - lo].copy_(state["exp_avg"].reshape(-1)[a - off:b - off])
+            self.exp_avg_sq[a - lo:b - lo].copy_(state["exp_avg_sq"].reshape(-1)[a - off:b - off])
+            steps[i].copy_(state["step"])
+        optimizer.state.clear()  # the shards are the live state now
+        return found
+
+    def release(self) -> None:
+        if self.impl == "p2p":
+            self.ipc.release()

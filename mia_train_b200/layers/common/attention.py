@@ -26,6 +26,7 @@ import torch.nn as nn
 
 from ...ops._native import reference_math
 from ...ops.attention import attention, attention_reference, rope_attention
+from ...parallel.tensor_parallel import rope_to_tp
 from .lora import apply_linear
 from .rope import RotaryTables
 
@@ -84,7 +85,7 @@ class SelfAttention(_AttentionBase):
 
     def _attend_packed(self, qkv: torch.Tensor, rope: Any) -> torch.Tensor:
         if rope is None or isinstance(rope, RotaryTables):
-            angles = rope.angles if rope is not None else None
+            angles = rope_to_tp(rope.angles, self) if rope is not None else None
             pairs = rope.pairs if rope is not None else None
             return rope_attention(qkv, angles, pairs, self.scale)
         q, k, v = qkv.unbind(dim=2)

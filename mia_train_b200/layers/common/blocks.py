@@ -14,7 +14,7 @@ import torch.nn as nn
 from ...ops.mlp import mlp
 from ...ops.norm import layer_norm
 from .attention import SelfAttention
-from .lora import apply_linear, is_adapted
+from .lora import apply_linear, needs_per_layer
 from .rope import AxialRotaryEmbedding
 
 
@@ -43,6 +43,6 @@ class TransformerBlock(nn.Module):
         x = self.attn(h, rope=rope, residual=x)
         h = layer_norm(x, self.norm2.weight, self.norm2.bias, self.norm2.eps)
         fc1, fc2 = self.mlp[0], self.mlp[2]
-        if is_adapted(fc1) or is_adapted(fc2):
+        if needs_per_layer(fc1) or needs_per_layer(fc2):
             return apply_linear(fc2, apply_linear(fc1, h, activation="gelu"), residual=x)
         return mlp(h, fc1.weight, fc1.bias, fc2.weight, fc2.bias, residual=x)

@@ -95,6 +95,10 @@ def apply_linear(
     gamma: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """`residual + gamma * act(module(x))` with the epilogue fused into the native GEMM."""
+    if hasattr(module, "_tp_mode"):  # a tensor-parallel shard: local GEMM plus its collective
+        from ...parallel.tensor_parallel import tp_linear
+
+        return tp_linear(module, x, activation=activation, residual=residual, gamma=gamma)
     if isinstance(module, LoRAMixin):
         y = linear(x, module.weight, module.bias)
         y = y + module.lora_forward(x).to(y.dtype)
@@ -108,3 +112,8 @@ def apply_linear(
 
 def is_adapted(module: nn.Module) -> bool:
     return isinstance(module, LoRAMixin)
+
+
+def needs_per_layer(module: nn.Module) -> bool:
+    """LoRA-adapted or tensor-parallel: the layer must run through `apply_linear`, not a fused op."""
+    return isinstance(module, LoRAMixin) or hasattr(module, "_tp_mode")

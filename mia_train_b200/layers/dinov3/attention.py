@@ -25,6 +25,7 @@ import torch.nn.functional as F
 
 from ...ops._native import reference_math
 from ...ops.attention import rope_attention
+from ...parallel.tensor_parallel import rope_to_tp
 from ..common.attention import flash4_status
 from ..common.batched_tokens import cat_keep_shapes, uncat_with_shapes
 from ..common.lora import apply_linear
@@ -98,6 +99,10 @@ class SelfAttention(nn.Module):
     # -- projections ----------------------------------------------------------------------
     def _qkv(self, x: torch.Tensor) -> torch.Tensor:
         if isinstance(self.qkv, LinearKMaskedBias) and self.qkv.bias is not None:
+            if hasattr(self.qkv, "_tp_mode"):
+                from ...parallel.tensor_parallel import tp_linear
+
+                return tp_linear(self.qkv, x, bias=self.qkv.masked_bias())
             from ...ops.linear import linear
 
             return linear(x, self.qkv.weight, self.qkv.masked_bias())
@@ -124,7 +129,7 @@ class SelfAttention(nn.Module):
                 hw_angles = torch.atan2(sin[..., : sin.shape[-1] // 2], cos[..., : cos.shape[-1] // 2])
             prefix = n - hw_angles.shape[-2]
             assert prefix >= 0
-            angles = F.pad(hw_angles.float(), (0, 0, prefix, 0))
+            angles = F.pad(rope_to_tp(hw_angles.float(), self), (0, 0, prefix, 0))
             if angles.dim() == 2:
                 angles = angles.unsqueeze(0)
         pairs = self._pairs_on(qkv.device) if angles is not None else None

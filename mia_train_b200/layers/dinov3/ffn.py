@@ -16,7 +16,7 @@ import torch.nn.functional as F
 
 from ...ops.mlp import mlp
 from ..common.batched_tokens import cat_keep_shapes, uncat_with_shapes
-from ..common.lora import apply_linear, is_adapted
+from ..common.lora import apply_linear, needs_per_layer
 
 
 class ListForwardMixin:
@@ -55,7 +55,7 @@ class Mlp(nn.Module, ListForwardMixin):
                 y = y * gamma
             return y if residual is None else residual + y
         exact_gelu = isinstance(self.act, nn.GELU) and getattr(self.act, "approximate", "none") == "none"
-        if exact_gelu and gamma is None and not (is_adapted(self.fc1) or is_adapted(self.fc2)):
+        if exact_gelu and gamma is None and not (needs_per_layer(self.fc1) or needs_per_layer(self.fc2)):
             return mlp(x, self.fc1.weight, self.fc1.bias, self.fc2.weight, self.fc2.bias, residual=residual)
         h = apply_linear(self.fc1, x, activation="gelu") if exact_gelu else self.act(apply_linear(self.fc1, x))
         return apply_linear(self.fc2, h, residual=residual, gamma=gamma)

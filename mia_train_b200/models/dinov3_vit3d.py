@@ -354,15 +354,10 @@ class DinoVisionTransformer3D(BaseModel):
     def extra_forward_methods(self) -> tuple[str, ...]:
         return ("forward_features", "get_intermediate_layers")
 
-    def tensor_parallel_plan(self) -> dict[str, Any]:
+    def tensor_parallel_plan(self) -> Any:
         from ..parallel.tensor_parallel import vit_block_plan
 
         return vit_block_plan(self.blocks, prefix="blocks")
-
-    def after_tensor_parallel(self, tp_mesh) -> None:
-        from ..parallel.tensor_parallel import localize_heads
-
-        localize_heads(self.blocks, tp_mesh.size())
 
     def flops(self, input_shape: tuple[int, ...]) -> int:
         r = self.spatial_rank

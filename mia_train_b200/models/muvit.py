@@ -188,6 +188,11 @@ class MuViT3D(BaseModel):
             "mlp": tuple(layer for b in self.blocks for layer in (b.mlp[0], b.mlp[2])),
         }
 
+    def tensor_parallel_plan(self):
+        from ..parallel.tensor_parallel import vit_block_plan
+
+        return vit_block_plan(self.blocks)
+
     def flops(self, input_shape: tuple[int, ...]) -> int:
         expected = (self.num_levels, self.in_channels, *self.img_size)
         if tuple(input_shape) != expected:

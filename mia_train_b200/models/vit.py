@@ -16,6 +16,8 @@ Differences:
 
 from __future__ import annotations
 
+from typing import Any
+
 import math
 
 import torch
@@ -194,6 +196,12 @@ class ViT3D(BaseModel):
             "attn_proj": tuple(b.attn.proj for b in self.blocks),
             "mlp": tuple(layer for b in self.blocks for layer in (b.mlp[0], b.mlp[2])),
         }
+
+    def tensor_parallel_plan(self) -> Any:
+        """Head-sharded attention and column/row-sharded MLP in every block."""
+        from ..parallel.tensor_parallel import vit_block_plan
+
+        return vit_block_plan(self.blocks)
 
     def flops(self, input_shape: tuple[int, ...]) -> int:
         if tuple(input_shape[-SPATIAL_RANK:]) != self.img_size:

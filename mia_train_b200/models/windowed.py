@@ -19,6 +19,7 @@ from ..layers.common.lora import apply_linear
 from ..layers.dinov3.block import SelfAttentionBlock, _norm
 from ..layers.dinov3.rope import RopeTables
 from ..ops.attention import attention, rope_attention, rotate_pairs
+from ..parallel.tensor_parallel import rope_to_tp
 
 
 def window_partition(x: torch.Tensor, grid: tuple[int, int, int], w: int) -> torch.Tensor:
@@ -50,8 +51,9 @@ def windowed_block_forward(
     if any(g % w for g in grid):
         raise ValueError(f"patch grid {grid} is not divisible by window_size {w}")
     attn = blk.attn
-    b, n_tok, c = x.shape
+    b, n_tok, _ = x.shape
     heads, hd = attn.num_heads, attn.head_dim
+    c = heads * hd  # this rank's share of the width under tensor parallelism
     h = _norm(blk.norm1, x)
     qkv = attn._qkv(h)  # (B, P + N, 3C)
     pre, pat = qkv[:, :n_prefix], qkv[:, n_prefix:]
@@ -61,7 +63,7 @@ def windowed_block_forward(
     packed = torch.cat([pre_rep, win], dim=1).reshape(b * nwin, n_prefix + w**3, 3, heads, hd)
     angles_win = pairs = None
     if rope is not None:
-        ang = rope.angles.float()  # (N, D/2)
+        ang = rope_to_tp(rope.angles.float(), attn)  # (N, D/2)
         ang_w = window_partition(ang.unsqueeze(0), grid, w)  # (nw, w^3, D/2)
         ang_w = F.pad(ang_w, (0, 0, n_prefix, 0))
         angles_win = ang_w.repeat(b, 1, 1)
@@ -73,7 +75,7 @@ def windowed_block_forward(
     k_all = qkv[..., c : 2 * c].reshape(b, n_tok, heads, hd)
     v_all = qkv[..., 2 * c :].reshape(b, n_tok, heads, hd)
     if rope is not None:
-        full = F.pad(rope.angles.float(), (0, 0, n_prefix, 0)).unsqueeze(0)
+        full = F.pad(rope_to_tp(rope.angles.float(), attn), (0, 0, n_prefix, 0)).unsqueeze(0)
         k_all = rotate_pairs(k_all, full, pairs)
     out_pre = attention(q_pre.contiguous(), k_all.contiguous(), v_all.contiguous(), attn.scale).reshape(b, n_prefix, c)
     out = torch.cat([out_pre, out_pat.to(out_pre.dtype)], dim=1)

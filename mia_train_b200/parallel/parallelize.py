@@ -32,6 +32,7 @@ from torch.distributed.tensor.parallel import parallelize_module
 from ..algorithms.base import BaseAlgorithm
 from ..models.base import BaseModel
 from .parallel_dims import ParallelDims
+from .tensor_parallel import BlockTensorParallelPlan, apply_tensor_parallel
 
 
 def _apply_tensor_parallel(model: nn.Module, mesh: DeviceMesh, dims: ParallelDims) -> None:
@@ -42,6 +43,9 @@ def _apply_tensor_parallel(model: nn.Module, mesh: DeviceMesh, dims: ParallelDim
         raise ValueError(
             f"{type(model).__name__} does not define a tensor_parallel_plan(), but tp={dims.tp} was requested"
         )
+    if isinstance(plan, BlockTensorParallelPlan):
+        apply_tensor_parallel(plan, mesh["tp"].get_group())
+        return
     parallelize_module(model, mesh["tp"], plan)
     prepare = getattr(model, "after_tensor_parallel", None)
     if prepare is not None:
