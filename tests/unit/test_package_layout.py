@@ -25,9 +25,3 @@ def test_no_scratch_imports_and_no_compat_layers():
         for word in banned:
             assert word not in text, f"{path} mentions {word!r}"
         assert not scratch.search(text), f"{path} refers to the scratch folder"
-
-
-def test_cuda_sources_have_no_cluster_multicast_loads():
-    qualifier = "multicast" + "::" + "cluster"  # spelled in pieces so this test is not itself a match
-    for path in (PKG / "csrc").glob("*"):
-        assert qualifier not in path.read_text(), path
