@@ -26,6 +26,8 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -400,6 +402,224 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------- CTA-pair variant
+// Cluster of two CTAs per 256 x BN output tile (cta_group::2). CTA r of the pair loads rows
+// m0 + 128 r .. +127 of A and rows n0 + (BN/2) r .. of B into its own shared memory; both sets of
+// loads complete on the even CTA's full barrier, whose producer announces the bytes of both. The
+// even CTA's MMA warp issues M=256 MMAs that read A and B from both CTAs and write each CTA's 128
+// accumulator rows into that CTA's TMEM; its commits arrive on the empty / accumulator-full
+// barriers of both CTAs. Both CTAs' epilogue warps release an accumulator on the even CTA's
+// accumulator-empty barrier. Per CTA and K block the pair moves 16 KB of A and BN * 64 bytes of B,
+// a third less than the single-CTA kernel at BN = 256, for the same tensor work.
+template <int BN, int STAGES>
+struct PairSmem {
+  static constexpr int kBHalfBytes = (BN / 2) * kBK * 2;
+  static constexpr int kStageBytes = kATileBytes + kBHalfBytes;
+  static constexpr int kBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ TileCoord pair_tile_coord(const GemmParams& p, int tile, int bn, int num_k) {
+  const int mn = tile % (p.num_m_tiles * p.num_n_tiles);
+  const int split = tile / (p.num_m_tiles * p.num_n_tiles);
+  TileCoord c;
+  c.m0 = (mn % p.num_m_tiles) * 256;
+  c.n0 = (mn / p.num_m_tiles) * bn;
+  c.kb_begin = split * p.k_blocks_per_split;
+  c.kb_end = min(num_k, c.kb_begin + p.k_blocks_per_split);
+  return c;
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const GemmParams p) {
+  using L = PairSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * kATileBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;      // [2]
+  uint64_t* drain_bar = tempty_bar + 2;      // [1]
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x / 2;
+  const int num_pairs = gridDim.x / 2;
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);   // the even CTA's producer; bytes of both CTAs
+      mbar_init(&empty_bar[s], 1);  // one commit from the even CTA's MMA warp
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 16);  // 8 epilogue warps x 2 CTAs (even CTA only)
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM of both allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+  const int num_k = (p.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs, own half of A and B)
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      constexpr uint32_t kTxPair = 2 * (kATileBytes + L::kBHalfBytes);
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+        const TileCoord tc = pair_tile_coord(p, tile, BN, num_k);
+        const int m0 = tc.m0 + 128 * (int)rank;
+        const int n0 = tc.n0 + (BN / 2) * (int)rank;
+        for (int kb = tc.kb_begin; kb < tc.kb_end; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          const int k0 = kb * kBK;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], kTxPair);
+          uint8_t* a_dst = smA + stage * kATileBytes;
+          uint8_t* b_dst = smB + stage * L::kBHalfBytes;
+          if (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, &full_bar[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(a_dst + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, &full_bar[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d_pair(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok && leader) {
+        int s = stage, ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(&full_bar[s], ph, nullptr, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (even CTA only)
+      constexpr uint32_t idesc = make_idesc_bf16(256, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool any_mma = false;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, kErrGemmMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        const TileCoord tc = pair_tile_coord(p, tile, BN, num_k);
+        for (int kb = tc.kb_begin; kb < tc.kb_end; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smA + stage * kATileBytes);
+          const uint32_t b_base = smem_u32(smB + stage * L::kBHalfBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t a_desc = A_MN ? make_sdesc_sw128(a_base + k * 2048, 8192, 1024)
+                                         : make_sdesc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t b_desc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
+                                         : make_sdesc_sw128(b_base + k * 32, 16, 1024);
+            tc_mma_f16_pair(d_tmem, a_desc, b_desc, idesc, (kb > tc.kb_begin || k > 0) ? 1u : 0u);
+            any_mma = true;
+          }
+          tc_commit_pair_both(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_both(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (!ok && any_mma) {
+        tc_commit_pair_both(drain_bar);
+        mbar_wait(drain_bar, 0, nullptr, nullptr, 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..9 (both CTAs, own 128 rows)
+    const int lane_group = warp % 4;
+    const int col_half = (warp - 2) / 4;
+    constexpr int kChunks = BN / 64;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < p.num_tiles; tile += num_pairs) {
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrGemmEpilogueWait)) break;
+      tc_fence_after();
+      const TileCoord tc = pair_tile_coord(p, tile, BN, num_k);
+      const int m = tc.m0 + 128 * (int)rank + lane_group * 32 + lane;
+      const int n0 = tc.n0 + col_half * (BN / 2);
+      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_half * (BN / 2);
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(t_row, r[0]);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        tmem_ld_wait_regs(r[c & 1]);
+        if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, r[(c + 1) & 1]);
+        epilogue_chunk(p, m, n0 + c * 32, r[c & 1]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(&tempty_bar[acc], 0);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer no longer reads this CTA's shared memory or signals its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------------------------------ host
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -472,6 +692,62 @@ static void dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const C
   else launch_gemm<BN, true, true, ST>(ta, tb, p, device, s);
 }
 
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, int device,
+                             cudaStream_t stream) {
+  using L = PairSmem<BN, STAGES>;
+  auto kern = gemm_tcgen05_pair_kernel<BN, A_MN, B_MN, STAGES>;
+  static bool configured[64] = {false};
+  if (!configured[device]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    configured[device] = true;
+  }
+  p.num_m_tiles = (p.M + 255) / 256;
+  p.num_n_tiles = (p.N + BN - 1) / BN;
+  const int num_k = (p.K + kBK - 1) / kBK;
+  if (p.splits < 1) p.splits = 1;
+  p.k_blocks_per_split = (num_k + p.splits - 1) / p.splits;
+  p.splits = (num_k + p.k_blocks_per_split - 1) / p.k_blocks_per_split;
+  p.num_tiles = p.num_m_tiles * p.num_n_tiles * p.splits;
+  if (p.splits > 1 && !p.accumulate)
+    C10_CUDA_CHECK(cudaMemsetAsync(p.D, 0, (size_t)p.M * p.N * sizeof(float), stream));
+  const int pairs = std::min(p.num_tiles, num_sms(device) / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+}
+
+template <int BN>
+static void dispatch_majors_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
+                                 int device, cudaStream_t s) {
+  constexpr int ST = 6;
+  if (!a_mn && !b_mn) launch_gemm_pair<BN, false, false, ST>(ta, tb, p, device, s);
+  else if (!a_mn && b_mn) launch_gemm_pair<BN, false, true, ST>(ta, tb, p, device, s);
+  else if (a_mn && !b_mn) launch_gemm_pair<BN, true, false, ST>(ta, tb, p, device, s);
+  else launch_gemm_pair<BN, true, true, ST>(ta, tb, p, device, s);
+}
+
+// 0: single-CTA tiles only; otherwise CTA pairs whenever M >= 256 (default). The environment
+// variable MIA_GEMM_PAIR sets the initial value, `set_gemm_pair_mode` changes it at run time.
+static std::atomic<int> g_pair_mode{[] {
+  const char* v = std::getenv("MIA_GEMM_PAIR");
+  return v == nullptr ? 2 : std::atoi(v);
+}()};
+
+static int pair_mode() { return g_pair_mode.load(std::memory_order_relaxed); }
+
+int64_t set_gemm_pair_mode(int64_t mode) { return g_pair_mode.exchange((int)mode); }
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Picks the N tile: 256 unless 128 gives noticeably better wave quantisation over the SMs.
@@ -482,6 +758,18 @@ static int choose_bn(int M, int N, int sms) {
     const long waves = (tiles + sms - 1) / sms;
     const double useful = (double)M * N;
     return useful / ((double)waves * sms * kBM * bn);
+  };
+  return eff(256) >= 0.85 * eff(128) ? 256 : 128;
+}
+
+// Same rule for 256 x BN tiles over CTA pairs.
+static int choose_bn_pair(int M, int N, int sms) {
+  if (N <= 128) return 128;
+  const int pairs = sms / 2;
+  auto eff = [&](int bn) {
+    const long tiles = (long)((M + 255) / 256) * ((N + bn - 1) / bn);
+    const long waves = (tiles + pairs - 1) / pairs;
+    return (double)M * N / ((double)waves * pairs * 256 * bn);
   };
   return eff(256) >= 0.85 * eff(128) ? 256 : 128;
 }
@@ -537,24 +825,34 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   p.aux_out = check_mat(aux_out, "aux_out");
   TORCH_CHECK(act != kActDGelu || p.aux != nullptr, "gemm: GELU' needs aux");
 
-  const int bn = choose_bn((int)M, (int)N, num_sms(device));
+  const bool use_pair = pair_mode() != 0 && M >= 256;
+  const int bn = use_pair ? choose_bn_pair((int)M, (int)N, num_sms(device)) : choose_bn((int)M, (int)N, num_sms(device));
   // Split K when the output alone cannot fill the SMs and nothing in the epilogue needs the full
   // sum (the weight-gradient GEMMs: tokens are K, the output is a small fp32 matrix).
   p.splits = 1;
   const bool plain_fp32 = p.d_fp32 && !p.bias && !p.gamma && !p.residual && !p.aux && !p.aux_out && act == kActNone;
   if (plain_fp32) {
-    const long tiles = (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
-    const int sms = num_sms(device);
+    const long tiles = use_pair ? (long)((M + 255) / 256) * ((N + bn - 1) / bn)
+                                : (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+    const int sms = use_pair ? num_sms(device) / 2 : num_sms(device);
     const int k_blocks = (int)((K + kBK - 1) / kBK);
     if (2 * tiles <= sms) p.splits = (int)std::max(1L, std::min<long>(k_blocks / 4, sms / tiles));
   }
-  // A tile: 128 rows x 64 K (K-major) or 64 M x 64 K per box, twice (M-major).
+  // A tile: 128 rows x 64 K (K-major) or 64 M x 64 K per box, twice (M-major). B: BN rows (BN / 2
+  // per CTA of a pair) x 64 K, or 64 N x 64 K boxes.
+  const int b_rows = use_pair ? bn / 2 : bn;
   CUtensorMap ta = a_kmajor ? make_map(a.data_ptr(), K, M, a.stride(0), 64, kBM)
                             : make_map(a.data_ptr(), M, K, a.stride(0), 64, 64);
-  CUtensorMap tb = b_kmajor ? make_map(b.data_ptr(), K, N, b.stride(0), 64, bn)
+  CUtensorMap tb = b_kmajor ? make_map(b.data_ptr(), K, N, b.stride(0), 64, b_rows)
                             : make_map(b.data_ptr(), N, K, b.stride(0), 64, 64);
-  if (bn == 256) dispatch_majors<256>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
-  else dispatch_majors<128>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+  if (use_pair) {
+    if (bn == 256) dispatch_majors_pair<256>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+    else dispatch_majors_pair<128>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+  } else if (bn == 256) {
+    dispatch_majors<256>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+  } else {
+    dispatch_majors<128>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+  }
 }
 
 // -------------------------------------------------------------- column sums (bias gradients)

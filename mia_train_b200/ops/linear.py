@@ -49,6 +49,11 @@ def gelu_grad_reference(h: torch.Tensor) -> torch.Tensor:
     return cdf + h * pdf
 
 
+# When a list, every `gemm` call appends (M, N, K, layout, out dtype, act, accumulate, residual): the
+# per-shape profile in ops/microbench.py pairs these with the kernels' device times.
+GEMM_TRACE: list | None = None
+
+
 def gemm(
     a: torch.Tensor,
     b: torch.Tensor,
@@ -74,6 +79,11 @@ def gemm(
     """
     m = a.shape[0] if a_kmajor else a.shape[1]
     n = b.shape[0] if b_kmajor else b.shape[1]
+    if GEMM_TRACE is not None:
+        k = a.shape[1] if a_kmajor else a.shape[0]
+        GEMM_TRACE.append((m, n, k, ("n" if a_kmajor else "t") + ("n" if b_kmajor else "t"),
+                           "f32" if (out is not None and out.dtype == torch.float32) or out_dtype == torch.float32 else "bf16",
+                           act, accumulate, residual is not None))
     if out is None:
         out = torch.empty((m, n), device=a.device, dtype=out_dtype)
     if use_native(a):

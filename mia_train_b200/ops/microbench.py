@@ -3,6 +3,7 @@
     python -m mia_train_b200.ops.microbench gemm --m 2048 --n 4096 --k 1024 [--layout nt|nn|tn|tt]
     python -m mia_train_b200.ops.microbench mae-step-gemms
     python -m mia_train_b200.ops.microbench attention --b 16 --h 16 --n 512 --d 32
+    python -m mia_train_b200.ops.microbench step-gemms [--depth 24]   # device time of every GEMM of a real step
 
 Times are CUDA-event averages after warm-up, with a synchronize on both sides. Layout letters
 give A then B: `n` = K-major ("normal" for D = A B^T), `t` = the transposed (M- or N-major) read.
@@ -88,6 +89,59 @@ def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20) -> dict:
             "bwd_tflops": 2.5 * flops / bwd_us / 1e6, "sdpa_fwd_us": sdpa_us}
 
 
+def step_gemms(depth: int = 24, batch: int = 16) -> str:
+    """Device time of each GEMM launched by one eager ViT-L MAE training step, grouped by shape."""
+    from collections import defaultdict
+
+    from torch.profiler import ProfilerActivity, profile
+
+    from ..algorithms.mae import MAE
+    from ..models.vit import ViT3D
+    from . import linear
+
+    dev = torch.device("cuda")
+    torch.manual_seed(0)
+    model = ViT3D(img_size=(128,) * 3, patch_size=(16,) * 3, embed_dim=1024, depth=depth, num_heads=16, mlp_ratio=4.0)
+    alg = MAE(model, input_axes="lcxyz", mask_ratio=0.75, decoder_embed_dim=512, decoder_depth=8,
+              decoder_num_heads=16).to(dev)
+    x = torch.randn(batch, 1, 1, 128, 128, 128, device=dev)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = alg({"img": x})
+        out["loss"].backward()
+        alg.zero_grad(set_to_none=True)
+
+    step()
+    torch.cuda.synchronize()
+    linear.GEMM_TRACE = []
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    trace, linear.GEMM_TRACE = linear.GEMM_TRACE, None
+    kernels = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA
+                      and "gemm_tcgen05" in e.name), key=lambda e: e.time_range.start)
+    if len(kernels) != len(trace):
+        return f"unmatched: {len(kernels)} GEMM kernels vs {len(trace)} calls"
+    agg: dict[tuple, list[float]] = defaultdict(lambda: [0.0, 0, 0.0])
+    for call, kern in zip(trace, kernels, strict=True):
+        us = kern.device_time_total
+        m, n, k = call[:3]
+        key = (*call, "pair" if "pair" in kern.name else "single", kern.name.split("<")[1].split(",")[0])
+        agg[key][0] += us
+        agg[key][1] += 1
+        agg[key][2] += 2.0 * m * n * k
+    total = sum(v[0] for v in agg.values())
+    flops = sum(v[2] for v in agg.values())
+    lines = [f"GEMMs of one step: {total / 1000:.3f} ms device time, {flops / 1e12:.3f} TFLOP, "
+             f"{flops / total / 1e6:.1f} TF/s average"]
+    for key, (us, cnt, f) in sorted(agg.items(), key=lambda kv: -kv[1][0]):
+        m, n, k, layout, dt, act, accum, res, kind, bn = key
+        lines.append(f"  {m:6d} {n:6d} {k:6d} {layout} {dt:4s} act={act} acc={int(accum)} res={int(res)} {kind:6s} BN={bn:3s}"
+                     f"  x{cnt:3d}  {us / cnt:8.1f} us  {f / us / 1e6:7.1f} TF/s  ({100 * us / total:4.1f}%)")
+    return "\n".join(lines)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(prog="python -m mia_train_b200.ops.microbench")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -101,23 +155,41 @@ def main() -> None:
     s = sub.add_parser("mae-step-gemms")
     s.add_argument("--batch", type=int, default=16)
     s.add_argument("--iters", type=int, default=20)
+    s.add_argument("--pair-modes", default="0,2",
+                   help="GEMM tile modes to compare (0 = single-CTA tiles, 2 = CTA pairs when M >= 256)")
+    sg = sub.add_parser("step-gemms")
+    sg.add_argument("--depth", type=int, default=24)
+    sg.add_argument("--batch", type=int, default=16)
     at = sub.add_parser("attention")
     for name, default in (("b", 16), ("h", 16), ("n", 512), ("d", 32), ("iters", 20)):
         at.add_argument(f"--{name}", type=int, default=default)
     args = ap.parse_args()
+    if args.cmd == "step-gemms":
+        print(step_gemms(args.depth, args.batch))
+        return
     if args.cmd == "gemm":
         print(bench_gemm(args.m, args.n, args.k, args.layout, args.iters, args.fp32_out))
     elif args.cmd == "attention":
         print(bench_attention(args.b, args.h, args.n, args.d, args.iters))
     else:
-        tot, tot_cb = 0.0, 0.0
+        from . import _native
+
+        modes = [int(x) for x in args.pair_modes.split(",")]
+        totals = dict.fromkeys(modes, 0.0)
+        tot_cb = 0.0
         for name, m, n, k, layout, fp32 in mae_step_gemms(args.batch):
-            r = bench_gemm(m, n, k, layout, args.iters, fp32)
-            tot += r["us"]
+            cols = []
+            for mode in modes:
+                previous = _native.native().set_gemm_pair_mode(mode)
+                r = bench_gemm(m, n, k, layout, args.iters, fp32)
+                _native.native().set_gemm_pair_mode(previous)
+                totals[mode] += r["us"]
+                cols.append(f"mode{mode} {r['us']:7.1f} us {r['tflops']:6.1f} TF/s")
             tot_cb += r["cublas_us"]
-            print(f"{name:18s} {m:6d} {n:6d} {k:6d} {layout}  native {r['us']:8.1f} us {r['tflops']:7.1f} TF/s"
-                  f"   cuBLAS {r['cublas_us']:8.1f} us {r['cublas_tflops']:7.1f} TF/s")
-        print(f"total one encoder+decoder block set: native {tot:.1f} us, cuBLAS {tot_cb:.1f} us")
+            print(f"{name:18s} {m:6d} {n:6d} {k:6d} {layout}  " + "  ".join(cols)
+                  + f"   cuBLAS {r['cublas_us']:7.1f} us {r['cublas_tflops']:6.1f} TF/s")
+        print("total one encoder+decoder block set: " + ", ".join(f"mode{m} {t:.1f} us" for m, t in totals.items())
+              + f", cuBLAS {tot_cb:.1f} us")
 
 
 if __name__ == "__main__":

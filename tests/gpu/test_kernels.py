@@ -35,9 +35,19 @@ def _close(actual, expected, rel=2e-2, atol=2e-2):
     assert err <= atol + rel * scale, f"max error {err:.4g} vs scale {scale:.4g}"
 
 
+@pytest.fixture(params=[0, 2], ids=["single_cta", "cta_pairs"])
+def pair_mode(request):
+    from mia_train_b200.ops._native import native
+
+    previous = native().set_gemm_pair_mode(request.param)
+    yield request.param
+    native().set_gemm_pair_mode(previous)
+
+
 @pytest.mark.parametrize("a_k,b_k", [(True, True), (True, False), (False, True), (False, False)])
-@pytest.mark.parametrize("mnk", [(256, 256, 128), (384, 648, 200), (128, 136, 64), (2048, 3072, 1024), (1000, 512, 4096)])
-def test_gemm_layouts(a_k, b_k, mnk):
+@pytest.mark.parametrize("mnk", [(256, 256, 128), (384, 648, 200), (128, 136, 64), (2048, 3072, 1024), (1000, 512, 4096),
+                                 (640, 200, 64)])
+def test_gemm_layouts(a_k, b_k, mnk, pair_mode):
     m, n, k = mnk
     torch.manual_seed(0)
     a = torch.randn(m, k, device=DEV).bfloat16()
@@ -50,7 +60,7 @@ def test_gemm_layouts(a_k, b_k, mnk):
     _no_errors()
 
 
-def test_gemm_epilogues():
+def test_gemm_epilogues(pair_mode):
     torch.manual_seed(1)
     m, n, k = 512, 768, 320
     a = torch.randn(m, k, device=DEV).bfloat16()
@@ -269,7 +279,7 @@ def test_mae_step_native_vs_reference_math():
 
 
 @pytest.mark.parametrize("mnk", [(512, 512, 8192), (1536, 512, 8192), (1024, 1024, 2048)])
-def test_gemm_split_k_weight_gradient(mnk):
+def test_gemm_split_k_weight_gradient(mnk, pair_mode):
     """dW-shaped GEMMs (small output, long K, fp32 accumulate) take the split-K path."""
     m, n, k = mnk
     torch.manual_seed(9)
