@@ -1,7 +1,7 @@
 // Non-causal multi-head attention, forward and backward, plus the RoPE split/merge around it.
 //
-// Layouts: q, k, v, dq, dk, dv are (B, H, N, D) bf16; the output o and its gradient do are
-// (B, N, H, D) so the output projection reads them as (B*N, H*D) without a transpose.
+// Layouts: q, k, v, dq, dk, dv are strided (B, H, N, D) views with contiguous D rows; the output
+// o and its gradient do are (B, N, H, D) so the output projection reads them as (B*N, H*D).
 //
 // Forward (flash-style, one CTA per 64 queries of one (b, h), 4 warps x 16 query rows): K/V
 // blocks of 64 keys stream through double-buffered shared memory (cp.async), S = Q K^T and
@@ -12,12 +12,14 @@
 // recomputes P^T from lse, accumulates dV and dK in registers, and adds dQ = dS K into an fp32
 // buffer with one atomic per element per CTA. `delta = rowsum(dO * O)` is a separate pass.
 //
-// RoPE: `rope_split_fwd` reads the fused projection (B, N, 3, H, D), rotates channel pairs of q
-// and k by per-token angles, and writes q, k, v in (B, H, N, D); `rope_split_bwd` un-rotates dq, dk
-// back into the packed gradient and reduces d(angle) per token.
+// The kernels take (batch, head, row) element strides, so they read q / k / v straight out of the
+// packed projection (B, N, 3, H, D) or the rotated buffer (B, N, 2, H, D) as well as from
+// contiguous (B, H, N, D) tensors. RoPE kernels: see the section below.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+
+#include <utility>
 
 #include "common.cuh"
 
@@ -50,6 +52,18 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
                : "r"(smem_u32(p)));
 }
 
+// Element strides of a (B, H, N, D) view whose rows of D are contiguous.
+struct Strides3 {
+  int64_t b, h, n;
+};
+
+// 2^x with the hardware approximation (relative error ~2^-22, flushes denormals), for softmax terms.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // C(16x8 fp32) += A(16x16 bf16, row) * B(16x8 bf16, col)
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -61,7 +75,7 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 
 // Loads `rows` x D bf16 rows (row stride `ld` elements in global) into padded shared memory.
 template <int D>
-__device__ __forceinline__ void load_rows_async(bf16* smem, const bf16* g, int ld, int row0, int rows, int nvalid) {
+__device__ __forceinline__ void load_rows_async(bf16* smem, const bf16* g, int64_t ld, int row0, int rows, int nvalid) {
   constexpr int kChunks = D / 8;
   constexpr int kStride = D + 8;
   for (int i = threadIdx.x; i < rows * kChunks; i += blockDim.x) {
@@ -76,7 +90,7 @@ template <int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                                 const bf16* __restrict__ v, bf16* __restrict__ o,
                                                                 float* __restrict__ lse, int H, int Nq, int Nk,
-                                                                float scale_log2) {
+                                                                float scale_log2, Strides3 qs, Strides3 ks, Strides3 vs) {
   constexpr int S = D + 8;  // padded row stride (elements)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   bf16* Qs = reinterpret_cast<bf16*>(smem_raw);
@@ -85,15 +99,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const bf16* __re
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
   const int q0 = blockIdx.x * kAttnBlockM;
-  const bf16* qg = q + (size_t)bh * Nq * D;
-  const bf16* kg = k + (size_t)bh * Nk * D;
-  const bf16* vg = v + (size_t)bh * Nk * D;
+  const bf16* qg = q + b * qs.b + h * qs.h;
+  const bf16* kg = k + b * ks.b + h * ks.h;
+  const bf16* vg = v + b * vs.b + h * vs.h;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int g = lane / 4, t = lane % 4;
 
-  load_rows_async<D>(Qs, qg, D, q0, kAttnBlockM, Nq);
-  load_rows_async<D>(Ks, kg, D, 0, kAttnBlockN, Nk);
-  load_rows_async<D>(Vs, vg, D, 0, kAttnBlockN, Nk);
+  load_rows_async<D>(Qs, qg, qs.n, q0, kAttnBlockM, Nq);
+  load_rows_async<D>(Ks, kg, ks.n, 0, kAttnBlockN, Nk);
+  load_rows_async<D>(Vs, vg, vs.n, 0, kAttnBlockN, Nk);
   cp_async_commit();
 
   uint32_t qf[D / 16][4];
@@ -106,8 +120,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const bf16* __re
   for (int j = 0; j < n_blocks; ++j) {
     const int buf = j & 1;
     if (j + 1 < n_blocks) {
-      load_rows_async<D>(Ks + (buf ^ 1) * kAttnBlockN * S, kg, D, (j + 1) * kAttnBlockN, kAttnBlockN, Nk);
-      load_rows_async<D>(Vs + (buf ^ 1) * kAttnBlockN * S, vg, D, (j + 1) * kAttnBlockN, kAttnBlockN, Nk);
+      load_rows_async<D>(Ks + (buf ^ 1) * kAttnBlockN * S, kg, ks.n, (j + 1) * kAttnBlockN, kAttnBlockN, Nk);
+      load_rows_async<D>(Vs + (buf ^ 1) * kAttnBlockN * S, vg, vs.n, (j + 1) * kAttnBlockN, kAttnBlockN, Nk);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -159,7 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const bf16* __re
       mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
       mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
       const float m_new = fmaxf(m_run[r], mx[r]);
-      corr[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
+      corr[r] = (m_run[r] == -INFINITY) ? 0.f : fast_exp2(m_run[r] - m_new);
       m_run[r] = m_new;
     }
     float rs[2] = {0.f, 0.f};
@@ -168,7 +182,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const bf16* __re
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float mr = m_run[e >> 1];
-        const float p = (s[nt][e] == -INFINITY) ? 0.f : exp2f(s[nt][e] - mr);
+        const float p = (s[nt][e] == -INFINITY) ? 0.f : fast_exp2(s[nt][e] - mr);
         s[nt][e] = p;
         rs[e >> 1] += p;
       }
@@ -248,7 +262,8 @@ template <int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v, const bf16* __restrict__ dout,
     const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq_acc, bf16* __restrict__ dk,
-    bf16* __restrict__ dv, int H, int Nq, int Nk, float scale, float scale_log2) {
+    bf16* __restrict__ dv, int H, int Nq, int Nk, float scale, float scale_log2, Strides3 qs, Strides3 ks, Strides3 vs,
+    Strides3 dqs, Strides3 dks, Strides3 dvs) {
   constexpr int S = D + 8;
   constexpr int SP = kAttnBlockM + 8;  // dS^T row stride
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -265,13 +280,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(
   const int k0 = blockIdx.x * kAttnBlockN;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int g = lane / 4, t = lane % 4;
-  const bf16* qg = q + (size_t)bh * Nq * D;
-  const bf16* kg = k + (size_t)bh * Nk * D;
-  const bf16* vg = v + (size_t)bh * Nk * D;
+  const bf16* qg = q + b * qs.b + h * qs.h;
+  const bf16* kg = k + b * ks.b + h * ks.h;
+  const bf16* vg = v + b * vs.b + h * vs.h;
   const bf16* dog = dout + ((size_t)b * Nq * H + h) * D;  // row stride H*D
 
-  load_rows_async<D>(Ks, kg, D, k0, kAttnBlockN, Nk);
-  load_rows_async<D>(Vs, vg, D, k0, kAttnBlockN, Nk);
+  load_rows_async<D>(Ks, kg, ks.n, k0, kAttnBlockN, Nk);
+  load_rows_async<D>(Vs, vg, vs.n, k0, kAttnBlockN, Nk);
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
@@ -294,8 +309,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(
   const int n_qblocks = (Nq + kAttnBlockM - 1) / kAttnBlockM;
   for (int qb = 0; qb < n_qblocks; ++qb) {
     const int q0 = qb * kAttnBlockM;
-    load_rows_async<D>(Qs, qg, D, q0, kAttnBlockM, Nq);
-    load_rows_async<D>(dOs, dog, H * D, q0, kAttnBlockM, Nq);
+    load_rows_async<D>(Qs, qg, qs.n, q0, kAttnBlockM, Nq);
+    load_rows_async<D>(dOs, dog, (int64_t)H * D, q0, kAttnBlockM, Nq);
     cp_async_commit();
     for (int i = threadIdx.x; i < kAttnBlockM; i += blockDim.x) {
       const int qi = q0 + i;
@@ -329,7 +344,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(
         const int qi_local = nt * 8 + 2 * t + (e & 1);
         const int key = my_key0 + g + 8 * (e >> 1);
         const bool valid = (q0 + qi_local < Nq) && (key < Nk);
-        st[nt][e] = valid ? exp2f(st[nt][e] * scale_log2 - lse_s[qi_local]) : 0.f;
+        st[nt][e] = valid ? fast_exp2(st[nt][e] * scale_log2 - lse_s[qi_local]) : 0.f;
       }
     }
     // dV += P^T dO
@@ -426,12 +441,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(
     for (int r = 0; r < 2; ++r) {
       const int qi = q0 + warp * 16 + g + 8 * r;
       if (qi >= Nq) continue;
-      float* dst = dq_acc + ((size_t)bh * Nq + qi) * D;
+      float* dst = dq_acc + b * dqs.b + h * dqs.h + qi * dqs.n;
 #pragma unroll
-      for (int dt = 0; dt < D / 8; ++dt) {
-        atomicAdd(dst + dt * 8 + 2 * t, dq[dt][2 * r] * scale);
-        atomicAdd(dst + dt * 8 + 2 * t + 1, dq[dt][2 * r + 1] * scale);
-      }
+      for (int dt = 0; dt < D / 8; ++dt)
+        atomicAdd(reinterpret_cast<float2*>(dst + dt * 8 + 2 * t), make_float2(dq[dt][2 * r] * scale, dq[dt][2 * r + 1] * scale));
     }
     __syncthreads();
   }
@@ -439,8 +452,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(
   for (int r = 0; r < 2; ++r) {
     const int key = my_key0 + g + 8 * r;
     if (key >= Nk) continue;
-    bf16* dkr = dk + ((size_t)bh * Nk + key) * D;
-    bf16* dvr = dv + ((size_t)bh * Nk + key) * D;
+    bf16* dkr = dk + b * dks.b + h * dks.h + key * dks.n;
+    bf16* dvr = dv + b * dvs.b + h * dvs.h + key * dvs.n;
 #pragma unroll
     for (int dt = 0; dt < D / 8; ++dt) {
       *reinterpret_cast<uint32_t*>(dkr + dt * 8 + 2 * t) =
@@ -461,146 +474,158 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restri
 }
 
 // ------------------------------------------------------------------------------------ RoPE
-// One CTA per token (b, n). The token's packed projection (3*H*D bf16) is staged in shared memory
-// with 16-byte loads; per-element rotation roles are built once per CTA from the pair list, and
-// cos/sin of the token's P angles are computed once and shared by every head of q and k.
-struct RopeRoles {
+// Token-major RoPE around the attention kernels. The fused projection qkv (B, N, 3, H, D) is never
+// split: v is read in place, q and k are rotated into qk (B, N, 2, H, D) by `rope_qk_fwd_kernel`,
+// and the attention kernels take strided (B, N, H, D) views. One warp per (token, q|k): the warp
+// stages the token's H*D channels in shared memory with 16-byte loads, computes cos/sin of the
+// token's P angles once, builds the channel -> (partner, pair, sign) table from `pairs`, then writes
+// rotated 16-byte chunks, so every global access is contiguous.
+//
+// Backward (`rope_qk_bwd_kernel`): the attention backward leaves dq (fp32, token-major) and the
+// rotated-space dk in the dqkv slot; the warp un-rotates both into dqkv (B, N, 3, H, D) and the two
+// warps of a token sum d(angle_p) = sum_heads (g2 y1 - g1 y2) over q and k in shared memory, so the
+// token's angle gradient is written once, without atomics.
+constexpr int kRopeTokensPerCta = 4;  // warps = 2 * tokens
+
+struct RopeRole {
   int16_t partner;  // -1: channel not rotated
   int16_t pair;
-  int8_t second;    // 0: first channel of its pair, 1: second
+  float sign;       // -1 for the first channel of its pair, +1 for the second
 };
 
-__device__ __forceinline__ void rope_build_roles(RopeRoles* roles, const int* __restrict__ pairs, int P, int D,
-                                                 float* cs, float* sn, const float* ang) {
-  for (int d = threadIdx.x; d < D; d += blockDim.x) roles[d] = RopeRoles{-1, 0, 0};
-  __syncthreads();
-  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+__device__ __forceinline__ void rope_roles_warp(RopeRole* roles, const int* __restrict__ pairs, int P, int D,
+                                                float* cs, float* sn, const float* ang) {
+  const int lane = threadIdx.x % 32;
+  for (int d = lane; d < D; d += 32) roles[d] = RopeRole{-1, 0, 0.f};
+  __syncwarp();
+  for (int p = lane; p < P; p += 32) {
     const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
-    roles[i1] = RopeRoles{(int16_t)i2, (int16_t)p, 0};
-    roles[i2] = RopeRoles{(int16_t)i1, (int16_t)p, 1};
-    float a = ang != nullptr ? ang[p] : 0.f;
+    roles[i1] = RopeRole{(int16_t)i2, (int16_t)p, -1.f};
+    roles[i2] = RopeRole{(int16_t)i1, (int16_t)p, 1.f};
+    const float a = ang != nullptr ? ang[p] : 0.f;
     sincosf(a, &sn[p], &cs[p]);
   }
-  __syncthreads();
+  __syncwarp();
 }
 
-// qkv (B, N, 3, H, D) -> q, k, v (B, H, N, D); pairs (P, 2) int32; angles (B or 1, N, P) fp32.
-__global__ void rope_split_fwd_kernel(const bf16* __restrict__ qkv, const float* __restrict__ angles,
-                                      const int* __restrict__ pairs, int P, int angle_bstride, bf16* __restrict__ q,
-                                      bf16* __restrict__ k, bf16* __restrict__ v, int N, int H, int D) {
+// qkv (B, N, 3, H, D) -> qk (B, N, 2, H, D); angles (B or 1, N, P) fp32.
+__global__ void rope_qk_fwd_kernel(const bf16* __restrict__ qkv, const float* __restrict__ angles,
+                                   const int* __restrict__ pairs, int P, int64_t angle_bstride, bf16* __restrict__ qk,
+                                   int BN, int N, int H, int D) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int HD = H * D;
-  bf16* xs = reinterpret_cast<bf16*>(smem_raw);                          // [3 * HD]
-  float* cs = reinterpret_cast<float*>(smem_raw + 3 * HD * 2);           // [P]
-  float* sn = cs + P;                                                    // [P]
-  RopeRoles* roles = reinterpret_cast<RopeRoles*>(sn + P);               // [D]
-  const int token = blockIdx.x;  // b * N + n
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int slot = warp;  // (token in CTA) * 2 + which
+  const size_t per_warp = (size_t)HD * 2 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16;
+  uint8_t* base = smem_raw + slot * ((per_warp + 15) / 16 * 16);
+  bf16* xs = reinterpret_cast<bf16*>(base);
+  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 2);
+  float* sn = cs + P;
+  RopeRole* roles = reinterpret_cast<RopeRole*>(sn + P);
+  const int token = blockIdx.x * kRopeTokensPerCta + warp / 2;
+  const int which = warp % 2;
+  if (token >= BN) return;
   const int b = token / N, n = token % N;
-  const uint4* src = reinterpret_cast<const uint4*>(qkv + (size_t)token * 3 * HD);
-  for (int c = threadIdx.x; c < 3 * HD / 8; c += blockDim.x) reinterpret_cast<uint4*>(xs)[c] = src[c];
-  const float* ang = (angles != nullptr && P > 0) ? angles + (size_t)b * angle_bstride + (size_t)n * P : nullptr;
-  rope_build_roles(roles, pairs, P, D, cs, sn, ang);
-  const int chunks_per_head = D / 8;
-  for (int c = threadIdx.x; c < 3 * HD / 8; c += blockDim.x) {
-    const int which = c / (HD / 8);
-    const int rem = c % (HD / 8);
-    const int h = rem / chunks_per_head;
-    const int d0 = (rem % chunks_per_head) * 8;
-    const bf16* x = xs + which * HD + h * D;
+  const uint4* src = reinterpret_cast<const uint4*>(qkv + ((size_t)token * 3 + which) * HD);
+  for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(xs)[c] = src[c];
+  const float* ang = angles + (size_t)b * angle_bstride + (size_t)n * P;
+  rope_roles_warp(roles, pairs, P, D, cs, sn, ang);
+  uint4* dst = reinterpret_cast<uint4*>(qk + ((size_t)token * 2 + which) * HD);
+  for (int c = lane; c < HD / 8; c += 32) {
+    const int h = (c * 8) / D, d0 = (c * 8) % D;
+    const bf16* x = xs + h * D;
     float o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int d = d0 + j;
       const float xi = __bfloat162float(x[d]);
-      const RopeRoles r = roles[d];
-      if (which < 2 && r.partner >= 0 && ang != nullptr) {
-        const float xp = __bfloat162float(x[r.partner]);
-        o[j] = r.second ? xi * cs[r.pair] + xp * sn[r.pair] : xi * cs[r.pair] - xp * sn[r.pair];
-      } else {
-        o[j] = xi;
-      }
+      const RopeRole r = roles[d];
+      o[j] = r.partner >= 0 ? xi * cs[r.pair] + r.sign * __bfloat162float(x[r.partner]) * sn[r.pair] : xi;
     }
-    bf16* dst = (which == 0 ? q : which == 1 ? k : v) + (((size_t)b * H + h) * N + n) * D + d0;
-    *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+    dst[c] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                        pack_bf16x2(o[6], o[7]));
   }
 }
 
-// Backward: dqkv (B, N, 3, H, D) from dq (fp32), dk, dv (B, H, N, D); dangles (B, N, P): the CTA
-// owns its token, so d(theta_p) = sum over heads and over q, k of (g2 * y1 - g1 * y2) is written
-// without atomics (y is the rotated value the attention saw, g its gradient).
-__global__ void rope_split_bwd_kernel(const float* __restrict__ dq, const bf16* __restrict__ dk,
-                                      const bf16* __restrict__ dv, const bf16* __restrict__ qr,
-                                      const bf16* __restrict__ kr, const float* __restrict__ angles,
-                                      const int* __restrict__ pairs, int P, int angle_bstride, bf16* __restrict__ dqkv,
-                                      float* __restrict__ dangles, int N, int H, int D) {
+// dq_acc (B, N, H, D) fp32; dqkv (B, N, 3, H, D) with the rotated-space dk in slot 1 and dv in
+// slot 2; y = the rotated q/k the attention saw (`qk`, or qkv itself when P == 0).
+__global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16* __restrict__ y, int64_t y_token_stride,
+                                   const float* __restrict__ angles, const int* __restrict__ pairs, int P,
+                                   int64_t angle_bstride, bf16* __restrict__ dqkv, float* __restrict__ dangles, int BN,
+                                   int N, int H, int D) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int HD = H * D;
-  float* gq = reinterpret_cast<float*>(smem_raw);                 // [HD]
-  float* gk = gq + HD;                                            // [HD]
-  float* yq = gk + HD;                                            // [HD]
-  float* yk = yq + HD;                                            // [HD]
-  float* cs = yk + HD;                                            // [P]
-  float* sn = cs + P;                                             // [P]
-  RopeRoles* roles = reinterpret_cast<RopeRoles*>(sn + P);        // [D]
-  const int token = blockIdx.x;
-  const int b = token / N, n = token % N;
-  const float* ang = (angles != nullptr && P > 0) ? angles + (size_t)b * angle_bstride + (size_t)n * P : nullptr;
-  for (int c = threadIdx.x; c < HD / 8; c += blockDim.x) {
-    const int h = c / (D / 8), d0 = (c % (D / 8)) * 8;
-    const size_t off = (((size_t)b * H + h) * N + n) * D + d0;
-    const float4 a = *reinterpret_cast<const float4*>(dq + off);
-    const float4 a2 = *reinterpret_cast<const float4*>(dq + off + 4);
-    float* gqd = gq + h * D + d0;
-    gqd[0] = a.x; gqd[1] = a.y; gqd[2] = a.z; gqd[3] = a.w; gqd[4] = a2.x; gqd[5] = a2.y; gqd[6] = a2.z; gqd[7] = a2.w;
-    const uint4 ukv = *reinterpret_cast<const uint4*>(dk + off);
-    const uint4 uq = *reinterpret_cast<const uint4*>(qr + off);
-    const uint4 uk = *reinterpret_cast<const uint4*>(kr + off);
-    const uint32_t w1[4] = {ukv.x, ukv.y, ukv.z, ukv.w}, w2[4] = {uq.x, uq.y, uq.z, uq.w}, w3[4] = {uk.x, uk.y, uk.z, uk.w};
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const size_t per_warp = (size_t)HD * 4 + (size_t)HD * 2 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16;
+  uint8_t* base = smem_raw + warp * ((per_warp + 15) / 16 * 16);
+  float* gs = reinterpret_cast<float*>(base);
+  bf16* ys = reinterpret_cast<bf16*>(base + (size_t)HD * 4);
+  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 6);
+  float* sn = cs + P;
+  float* dpart = sn + P;
+  RopeRole* roles = reinterpret_cast<RopeRole*>(dpart + P);
+  const int token = blockIdx.x * kRopeTokensPerCta + warp / 2;
+  const int which = warp % 2;
+  const bool active = token < BN;
+  const int b = active ? token / N : 0, n = active ? token % N : 0;
+  bf16* dst = dqkv + ((size_t)token * 3 + which) * HD;
+  if (active && !(P == 0 && which == 1)) {  // without RoPE the dk slot is already final
+    if (which == 0) {
+      const float4* g4 = reinterpret_cast<const float4*>(dq_acc + (size_t)token * HD);
+      for (int c = lane; c < HD / 4; c += 32) reinterpret_cast<float4*>(gs)[c] = g4[c];
+    } else {
+      const uint4* g8 = reinterpret_cast<const uint4*>(dst);
+      for (int c = lane; c < HD / 8; c += 32) {
+        const uint4 u = g8[c];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int hh = 0; hh < 4; ++hh) {
-      gk[h * D + d0 + 2 * hh] = bf16_lo(w1[hh]);
-      gk[h * D + d0 + 2 * hh + 1] = bf16_hi(w1[hh]);
-      yq[h * D + d0 + 2 * hh] = bf16_lo(w2[hh]);
-      yq[h * D + d0 + 2 * hh + 1] = bf16_hi(w2[hh]);
-      yk[h * D + d0 + 2 * hh] = bf16_lo(w3[hh]);
-      yk[h * D + d0 + 2 * hh + 1] = bf16_hi(w3[hh]);
-    }
-    // dv passes straight through
-    *reinterpret_cast<uint4*>(dqkv + (size_t)token * 3 * HD + 2 * HD + h * D + d0) =
-        *reinterpret_cast<const uint4*>(dv + off);
-  }
-  rope_build_roles(roles, pairs, P, D, cs, sn, ang);
-  for (int c = threadIdx.x; c < 2 * HD / 8; c += blockDim.x) {
-    const int which = c / (HD / 8);
-    const int rem = c % (HD / 8);
-    const int h = rem / (D / 8), d0 = (rem % (D / 8)) * 8;
-    const float* g = (which == 0 ? gq : gk) + h * D;
-    float o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = d0 + j;
-      const RopeRoles r = roles[d];
-      if (r.partner >= 0 && ang != nullptr) {
-        const float gi = g[d], gp = g[r.partner];
-        o[j] = r.second ? gi * cs[r.pair] - gp * sn[r.pair] : gi * cs[r.pair] + gp * sn[r.pair];
-      } else {
-        o[j] = g[d];
+        for (int hh = 0; hh < 4; ++hh) {
+          gs[c * 8 + 2 * hh] = bf16_lo(w[hh]);
+          gs[c * 8 + 2 * hh + 1] = bf16_hi(w[hh]);
+        }
       }
     }
-    *reinterpret_cast<uint4*>(dqkv + (size_t)token * 3 * HD + which * HD + h * D + d0) =
-        make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
-  }
-  if (dangles != nullptr && ang != nullptr) {
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
-      const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
-      float acc = 0.f;
-      for (int h = 0; h < H; ++h) {
-        acc += gq[h * D + i2] * yq[h * D + i1] - gq[h * D + i1] * yq[h * D + i2];
-        acc += gk[h * D + i2] * yk[h * D + i1] - gk[h * D + i1] * yk[h * D + i2];
-      }
-      dangles[(size_t)token * P + p] = acc;
+    if (P > 0) {
+      const uint4* y8 = reinterpret_cast<const uint4*>(y + (size_t)token * y_token_stride + (size_t)which * HD);
+      for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(ys)[c] = y8[c];
+      rope_roles_warp(roles, pairs, P, D, cs, sn, angles + (size_t)b * angle_bstride + (size_t)n * P);
+    } else {
+      __syncwarp();
     }
+    for (int c = lane; c < HD / 8; c += 32) {
+      const int h = (c * 8) / D, d0 = (c * 8) % D;
+      const float* g = gs + h * D;
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = d0 + j;
+        if (P > 0) {
+          const RopeRole r = roles[d];
+          // inverse rotation: the transpose of [[c, -s], [s, c]] acting on (first, second)
+          o[j] = r.partner >= 0 ? g[d] * cs[r.pair] - r.sign * g[r.partner] * sn[r.pair] : g[d];
+        } else {
+          o[j] = g[d];
+        }
+      }
+      reinterpret_cast<uint4*>(dst)[c] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                    pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+    }
+    if (dangles != nullptr && P > 0) {
+      for (int p = lane; p < P; p += 32) {
+        const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
+        float acc = 0.f;
+        for (int h = 0; h < H; ++h)
+          acc += gs[h * D + i2] * __bfloat162float(ys[h * D + i1]) - gs[h * D + i1] * __bfloat162float(ys[h * D + i2]);
+        dpart[p] = acc;
+      }
+    }
+  }
+  __syncthreads();
+  if (active && dangles != nullptr && P > 0 && which == 0) {
+    // partner warp (the token's k) is warp + 1, same CTA
+    const uint8_t* kbase = smem_raw + (warp + 1) * ((per_warp + 15) / 16 * 16);
+    const float* kpart = reinterpret_cast<const float*>(kbase + (size_t)HD * 6) + 2 * P;
+    for (int p = lane; p < P; p += 32) dangles[(size_t)token * P + p] = dpart[p] + kpart[p];
   }
 }
 
@@ -614,6 +639,10 @@ static constexpr float kLog2e = 1.4426950408889634f;
     if ((D_) == 128) { constexpr int HD = 128; return __VA_ARGS__(); }        \
     TORCH_CHECK(false, "attention: head_dim must be 32, 64 or 128, got ", D_); \
   }()
+
+// Strides of a (B, H, N, D) tensor and of a (B, N, H, D) view presented as (B, H, N, D).
+static Strides3 bhnd_strides(const torch::Tensor& t) { return Strides3{t.stride(0), t.stride(1), t.stride(2)}; }
+static Strides3 bnhd_strides(const torch::Tensor& t) { return Strides3{t.stride(0), t.stride(2), t.stride(1)}; }
 
 void attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse, double scale) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
@@ -632,7 +661,7 @@ void attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
     kern<<<grid, kAttnThreads, smem, stream>>>(
         reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
         reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), H,
-        Nq, Nk, (float)scale * kLog2e);
+        Nq, Nk, (float)scale * kLog2e, bhnd_strides(q), bhnd_strides(k), bhnd_strides(v));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   });
 }
@@ -663,7 +692,8 @@ static void attention_bwd_core(torch::Tensor q, torch::Tensor k, torch::Tensor v
         reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
         lse.data_ptr<float>(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
         reinterpret_cast<bf16*>(dk.data_ptr()), reinterpret_cast<bf16*>(dv.data_ptr()), H, Nq, Nk, (float)scale,
-        (float)scale * kLog2e);
+        (float)scale * kLog2e, bhnd_strides(q), bhnd_strides(k), bhnd_strides(v), bhnd_strides(dq_acc),
+        bhnd_strides(dk), bhnd_strides(dv));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   });
 }
@@ -681,60 +711,138 @@ void attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void rope_split_fwd(torch::Tensor qkv, c10::optional<torch::Tensor> angles, torch::Tensor pairs, torch::Tensor q,
-                    torch::Tensor k, torch::Tensor v) {
-  TORCH_CHECK(qkv.is_contiguous() && qkv.dim() == 5 && qkv.size(2) == 3, "rope_split_fwd: (B, N, 3, H, D) input");
+static size_t rope_fwd_smem(int H, int D, int P) {
+  const size_t per_warp = ((size_t)H * D * 2 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
+  return per_warp * 2 * kRopeTokensPerCta;
+}
+
+static size_t rope_bwd_smem(int H, int D, int P) {
+  const size_t per_warp = ((size_t)H * D * 6 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
+  return per_warp * 2 * kRopeTokensPerCta;
+}
+
+static std::pair<const float*, int64_t> rope_angles(const c10::optional<torch::Tensor>& angles, int N, int P,
+                                                     const char* who) {
+  if (!angles.has_value() || P == 0) return {nullptr, 0};
+  TORCH_CHECK(angles->scalar_type() == at::kFloat && angles->is_contiguous() && angles->dim() == 3 &&
+                  angles->size(1) == N && angles->size(2) == P,
+              who, ": angles must be contiguous fp32 (B or 1, N, P)");
+  return {angles->data_ptr<float>(), angles->size(0) == 1 ? 0 : (int64_t)N * P};
+}
+
+// qkv (B, N, 3, H, D) -> rotated q and k in qk (B, N, 2, H, D).
+void rope_qk_fwd(torch::Tensor qkv, torch::Tensor angles, torch::Tensor pairs, torch::Tensor qk) {
+  TORCH_CHECK(qkv.is_contiguous() && qkv.dim() == 5 && qkv.size(2) == 3, "rope_qk_fwd: (B, N, 3, H, D) input");
+  TORCH_CHECK(qk.is_contiguous() && qk.size(2) == 2, "rope_qk_fwd: (B, N, 2, H, D) output");
   const int B = (int)qkv.size(0), N = (int)qkv.size(1), H = (int)qkv.size(3), D = (int)qkv.size(4);
-  c10::cuda::CUDAGuard guard(qkv.device());
-  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int P = (int)pairs.size(0);
-  const float* ang = nullptr;
-  int bstride = 0;
-  if (angles.has_value() && P > 0) {
-    TORCH_CHECK(angles->scalar_type() == at::kFloat && angles->is_contiguous() && angles->size(-1) == P &&
-                    angles->size(1) == N,
-                "rope_split_fwd: angles must be contiguous fp32 (B or 1, N, P)");
-    ang = angles->data_ptr<float>();
-    bstride = angles->size(0) == 1 ? 0 : N * P;
-  }
-  TORCH_CHECK(D % 8 == 0 && D <= 256, "rope_split_fwd: head_dim must be a multiple of 8, at most 256");
-  if ((long)B * N == 0) return;
-  const size_t smem = (size_t)3 * H * D * 2 + 2 * (size_t)P * 4 + (size_t)D * sizeof(RopeRoles) + 16;
-  if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(rope_split_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  rope_split_fwd_kernel<<<B * N, 128, smem, stream>>>(
+  TORCH_CHECK(D % 8 == 0 && D <= 256 && P > 0 && P <= D / 2, "rope_qk_fwd: head_dim a multiple of 8 (<= 256), 1..D/2 pairs");
+  auto [ang, bstride] = rope_angles(angles, N, P, "rope_qk_fwd");
+  TORCH_CHECK(ang != nullptr, "rope_qk_fwd: angles required");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  const int BN = B * N;
+  if (BN == 0) return;
+  const size_t smem = rope_fwd_smem(H, D, P);
+  C10_CUDA_CHECK(cudaFuncSetAttribute(rope_qk_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rope_qk_fwd_kernel<<<(BN + kRopeTokensPerCta - 1) / kRopeTokensPerCta, 64 * kRopeTokensPerCta, smem,
+                       at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(qkv.data_ptr()), ang, pairs.data_ptr<int>(), P, bstride,
-      reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()), reinterpret_cast<bf16*>(v.data_ptr()),
-      N, H, D);
+      reinterpret_cast<bf16*>(qk.data_ptr()), BN, N, H, D);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// Fused backward of rope_split + attention: attention backward into an fp32 dq, then the RoPE
-// un-rotation into the packed (B, N, 3, H, D) gradient and per-token d(angle).
-void rope_attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
-                        torch::Tensor lse, c10::optional<torch::Tensor> angles, torch::Tensor pairs,
-                        torch::Tensor dqkv, c10::optional<torch::Tensor> dangles, double scale) {
+static void check_view(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 4 && t.stride(3) == 1 && t.scalar_type() == at::kBFloat16, "attention: ", name,
+              " must be a bf16 (B, N, H, D) view with contiguous rows");
+  TORCH_CHECK(t.stride(1) % 8 == 0 && t.stride(2) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0,
+              "attention: ", name, " rows must be 16-byte aligned");
+}
+
+// Attention on strided (B, N, H, D) views (e.g. slices of the packed projection); o (B, N, H, D)
+// contiguous, lse (B, H, N).
+void attention_fwd_strided(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse,
+                           double scale) {
+  check_view(q, "q");
+  check_view(k, "k");
+  check_view(v, "v");
+  TORCH_CHECK(o.is_contiguous() && lse.is_contiguous(), "attention_fwd_strided: contiguous o and lse");
+  const int B = (int)q.size(0), Nq = (int)q.size(1), H = (int)q.size(2), D = (int)q.size(3);
+  const int Nk = (int)k.size(1);
   c10::cuda::CUDAGuard guard(q.device());
-  const int B = (int)q.size(0), H = (int)q.size(1), N = (int)q.size(2), D = (int)q.size(3);
-  auto dq_acc = torch::empty(q.sizes(), q.options().dtype(at::kFloat));
-  auto dk = torch::empty_like(k);
-  auto dv = torch::empty_like(v);
-  attention_bwd_core(q, k, v, o, dout, lse, dq_acc, dk, dv, scale);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (Nq == 0) return;
+  DISPATCH_HEAD_DIM(D, [&] {
+    constexpr int S = HD + 8;
+    const size_t smem = (size_t)(kAttnBlockM + 4 * kAttnBlockN) * S * 2;
+    auto kern = attn_fwd_kernel<HD>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((Nq + kAttnBlockM - 1) / kAttnBlockM, B * H);
+    kern<<<grid, kAttnThreads, smem, stream>>>(
+        reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
+        reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), H,
+        Nq, Nk, (float)scale * kLog2e, bnhd_strides(q), bnhd_strides(k), bnhd_strides(v));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  });
+}
+
+// Backward of attention_fwd_strided (+ RoPE when P > 0) into the packed gradient
+// dqkv (B, N, 3, H, D): dv and dk are written by the attention backward straight into their slots,
+// dq accumulates in fp32 and is cast (and un-rotated, with dk) by rope_qk_bwd_kernel.
+void rope_attention_bwd_packed(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
+                               torch::Tensor lse, c10::optional<torch::Tensor> angles, torch::Tensor pairs,
+                               torch::Tensor dqkv, c10::optional<torch::Tensor> dangles, double scale) {
+  check_view(q, "q");
+  check_view(k, "k");
+  check_view(v, "v");
+  TORCH_CHECK(dqkv.is_contiguous() && dqkv.dim() == 5 && dqkv.size(2) == 3, "rope_attention_bwd_packed: (B, N, 3, H, D) dqkv");
+  TORCH_CHECK(dout.is_contiguous() && o.is_contiguous(), "rope_attention_bwd_packed: contiguous o / do");
+  const int B = (int)q.size(0), N = (int)q.size(1), H = (int)q.size(2), D = (int)q.size(3);
+  TORCH_CHECK(k.size(1) == N, "rope_attention_bwd_packed: self-attention (Nq == Nk) expected");
+  c10::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  auto dq_acc = torch::zeros({B, N, H, D}, q.options().dtype(at::kFloat));
+  auto dk_view = dqkv.select(2, 1);
+  auto dv_view = dqkv.select(2, 2);
+  auto delta = torch::empty({B, H, N}, q.options().dtype(at::kFloat));
+  DISPATCH_HEAD_DIM(D, [&] {
+    const int rows = B * H * N;
+    attn_delta_kernel<HD><<<(rows * 32 + 255) / 256, 256, 0, stream>>>(
+        reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+        delta.data_ptr<float>(), H, N, rows);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    constexpr int S = HD + 8;
+    const size_t smem = (size_t)(2 * kAttnBlockN + 2 * kAttnBlockM) * S * 2 + (size_t)kAttnBlockN * (kAttnBlockM + 8) * 2 +
+                        2 * kAttnBlockM * 4;
+    auto kern = attn_bwd_kernel<HD>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((N + kAttnBlockN - 1) / kAttnBlockN, B * H);
+    kern<<<grid, kAttnThreads, smem, stream>>>(
+        reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
+        reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+        lse.data_ptr<float>(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
+        reinterpret_cast<bf16*>(dk_view.data_ptr()), reinterpret_cast<bf16*>(dv_view.data_ptr()), H, N, N,
+        (float)scale, (float)scale * kLog2e, bnhd_strides(q), bnhd_strides(k), bnhd_strides(v),
+        bnhd_strides(dq_acc), bnhd_strides(dk_view), bnhd_strides(dv_view));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  });
   const int P = (int)pairs.size(0);
-  const float* ang = nullptr;
-  int bstride = 0;
-  if (angles.has_value() && P > 0) {
-    ang = angles->data_ptr<float>();
-    bstride = angles->size(0) == 1 ? 0 : N * P;
-  }
+  auto [ang, bstride] = rope_angles(angles, N, P, "rope_attention_bwd_packed");
+  const int Pk = ang != nullptr ? P : 0;
   float* dang = (dangles.has_value() && ang != nullptr) ? dangles->data_ptr<float>() : nullptr;
-  TORCH_CHECK(D % 8 == 0 && D <= 256, "rope_attention_bwd: head_dim must be a multiple of 8, at most 256");
-  const size_t smem = (size_t)4 * H * D * 4 + 2 * (size_t)P * 4 + (size_t)D * sizeof(RopeRoles) + 16;
-  if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(rope_split_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  rope_split_bwd_kernel<<<B * N, 128, smem, stream>>>(
-      dq_acc.data_ptr<float>(), reinterpret_cast<const bf16*>(dk.data_ptr()), reinterpret_cast<const bf16*>(dv.data_ptr()),
-      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()), ang,
-      pairs.data_ptr<int>(), P, bstride, reinterpret_cast<bf16*>(dqkv.data_ptr()), dang, N, H, D);
+  if (dang != nullptr)
+    TORCH_CHECK(dangles->is_contiguous() && dangles->numel() == (int64_t)B * N * P, "rope_attention_bwd_packed: dangles (B, N, P)");
+  // y: the rotated q / k the attention read (token stride of the q view's token axis)
+  const bf16* y = reinterpret_cast<const bf16*>(q.data_ptr());
+  const int64_t y_token_stride = q.stride(1);
+  TORCH_CHECK(Pk == 0 || k.data_ptr() == static_cast<const void*>(reinterpret_cast<const bf16*>(q.data_ptr()) + H * D),
+              "rope_attention_bwd_packed: k must follow q in the rotated buffer");
+  const int BN = B * N;
+  if (BN == 0) return;
+  const size_t smem = rope_bwd_smem(H, D, Pk);
+  C10_CUDA_CHECK(cudaFuncSetAttribute(rope_qk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rope_qk_bwd_kernel<<<(BN + kRopeTokensPerCta - 1) / kRopeTokensPerCta, 64 * kRopeTokensPerCta, smem, stream>>>(
+      dq_acc.data_ptr<float>(), y, y_token_stride, ang, pairs.data_ptr<int>(), Pk, bstride,
+      reinterpret_cast<bf16*>(dqkv.data_ptr()), dang, BN, N, H, D);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -793,8 +901,9 @@ int noalloc_launch(const mia::bf16* q, const mia::bf16* k, const mia::bf16* v, c
   if (cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return MIA_NOALLOC_ERR_CUDA;
   dim3 grid((Nk + kAttnBlockN - 1) / kAttnBlockN, B * H);
+  const Strides3 sq{(int64_t)H * Nq * D, (int64_t)Nq * D, D}, sk{(int64_t)H * Nk * D, (int64_t)Nk * D, D};
   attn_bwd_kernel<D><<<grid, kAttnThreads, smem, stream>>>(q, k, v, dout, lse, delta, dq_acc, dk, dv, H, Nq, Nk, scale,
-                                                          scale * kLog2e);
+                                                          scale * kLog2e, sq, sk, sk, sq, sk, sk);
   f32_to_bf16_kernel<<<(unsigned)((dq_elems / 2 + 255) / 256 + 1), 256, 0, stream>>>(dq_acc, dq, dq_elems);
   return cudaGetLastError() == cudaSuccess ? MIA_NOALLOC_OK : MIA_NOALLOC_ERR_CUDA;
 }

@@ -17,11 +17,12 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tenso
 void attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse, double scale);
 void attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, double scale);
-void rope_split_fwd(torch::Tensor qkv, c10::optional<torch::Tensor> angles, torch::Tensor pairs, torch::Tensor q,
-                    torch::Tensor k, torch::Tensor v);
-void rope_attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
-                        torch::Tensor lse, c10::optional<torch::Tensor> angles, torch::Tensor pairs,
-                        torch::Tensor dqkv, c10::optional<torch::Tensor> dangles, double scale);
+void rope_qk_fwd(torch::Tensor qkv, torch::Tensor angles, torch::Tensor pairs, torch::Tensor qk);
+void attention_fwd_strided(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse,
+                           double scale);
+void rope_attention_bwd_packed(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
+                               torch::Tensor lse, c10::optional<torch::Tensor> angles, torch::Tensor pairs,
+                               torch::Tensor dqkv, c10::optional<torch::Tensor> dangles, double scale);
 void multi_tensor_sumsq(std::vector<at::Tensor> tensors, at::Tensor out);
 void multi_tensor_scale(std::vector<at::Tensor> tensors, at::Tensor coef);
 void ema_update(std::vector<at::Tensor> teacher, std::vector<at::Tensor> student, double momentum);
@@ -65,8 +66,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_bwd", &mia::layernorm_bwd);
   m.def("attention_fwd", &mia::attention_fwd);
   m.def("attention_bwd", &mia::attention_bwd);
-  m.def("rope_split_fwd", &mia::rope_split_fwd);
-  m.def("rope_attention_bwd", &mia::rope_attention_bwd);
+  m.def("rope_qk_fwd", &mia::rope_qk_fwd, "rotate q and k of a packed (B, N, 3, H, D) projection into (B, N, 2, H, D)");
+  m.def("attention_fwd_strided", &mia::attention_fwd_strided, "attention on strided (B, N, H, D) views");
+  m.def("rope_attention_bwd_packed", &mia::rope_attention_bwd_packed, "attention (+RoPE) backward into the packed gradient");
   m.def("multi_tensor_sumsq", &mia::multi_tensor_sumsq);
   m.def("multi_tensor_scale", &mia::multi_tensor_scale);
   m.def("ema_update", &mia::ema_update, "teacher = m * teacher + (1 - m) * student over tensor lists");

@@ -54,6 +54,14 @@ struct PeerPtrs {
   int64_t p[kMaxWorld];
 };
 
+// p.p[i] without a dynamic index into the parameter array (which would copy it to local memory).
+__device__ __forceinline__ int64_t pick(const PeerPtrs p, int i) {
+  int64_t r = p.p[0];
+#pragma unroll
+  for (int j = 1; j < kMaxWorld; ++j) r = (i == j) ? p.p[j] : r;
+  return r;
+}
+
 __device__ __forceinline__ void st_release_sys(int* addr, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
@@ -76,15 +84,15 @@ __device__ __forceinline__ int* flag_slot(int64_t base, int kind, int block, int
 
 // Threads 0..world-1 of the block each signal one peer, then each wait for one peer.
 // Returns false (after recording `code`) if a peer did not arrive before the deadline.
-__device__ bool block_barrier(const PeerPtrs& flags, int kind, int rank, int world, int epoch, uint64_t timeout_ns,
+__device__ __forceinline__ bool block_barrier(const PeerPtrs flags, int kind, int rank, int world, int epoch, uint64_t timeout_ns,
                               int* err, int code) {
   __shared__ int failed;
   if (threadIdx.x == 0) failed = 0;
   __syncthreads();
   const int t = threadIdx.x;
   if (t < world) {
-    st_release_sys(flag_slot(flags.p[t], kind, blockIdx.x, rank), epoch);
-    const int* mine = flag_slot(flags.p[rank], kind, blockIdx.x, t);
+    st_release_sys(flag_slot(pick(flags, t), kind, blockIdx.x, rank), epoch);
+    const int* mine = flag_slot(pick(flags, rank), kind, blockIdx.x, t);
     const uint64_t deadline = globaltimer_ns() + timeout_ns;
     while (ld_acquire_sys(mine) < epoch) {
       if (globaltimer_ns() > deadline) {
@@ -104,7 +112,7 @@ __global__ void zero_reduce_scatter_kernel(PeerPtrs grads, PeerPtrs flags, int64
   const int epoch = *epoch_ptr + 1;
   float s = 0.f;
   if (block_barrier(flags, 0, rank, world, epoch, timeout_ns, err, kErrZeroReduceScatterWait)) {
-    float* out = reinterpret_cast<float*>(grads.p[rank]) + shard_off;
+    float* out = reinterpret_cast<float*>(pick(grads, rank)) + shard_off;
     const int64_t n4 = shard_len / 4;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -114,7 +122,7 @@ __global__ void zero_reduce_scatter_kernel(PeerPtrs grads, PeerPtrs flags, int64
         // start with a rotated peer so ranks spread their reads over different sources
         int p = rank + q;
         if (p >= world) p -= world;
-        const float4 v = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grads.p[p]) + shard_off)[i];
+        const float4 v = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pick(grads, p)) + shard_off)[i];
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
@@ -154,11 +162,11 @@ __global__ void zero_norm_exchange_kernel(PeerPtrs flags, const float* __restric
   if (t == 0) failed = 0;
   __syncthreads();
   if (t < world) {
-    float* peer_values = reinterpret_cast<float*>(reinterpret_cast<int*>(flags.p[t]) + kFlagInts);
+    float* peer_values = reinterpret_cast<float*>(reinterpret_cast<int*>(pick(flags, t)) + kFlagInts);
     peer_values[rank] = local_total;
     __threadfence_system();
-    st_release_sys(flag_slot(flags.p[t], 1, 0, rank), epoch);
-    const int* mine = flag_slot(flags.p[rank], 1, 0, t);
+    st_release_sys(flag_slot(pick(flags, t), 1, 0, rank), epoch);
+    const int* mine = flag_slot(pick(flags, rank), 1, 0, t);
     const uint64_t deadline = globaltimer_ns() + timeout_ns;
     while (ld_acquire_sys(mine) < epoch) {
       if (globaltimer_ns() > deadline) {
@@ -170,7 +178,7 @@ __global__ void zero_norm_exchange_kernel(PeerPtrs flags, const float* __restric
   }
   __syncthreads();
   if (t == 0) {
-    const float* values = reinterpret_cast<const float*>(reinterpret_cast<const int*>(flags.p[rank]) + kFlagInts);
+    const float* values = reinterpret_cast<const float*>(reinterpret_cast<const int*>(pick(flags, rank)) + kFlagInts);
     float total = 0.f;
     for (int p = 0; p < world; ++p) total += values[p];
     // the averaged gradient is sum / world, so its norm is sqrt(sum of squares of sums) / world
@@ -191,8 +199,8 @@ __global__ void zero_all_gather_kernel(PeerPtrs data, PeerPtrs shadow, PeerPtrs 
   // 1) push: groups of 8 elements (one uint4 of bf16, two float4 of fp32); bf16_begin and the
   //    shard bounds are multiples of 64, so a group never straddles the region boundary.
   const int64_t groups = shard_len / 8;
-  const float* my_data = reinterpret_cast<const float*>(data.p[rank]);
-  const __nv_bfloat16* my_shadow = reinterpret_cast<const __nv_bfloat16*>(shadow.p[rank]);
+  const float* my_data = reinterpret_cast<const float*>(pick(data, rank));
+  const __nv_bfloat16* my_shadow = reinterpret_cast<const __nv_bfloat16*>(pick(shadow, rank));
   for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = own0 + g * 8;
     if (e >= bf16_begin) {
@@ -200,7 +208,7 @@ __global__ void zero_all_gather_kernel(PeerPtrs data, PeerPtrs shadow, PeerPtrs 
       for (int q = 1; q < world; ++q) {
         int p = rank + q;
         if (p >= world) p -= world;
-        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(shadow.p[p]) + e) = v;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(pick(shadow, p)) + e) = v;
       }
     } else {
       const float4 a = *reinterpret_cast<const float4*>(my_data + e);
@@ -208,7 +216,7 @@ __global__ void zero_all_gather_kernel(PeerPtrs data, PeerPtrs shadow, PeerPtrs 
       for (int q = 1; q < world; ++q) {
         int p = rank + q;
         if (p >= world) p -= world;
-        float* dst = reinterpret_cast<float*>(data.p[p]) + e;
+        float* dst = reinterpret_cast<float*>(pick(data, p)) + e;
         *reinterpret_cast<float4*>(dst) = a;
         *reinterpret_cast<float4*>(dst + 4) = b;
       }
@@ -219,8 +227,8 @@ __global__ void zero_all_gather_kernel(PeerPtrs data, PeerPtrs shadow, PeerPtrs 
   // 2) refresh the local copies of the other shards; every block must finish its barrier first,
   //    so this phase only touches ranges whose writers this block has heard from: block b covers
   //    exactly the groups that block b of every peer wrote.
-  float* d = reinterpret_cast<float*>(data.p[rank]);
-  __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(shadow.p[rank]);
+  float* d = reinterpret_cast<float*>(pick(data, rank));
+  __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(pick(shadow, rank));
   for (int q = 1; q < world; ++q) {
     int p = rank + q;
     if (p >= world) p -= world;

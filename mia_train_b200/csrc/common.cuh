@@ -268,12 +268,32 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// Exact (erf) GELU and its derivative. Phi(x) = 0.5 (1 + erf(x / sqrt 2)) uses the rational
+// approximation of Abramowitz & Stegun, Handbook of Mathematical Functions, eq. 7.1.26:
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z),  z >= 0,
+// |error| <= 1.5e-7, odd in z. exp(-z^2) with z = x / sqrt 2 is exp(-x^2 / 2), the same factor as
+// the normal density, so the derivative costs no second exponential. Tested against torch's erf
+// GELU in tests/gpu/test_kernels.py.
+struct NormalCdfPdf {
+  float cdf, pdf;
+};
+
+__device__ __forceinline__ NormalCdfPdf normal_cdf_pdf(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float e = __expf(-0.5f * x * x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f),
+                              0.254829592f);
+  const float erf_abs = 1.0f - poly * e;
+  const float erf_x = copysignf(erf_abs, x);
+  return NormalCdfPdf{0.5f * (1.0f + erf_x), 0.39894228040143268f * e};
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return x * normal_cdf_pdf(x).cdf; }
 
 __device__ __forceinline__ float gelu_erf_grad(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
-  const float pdf = 0.39894228040143268f * expf(-0.5f * x * x);
-  return cdf + x * pdf;
+  const NormalCdfPdf n = normal_cdf_pdf(x);
+  return n.cdf + x * n.pdf;
 }
 
 }  // namespace mia

@@ -83,19 +83,32 @@ struct GemmSmem {
   static constexpr int kBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// Epilogue variants, fixed at compile time so each kernel carries only the code it runs (the
+// all-features epilogue is large enough to thrash the instruction cache of the warps running it):
+//   kEpiPlain  bias / LayerScale / residual / fp32 / accumulate / split-K, no activation
+//   kEpiGelu   bias + GELU (+ pre-activation store), bf16 out
+//   kEpiDGelu  GELU' from the stored pre-activation, bf16 out
+//   kEpiAll    everything (single-CTA kernel)
+enum Epi : int { kEpiPlain = 0, kEpiGelu = 1, kEpiDGelu = 2, kEpiAll = 3 };
+
+template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n, const uint32_t (&r)[32]) {
   if (m >= p.M || n >= p.N) return;
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  if (p.splits > 1) {  // split-K partial: atomically added into the fp32 output
+  constexpr bool kAct = EPI != kEpiPlain;
+  constexpr bool kExtras = EPI == kEpiPlain || EPI == kEpiAll;  // LayerScale, residual, fp32, accumulate, split-K
+  if (kExtras && p.splits > 1) {  // split-K partial: atomically added into the fp32 output
     float* dst = reinterpret_cast<float*>(p.D) + (size_t)m * p.N + n;
     if (n + 32 <= p.N) {
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         atomicAdd(reinterpret_cast<float4*>(dst) + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
     } else {
-      for (int j = 0; j < 32 && n + j < p.N; ++j) atomicAdd(dst + j, v[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < p.N) atomicAdd(dst + j, v[j]);
     }
     return;
   }
@@ -110,10 +123,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
         v[4 * q] += bb.x; v[4 * q + 1] += bb.y; v[4 * q + 2] += bb.z; v[4 * q + 3] += bb.w;
       }
     } else {
-      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] += __ldg(p.bias + n + j);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < p.N) v[j] += __ldg(p.bias + n + j);
     }
   }
-  if (p.act == kActGelu) {
+  if (kAct && (EPI == kEpiGelu || p.act == kActGelu)) {
     if (p.aux_out != nullptr) {
       if (full) {
         uint4* dst = reinterpret_cast<uint4*>(p.aux_out + row + n);
@@ -122,12 +137,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
           dst[q] = make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
                               pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
       } else {
-        for (int j = 0; j < 32 && n + j < p.N; ++j) p.aux_out[row + n + j] = __float2bfloat16_rn(v[j]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n + j < p.N) p.aux_out[row + n + j] = __float2bfloat16_rn(v[j]);
       }
     }
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-  } else if (p.act == kActDGelu) {
+  } else if (kAct && (EPI == kEpiDGelu || p.act == kActDGelu)) {
     if (full) {
       const uint4* src = reinterpret_cast<const uint4*>(p.aux + row + n);
 #pragma unroll
@@ -141,10 +158,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
         }
       }
     } else {
-      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] *= gelu_erf_grad(__bfloat162float(p.aux[row + n + j]));
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < p.N) v[j] *= gelu_erf_grad(__bfloat162float(p.aux[row + n + j]));
     }
   }
-  if (p.gamma != nullptr) {
+  if (kExtras && p.gamma != nullptr) {
     if (full) {
       const float4* g4 = reinterpret_cast<const float4*>(p.gamma + n);
 #pragma unroll
@@ -153,10 +172,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
         v[4 * q] *= gg.x; v[4 * q + 1] *= gg.y; v[4 * q + 2] *= gg.z; v[4 * q + 3] *= gg.w;
       }
     } else {
-      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] *= __ldg(p.gamma + n + j);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < p.N) v[j] *= __ldg(p.gamma + n + j);
     }
   }
-  if (p.residual != nullptr) {
+  if (kExtras && p.residual != nullptr) {
     if (full) {
       const uint4* src = reinterpret_cast<const uint4*>(p.residual + row + n);
 #pragma unroll
@@ -170,10 +191,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
         }
       }
     } else {
-      for (int j = 0; j < 32 && n + j < p.N; ++j) v[j] += __bfloat162float(p.residual[row + n + j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < p.N) v[j] += __bfloat162float(p.residual[row + n + j]);
     }
   }
-  if (p.d_fp32) {
+  if (kExtras && p.d_fp32) {
     float* dst = reinterpret_cast<float*>(p.D) + row + n;
     if (full) {
       float4* d4 = reinterpret_cast<float4*>(dst);
@@ -187,7 +210,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
         d4[q] = o;
       }
     } else {
-      for (int j = 0; j < 32 && n + j < p.N; ++j) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < p.N) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
     }
   } else {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row + n;
@@ -195,7 +220,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
       uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        if (p.accumulate) {
+        if (kExtras && p.accumulate) {
           uint4 old = d4[q];
           uint32_t w[4] = {old.x, old.y, old.z, old.w};
 #pragma unroll
@@ -208,9 +233,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
                            pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
       }
     } else {
-      for (int j = 0; j < 32 && n + j < p.N; ++j) {
-        float o = v[j] + (p.accumulate ? __bfloat162float(dst[j]) : 0.f);
-        dst[j] = __float2bfloat16_rn(o);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (n + j < p.N) {
+          const float o = v[j] + ((kExtras && p.accumulate) ? __bfloat162float(dst[j]) : 0.f);
+          dst[j] = __float2bfloat16_rn(o);
+        }
       }
     }
   }
@@ -386,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kChunks; ++c) {
         tmem_ld_wait_regs(r[c & 1]);
         if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, r[(c + 1) & 1]);
-        epilogue_chunk(p, m, n0 + c * 32, r[c & 1]);
+        epilogue_chunk<kEpiAll>(p, m, n0 + c * 32, r[c & 1]);
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -429,7 +457,7 @@ __device__ __forceinline__ TileCoord pair_tile_coord(const GemmParams& p, int ti
   return c;
 }
 
-template <int BN, bool A_MN, bool B_MN, int STAGES>
+template <int BN, bool A_MN, bool B_MN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const GemmParams p) {
@@ -602,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kChunks; ++c) {
         tmem_ld_wait_regs(r[c & 1]);
         if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, r[(c + 1) & 1]);
-        epilogue_chunk(p, m, n0 + c * 32, r[c & 1]);
+        epilogue_chunk<EPI>(p, m, n0 + c * 32, r[c & 1]);
       }
       tc_fence_before();
       __syncwarp();
@@ -692,11 +720,11 @@ static void dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const C
   else launch_gemm<BN, true, true, ST>(ta, tb, p, device, s);
 }
 
-template <int BN, bool A_MN, bool B_MN, int STAGES>
+template <int BN, bool A_MN, bool B_MN, int STAGES, int EPI>
 static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, int device,
                              cudaStream_t stream) {
   using L = PairSmem<BN, STAGES>;
-  auto kern = gemm_tcgen05_pair_kernel<BN, A_MN, B_MN, STAGES>;
+  auto kern = gemm_tcgen05_pair_kernel<BN, A_MN, B_MN, STAGES, EPI>;
   static bool configured[64] = {false};
   if (!configured[device]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
@@ -728,13 +756,15 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmP
 }
 
 template <int BN>
-static void dispatch_majors_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
-                                 int device, cudaStream_t s) {
+static void dispatch_majors_pair(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                                 GemmParams& p, int device, cudaStream_t s) {
   constexpr int ST = 6;
-  if (!a_mn && !b_mn) launch_gemm_pair<BN, false, false, ST>(ta, tb, p, device, s);
-  else if (!a_mn && b_mn) launch_gemm_pair<BN, false, true, ST>(ta, tb, p, device, s);
-  else if (a_mn && !b_mn) launch_gemm_pair<BN, true, false, ST>(ta, tb, p, device, s);
-  else launch_gemm_pair<BN, true, true, ST>(ta, tb, p, device, s);
+  if (epi == kEpiGelu) return launch_gemm_pair<BN, false, false, ST, kEpiGelu>(ta, tb, p, device, s);
+  if (epi == kEpiDGelu) return launch_gemm_pair<BN, false, true, ST, kEpiDGelu>(ta, tb, p, device, s);
+  if (!a_mn && !b_mn) launch_gemm_pair<BN, false, false, ST, kEpiPlain>(ta, tb, p, device, s);
+  else if (!a_mn && b_mn) launch_gemm_pair<BN, false, true, ST, kEpiPlain>(ta, tb, p, device, s);
+  else if (a_mn && !b_mn) launch_gemm_pair<BN, true, false, ST, kEpiPlain>(ta, tb, p, device, s);
+  else launch_gemm_pair<BN, true, true, ST, kEpiPlain>(ta, tb, p, device, s);
 }
 
 // 0: single-CTA tiles only; otherwise CTA pairs whenever M >= 256 (default). The environment
@@ -825,7 +855,22 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   p.aux_out = check_mat(aux_out, "aux_out");
   TORCH_CHECK(act != kActDGelu || p.aux != nullptr, "gemm: GELU' needs aux");
 
-  const bool use_pair = pair_mode() != 0 && M >= 256;
+  // The CTA-pair kernels carry the activation epilogues only in the layouts the MLP uses: GELU with
+  // both operands K-major (fc1 forward), GELU' with B N-major (dX of fc1). Other activated calls
+  // take the single-CTA kernel, whose epilogue has everything.
+  int epi = kEpiPlain;
+  bool pair_ok = true;
+  if (act == kActGelu) {
+    epi = kEpiGelu;
+    pair_ok = a_kmajor && b_kmajor;
+  } else if (act == kActDGelu) {
+    epi = kEpiDGelu;
+    pair_ok = a_kmajor && !b_kmajor;
+  }
+  if (epi != kEpiPlain &&
+      (d.scalar_type() == at::kFloat || gamma.has_value() || residual.has_value() || accumulate))
+    pair_ok = false;
+  const bool use_pair = pair_mode() != 0 && M >= 256 && pair_ok;
   const int bn = use_pair ? choose_bn_pair((int)M, (int)N, num_sms(device)) : choose_bn((int)M, (int)N, num_sms(device));
   // Split K when the output alone cannot fill the SMs and nothing in the epilogue needs the full
   // sum (the weight-gradient GEMMs: tokens are K, the output is a small fp32 matrix).
@@ -846,8 +891,8 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   CUtensorMap tb = b_kmajor ? make_map(b.data_ptr(), K, N, b.stride(0), 64, b_rows)
                             : make_map(b.data_ptr(), N, K, b.stride(0), 64, 64);
   if (use_pair) {
-    if (bn == 256) dispatch_majors_pair<256>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
-    else dispatch_majors_pair<128>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+    if (bn == 256) dispatch_majors_pair<256>(!a_kmajor, !b_kmajor, epi, ta, tb, p, device, stream);
+    else dispatch_majors_pair<128>(!a_kmajor, !b_kmajor, epi, ta, tb, p, device, stream);
   } else if (bn == 256) {
     dispatch_majors<256>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
   } else {

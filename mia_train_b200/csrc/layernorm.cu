@@ -55,6 +55,63 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Row held in registers (n == NCH * 256: eight elements per lane per 256-column chunk), read once;
+// mean and variance from the registers (two-pass in registers, so no catastrophic cancellation).
+template <typename T, int NCH>
+__global__ void layernorm_fwd_reg_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                         const float* __restrict__ b, T* __restrict__ y, float* __restrict__ mean_out,
+                                         float* __restrict__ rstd_out, int rows, float eps, int rms) {
+  constexpr int n = NCH * 256;
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
+    const T* xr = x + (size_t)row * n;
+    float v[NCH][8];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) Vec8<T>::load(xr + c * 256 + lane * 8, v[c]);
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[c][j];
+    const float mean = rms ? 0.f : warp_sum(s) * (1.0f / n);
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[c][j] - mean;
+        ss += d * d;
+      }
+    const float rstd = rsqrtf(warp_sum(ss) * (1.0f / n) + eps);
+    T* yr = y + (size_t)row * n;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = c * 256 + lane * 8;
+      float wv[8], bv[8];
+      if (w != nullptr) {
+        Vec8<float>::load(w + col, wv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[j] = 1.f;
+      }
+      if (b != nullptr) {
+        Vec8<float>::load(b + col, bv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bv[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[c][j] = (v[c][j] - mean) * rstd * wv[j] + bv[j];
+      Vec8<T>::store(yr + col, v[c]);
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
 template <typename T>
 __global__ void layernorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                                      T* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
@@ -213,6 +270,32 @@ void layernorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w, c10::optiona
   if (rows == 0) return;
   const int threads = 256;
   const int grid = std::min((rows + 7) / 8, sm_count(x) * 8);
+  if (n % 256 == 0 && n / 256 <= 8) {
+    auto launch = [&](auto tag, auto nch) {
+      using T = decltype(tag);
+      constexpr int NCH = decltype(nch)::value;
+      layernorm_fwd_reg_kernel<T, NCH><<<grid, threads, 0, stream>>>(
+          reinterpret_cast<const T*>(x.data_ptr()), wp, bp, reinterpret_cast<T*>(y.data_ptr()),
+          mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, (float)eps, rms ? 1 : 0);
+    };
+    auto by_width = [&](auto tag) {
+      switch (n / 256) {
+        case 1: launch(tag, std::integral_constant<int, 1>{}); break;
+        case 2: launch(tag, std::integral_constant<int, 2>{}); break;
+        case 3: launch(tag, std::integral_constant<int, 3>{}); break;
+        case 4: launch(tag, std::integral_constant<int, 4>{}); break;
+        case 5: launch(tag, std::integral_constant<int, 5>{}); break;
+        case 6: launch(tag, std::integral_constant<int, 6>{}); break;
+        case 7: launch(tag, std::integral_constant<int, 7>{}); break;
+        default: launch(tag, std::integral_constant<int, 8>{}); break;
+      }
+    };
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat, "layernorm: bf16 or fp32 input");
+    if (x.scalar_type() == at::kBFloat16) by_width(__nv_bfloat16{});
+    else by_width(float{});
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   if (x.scalar_type() == at::kBFloat16) {
     layernorm_fwd_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), wp, bp, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),

@@ -47,19 +47,31 @@ def _native_ok(x: torch.Tensor, head_dim: int) -> bool:
 
 
 class _NativeRopeAttention(torch.autograd.Function):
+    """Attention (+ RoPE) on the packed projection without splitting it.
+
+    Forward: q and k are rotated into a (B, N, 2, H, D) buffer (skipped without RoPE); the attention
+    kernel reads q / k from it and v straight out of `qkv` through strided views. Backward writes dv
+    and the rotated-space dk into their slots of the packed gradient, then one kernel un-rotates dq
+    and dk in place and reduces the per-token angle gradient.
+    """
+
     @staticmethod
     def forward(ctx, qkv, angles, pairs, scale):  # type: ignore[override]
         b, n, three, h, d = qkv.shape
         qkv = qkv.contiguous()
-        q = torch.empty((b, h, n, d), device=qkv.device, dtype=qkv.dtype)
-        k = torch.empty_like(q)
-        v = torch.empty_like(q)
-        ang = angles.float().contiguous() if angles is not None else None
-        native().rope_split_fwd(qkv, ang, pairs, q, k, v)
+        ang = angles.float().contiguous() if angles is not None and pairs.numel() else None
+        if ang is not None:
+            qk = torch.empty((b, n, 2, h, d), device=qkv.device, dtype=qkv.dtype)
+            native().rope_qk_fwd(qkv, ang, pairs, qk)
+            q, k = qk[:, :, 0], qk[:, :, 1]
+        else:
+            qk = None
+            q, k = qkv[:, :, 0], qkv[:, :, 1]
+        v = qkv[:, :, 2]
         o = torch.empty((b, n, h, d), device=qkv.device, dtype=qkv.dtype)
         lse = torch.empty((b, h, n), device=qkv.device, dtype=torch.float32)
-        native().attention_fwd(q, k, v, o, lse, float(scale))
-        ctx.save_for_backward(q, k, v, o, lse, ang, pairs)
+        native().attention_fwd_strided(q, k, v, o, lse, float(scale))
+        ctx.save_for_backward(qkv, qk, o, lse, ang, pairs)
         ctx.scale = scale
         ctx.angles_shape = angles.shape if angles is not None else None
         ctx.angles_dtype = angles.dtype if angles is not None else None
@@ -67,17 +79,19 @@ class _NativeRopeAttention(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do):  # type: ignore[override]
-        q, k, v, o, lse, ang, pairs = ctx.saved_tensors
-        do = do.to(q.dtype).contiguous()
-        b, h, n, d = q.shape
-        dqkv = torch.empty((b, n, 3, h, d), device=q.device, dtype=q.dtype)
+        qkv, qk, o, lse, ang, pairs = ctx.saved_tensors
+        do = do.to(qkv.dtype).contiguous()
+        b, n, _, h, d = qkv.shape
+        src = qk if qk is not None else qkv
+        q, k, v = src[:, :, 0], src[:, :, 1], qkv[:, :, 2]
+        dqkv = torch.empty_like(qkv)
         dang = None
-        if ang is not None:
-            dang = torch.zeros((ang.shape[0] if ang.shape[0] == b else b, n, pairs.shape[0]), device=q.device, dtype=torch.float32)
-        native().rope_attention_bwd(q, k, v, o, do, lse, ang, pairs, dqkv, dang, float(ctx.scale))
-        if dang is not None and ctx.angles_shape[0] == 1 and b != 1:
-            dang = dang.sum(0, keepdim=True)
+        if ang is not None and ctx.needs_input_grad[1]:
+            dang = torch.empty((b, n, pairs.shape[0]), device=qkv.device, dtype=torch.float32)
+        native().rope_attention_bwd_packed(q, k, v, o, do, lse, ang, pairs, dqkv, dang, float(ctx.scale))
         if dang is not None:
+            if ctx.angles_shape[0] == 1 and b != 1:
+                dang = dang.sum(0, keepdim=True)
             dang = dang.to(ctx.angles_dtype)
         return dqkv, dang, None, None
 

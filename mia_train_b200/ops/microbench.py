@@ -33,7 +33,10 @@ def _time(fn, iters: int = 20, warmup: int = 5) -> float:
     return start.elapsed_time(end) / iters * 1000.0  # microseconds
 
 
-def bench_gemm(m: int, n: int, k: int, layout: str = "nn", iters: int = 20, out_fp32: bool = False) -> dict:
+def bench_gemm(m: int, n: int, k: int, layout: str = "nn", iters: int = 20, out_fp32: bool = False,
+               act: str = "none") -> dict:
+    from .linear import ACT_DGELU, ACT_GELU, ACT_NONE
+
     dev = torch.device("cuda")
     a = torch.randn(m, k, device=dev).bfloat16()
     b = torch.randn(n, k, device=dev).bfloat16()
@@ -41,7 +44,10 @@ def bench_gemm(m: int, n: int, k: int, layout: str = "nn", iters: int = 20, out_
     a_in = a if a_k else a.t().contiguous()
     b_in = b if b_k else b.t().contiguous()
     out = torch.empty(m, n, device=dev, dtype=torch.float32 if out_fp32 else torch.bfloat16)
-    us = _time(lambda: gemm(a_in, b_in, a_kmajor=a_k, b_kmajor=b_k, out=out), iters)
+    code = {"none": ACT_NONE, "gelu": ACT_GELU, "dgelu": ACT_DGELU}[act]
+    extra = torch.randn(m, n, device=dev).bfloat16() if act != "none" else None
+    kw = {"aux_out": extra} if act == "gelu" else {"aux": extra} if act == "dgelu" else {}
+    us = _time(lambda: gemm(a_in, b_in, a_kmajor=a_k, b_kmajor=b_k, out=out, act=code, **kw), iters)
     am = a_in if a_k else a_in.t()
     bm = b_in if b_k else b_in.t()
     us_cublas = _time(lambda: torch.matmul(am, bm.t()), iters)
@@ -152,6 +158,7 @@ def main() -> None:
     g.add_argument("--layout", default="nn")
     g.add_argument("--iters", type=int, default=20)
     g.add_argument("--fp32-out", action="store_true")
+    g.add_argument("--act", choices=("none", "gelu", "dgelu"), default="none")
     s = sub.add_parser("mae-step-gemms")
     s.add_argument("--batch", type=int, default=16)
     s.add_argument("--iters", type=int, default=20)
@@ -168,7 +175,7 @@ def main() -> None:
         print(step_gemms(args.depth, args.batch))
         return
     if args.cmd == "gemm":
-        print(bench_gemm(args.m, args.n, args.k, args.layout, args.iters, args.fp32_out))
+        print(bench_gemm(args.m, args.n, args.k, args.layout, args.iters, args.fp32_out, args.act))
     elif args.cmd == "attention":
         print(bench_attention(args.b, args.h, args.n, args.d, args.iters))
     else:

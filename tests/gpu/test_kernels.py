@@ -84,6 +84,22 @@ def test_gemm_epilogues(pair_mode):
     _no_errors()
 
 
+def test_gelu_epilogue_matches_exact_erf_gelu():
+    """fp32 GELU / GELU' epilogues against torch's exact-erf GELU on exactly representable inputs."""
+    torch.manual_seed(3)
+    m, n, k = 256, 512, 64
+    # small integers / 8: every product and sum is exact in fp32, so the pre-activation is exact
+    a = (torch.randint(-8, 9, (m, k), device=DEV).float() / 8).bfloat16()
+    b = (torch.randint(-8, 9, (n, k), device=DEV).float() / 64).bfloat16()
+    pre = a.float() @ b.float().t()
+    y = gemm(a, b, act=ACT_GELU, out_dtype=torch.float32)
+    torch.testing.assert_close(y, F.gelu(pre), atol=3e-6, rtol=1e-6)
+    aux = pre.bfloat16()
+    g = gemm(a, b, act=ACT_DGELU, aux=aux, out_dtype=torch.float32)
+    torch.testing.assert_close(g, pre * gelu_grad_reference(aux.float()), atol=3e-6, rtol=2e-6)
+    _no_errors()
+
+
 def test_column_sum():
     from mia_train_b200.ops.linear import column_sum
 
@@ -146,12 +162,12 @@ def test_attention_fwd_bwd(shape):
     _no_errors()
 
 
-def test_rope_attention_matches_reference():
+@pytest.mark.parametrize("b,n,h,d", [(2, 128, 4, 64), (3, 77, 2, 32), (1, 200, 3, 128)])
+def test_rope_attention_matches_reference(b, n, h, d):
     from mia_train_b200.layers.common.rope import AxialRotaryEmbedding
     from mia_train_b200.ops import attention as attn_ops
 
     torch.manual_seed(4)
-    b, n, h, d = 2, 128, 4, 64
     rot = AxialRotaryEmbedding(d, 3).to(DEV)
     coords = torch.randint(0, 8, (b, n, 3), device=DEV).float()
     qkv = torch.randn(b, n, 3, h, d, device=DEV).bfloat16().requires_grad_(True)
@@ -173,6 +189,51 @@ def test_rope_attention_matches_reference():
     _close(g_native, qkv32.grad, rel=3e-2, atol=3e-2)
     for fn, f in zip(f_native, rot.inv_freqs, strict=True):
         _close(fn, f.grad, rel=5e-2, atol=5e-2)
+    _no_errors()
+
+
+@pytest.mark.parametrize("b,n,h,d", [(2, 128, 4, 64), (2, 100, 2, 32)])
+def test_packed_attention_without_rope(b, n, h, d):
+    from mia_train_b200.ops import attention as attn_ops
+
+    torch.manual_seed(6)
+    qkv = torch.randn(b, n, 3, h, d, device=DEV).bfloat16().requires_grad_(True)
+    out = attn_ops.rope_attention(qkv, None, None, d**-0.5)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    with _native.reference_math():
+        qkv32 = qkv.detach().float().requires_grad_(True)
+        ref = attn_ops.rope_attention(qkv32, None, None, d**-0.5)
+        ref.backward(dout.float())
+    _close(out, ref)
+    _close(qkv.grad, qkv32.grad, rel=3e-2, atol=3e-2)
+    _no_errors()
+
+
+def test_dinov3_rope_attention_shared_angles():
+    """DINOv3 layout: prefix tokens unrotated, pairs (i, i + D/2), angles shared by the batch."""
+    from mia_train_b200.layers.dinov3.attention import half_pairs
+    from mia_train_b200.ops import attention as attn_ops
+
+    torch.manual_seed(7)
+    b, n, h, d = 3, 69, 4, 64
+    pairs = half_pairs(d, DEV)
+    ang = torch.randn(1, n, d // 2, device=DEV).requires_grad_(True)
+    with torch.no_grad():
+        ang[:, :5] = 0.0
+    qkv = torch.randn(b, n, 3, h, d, device=DEV).bfloat16().requires_grad_(True)
+    out = attn_ops.rope_attention(qkv, ang, pairs, d**-0.5)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    g_ang = ang.grad.clone()
+    ang.grad = None
+    with _native.reference_math():
+        qkv32 = qkv.detach().float().requires_grad_(True)
+        ref = attn_ops.rope_attention(qkv32, ang, pairs, d**-0.5)
+        ref.backward(dout.float())
+    _close(out, ref)
+    _close(qkv.grad, qkv32.grad, rel=3e-2, atol=3e-2)
+    _close(g_ang, ang.grad, rel=5e-2, atol=5e-2)
     _no_errors()
 
 
