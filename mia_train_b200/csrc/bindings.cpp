@@ -56,6 +56,9 @@ void zero_all_gather(std::vector<int64_t> data_peers, std::vector<int64_t> shado
                      int64_t shard_len, int64_t bf16_begin, int64_t total, at::Tensor epoch, int64_t rank, int64_t blocks,
                      double timeout_ms);
 void zero_advance_epoch(at::Tensor epoch);
+at::Tensor axial_angles_fwd(at::Tensor coords, std::vector<at::Tensor> freqs);
+void axial_angles_bwd(at::Tensor dangles, at::Tensor coords, std::vector<at::Tensor> freqs,
+                      std::vector<at::Tensor> dfreqs);
 }  // namespace mia
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -93,5 +96,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("zero_all_gather", &mia::zero_all_gather, "peer-memory parameter all-gather + local refresh");
   m.def("zero_advance_epoch", &mia::zero_advance_epoch);
   m.def("set_gemm_pair_mode", &mia::set_gemm_pair_mode, "0: single-CTA GEMM tiles; else CTA pairs when M >= 256; returns the previous mode");
+  m.def("axial_angles_fwd", &mia::axial_angles_fwd, "angles[r, p] = coords[r, axis(p)] * freq(p)");
+  m.def("axial_angles_bwd", &mia::axial_angles_bwd, "accumulate the frequency gradients of axial_angles_fwd");
   m.def("check_errors", &mia::read_and_clear_errors, "read and clear the device error word");
 }

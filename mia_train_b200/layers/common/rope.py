@@ -18,6 +18,8 @@ from dataclasses import dataclass
 import torch
 import torch.nn as nn
 
+from ...ops._native import native, use_native
+from ...ops._params import grad_sink
 from ...ops.attention import rotate_pairs
 
 
@@ -55,6 +57,25 @@ class RotaryTables:
         return rotate_pairs(x, self.angles, self.pairs)
 
 
+class _AxialAngles(torch.autograd.Function):
+    """Native angle table; frequency gradients are added straight into `main_grad` when present."""
+
+    @staticmethod
+    def forward(ctx, coords, *freqs):  # type: ignore[override]
+        coords = coords.float().contiguous()
+        ctx.save_for_backward(coords, *freqs)
+        return native().axial_angles_fwd(coords, [f.contiguous() for f in freqs])
+
+    @staticmethod
+    def backward(ctx, dangles):  # type: ignore[override]
+        coords, *freqs = ctx.saved_tensors
+        sinks = [grad_sink(f) for f in freqs]
+        outs = [s if s is not None else torch.zeros_like(f) for s, f in zip(sinks, freqs, strict=True)]
+        native().axial_angles_bwd(dangles.float().contiguous(), coords, [f.contiguous() for f in freqs], outs)
+        grads = [None if s is not None else o for s, o in zip(sinks, outs, strict=True)]
+        return (None, *grads)
+
+
 class AxialRotaryEmbedding(nn.Module):
     def __init__(self, head_dim: int, spatial_rank: int, base: float = 10000.0) -> None:
         super().__init__()
@@ -78,6 +99,9 @@ class AxialRotaryEmbedding(nn.Module):
                 f"expected coordinates with {self.spatial_rank} components on the last axis, got "
                 f"{tuple(coords.shape)}"
             )
+        freqs = list(self.inv_freqs)
+        if coords.is_cuda and all(type(f) is nn.Parameter or type(f) is torch.Tensor for f in freqs) and use_native(coords):
+            return _AxialAngles.apply(coords, *freqs)
         per_axis = [
             coords[..., a].float().unsqueeze(-1) * f.float() for a, f in enumerate(self.inv_freqs)
         ]

@@ -192,6 +192,27 @@ def test_rope_attention_matches_reference(b, n, h, d):
     _no_errors()
 
 
+def test_axial_angles_native_matches_torch():
+    from mia_train_b200.layers.common.rope import AxialRotaryEmbedding
+
+    torch.manual_seed(8)
+    rot = AxialRotaryEmbedding(64, 3).to(DEV)
+    coords = torch.randn(4, 37, 3, device=DEV) * 10
+    ang = rot.angles(coords)
+    g = torch.randn_like(ang)
+    ang.backward(g)
+    got = [f.grad.clone() for f in rot.inv_freqs]
+    for f in rot.inv_freqs:
+        f.grad = None
+    with _native.reference_math():
+        ref = rot.angles(coords)
+        ref.backward(g)
+    torch.testing.assert_close(ang, ref, atol=1e-5, rtol=1e-6)
+    for a, f in zip(got, rot.inv_freqs, strict=True):
+        torch.testing.assert_close(a, f.grad, atol=1e-2, rtol=1e-4)
+    _no_errors()
+
+
 @pytest.mark.parametrize("b,n,h,d", [(2, 128, 4, 64), (2, 100, 2, 32)])
 def test_packed_attention_without_rope(b, n, h, d):
     from mia_train_b200.ops import attention as attn_ops
