@@ -58,6 +58,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--batch", type=int, default=CONFIG["per_rank_batch"])
     ap.add_argument("--depth", type=int, default=24, help="encoder depth (24 = the named config)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--overlap-dp", action="store_true",
+                    help="reduce-scatter each block's gradients during backward (side stream) instead of after it")
     ap.add_argument("--dp-impl", choices=("p2p", "nccl", "allreduce"), default="p2p",
                     help="data-parallel gradient path for N > 1 (sharded optimizer over peer memory by default)")
     ap.add_argument("--profile-kernels", type=int, default=0, metavar="STEPS",
@@ -200,7 +202,8 @@ def native_arm(args: argparse.Namespace, rank: int, world: int, local: int) -> d
                                     lambda: torch.autocast("cuda", dtype=torch.bfloat16))
 
     step = CapturedStep(alg, opt, tcfg, {"img": pool_dev[: args.batch]}, eager_steps=2, forward=forward,
-                        process_group=dist.group.WORLD if world > 1 else None, dp_impl=args.dp_impl)
+                        process_group=dist.group.WORLD if world > 1 else None, dp_impl=args.dp_impl,
+                        overlap=args.overlap_dp)
 
     def device_batch(i: int) -> dict:
         j = (i * args.batch) % pool_dev.shape[0]
@@ -427,7 +430,9 @@ def main() -> None:
                     "model": CONFIG["model"] if args.depth == 24 else CONFIG["model"] + f" (depth {args.depth})",
                     "global_batch": args.batch * world,
                     "seq_len": CONFIG["seq_len"],
-                    "parallelism": f"dp{world}" + (f" (sharded optimizer, {args.dp_impl})" if world > 1 and args.impl == "native" else ""),
+                    "parallelism": f"dp{world}" + (
+                        f" (sharded optimizer, {args.dp_impl}{', overlapped' if args.overlap_dp else ''})"
+                        if world > 1 and args.impl == "native" else ""),
                     "l2": "inputs and weights larger than L2 (no flush)",
                 },
                 "mfu": round(mfu, 4),

@@ -49,12 +49,13 @@ void ipc_free(int64_t local_ptr, int64_t device);
 int64_t comm_flag_bytes();
 int64_t comm_max_blocks();
 void zero_reduce_scatter(std::vector<int64_t> grad_peers, std::vector<int64_t> flag_peers, int64_t shard_off,
-                         int64_t shard_len, at::Tensor partial, at::Tensor epoch, int64_t rank, double timeout_ms);
+                         int64_t shard_len, at::Tensor partial, at::Tensor epoch, int64_t rank, double timeout_ms,
+                         int64_t seq, int64_t threads);
 void zero_norm_exchange(std::vector<int64_t> flag_peers, at::Tensor partial, at::Tensor epoch, int64_t rank,
                         double max_norm, at::Tensor grad_scale, at::Tensor grad_norm, double timeout_ms);
 void zero_all_gather(std::vector<int64_t> data_peers, std::vector<int64_t> shadow_peers, std::vector<int64_t> flag_peers,
-                     int64_t shard_len, int64_t bf16_begin, int64_t total, at::Tensor epoch, int64_t rank, int64_t blocks,
-                     double timeout_ms);
+                     int64_t seg_lo, int64_t shard_len, int64_t bf16_begin, at::Tensor epoch, int64_t rank, int64_t blocks,
+                     double timeout_ms, int64_t seq);
 void zero_advance_epoch(at::Tensor epoch);
 at::Tensor axial_angles_fwd(at::Tensor coords, std::vector<at::Tensor> freqs);
 void axial_angles_bwd(at::Tensor dangles, at::Tensor coords, std::vector<at::Tensor> freqs,

@@ -13,14 +13,16 @@
 // the failure. `epoch` is a device counter advanced once per step by `zero_advance_epoch`, so the
 // whole step can be captured in a CUDA graph and replayed.
 //
-// Kernels of one step (same grid on every rank, same order):
-//   zero_reduce_scatter  -- start barrier (all ranks finished backward), then rank r sums the
-//                           gradient shard r from every peer into its local gradient buffer and
-//                           accumulates per-CTA sums of squares.
+// The flat buffers are cut into segments; rank r owns the r-th slice of every segment. Kernels of
+// one step (same grids on every rank, same order):
+//   zero_reduce_scatter  -- per segment, possibly while backward still runs on later segments:
+//                           start barrier (every rank finished that segment's gradients), then
+//                           rank r sums its slice from every peer into its local gradient buffer
+//                           and accumulates per-CTA sums of squares.
 //   zero_norm_exchange   -- one CTA: local sum of squares -> every peer, barrier, global norm,
 //                           clip coefficient (times 1/world) into a device scalar for AdamW.
 //   (AdamW on the local shard: the multi-tensor kernel in optim.cu.)
-//   zero_all_gather      -- push the updated shard to every peer (fp32 master values for the
+//   zero_all_gather      -- per segment: push the updated slice to every peer (fp32 master values for the
 //                           fp32 region, bf16 shadow values for the bf16 region), system fence,
 //                           end barrier; then refresh the local copies of the other ranks' shards
 //                           (bf16 region: fp32 <- bf16 shadow; fp32 region: shadow <- bf16(fp32)).
@@ -49,6 +51,10 @@ constexpr int kMaxBlocks = 512;
 constexpr int kKinds = 4;  // 0 reduce-scatter start, 1 norm exchange, 2 all-gather end, 3 spare
 constexpr int kFlagInts = kKinds * kMaxBlocks * kMaxWorld;
 constexpr int kValueFloats = kMaxWorld;
+// Barrier values are epoch * kSeqPerStep + seq + 1: `seq` numbers the launches of one kind within a
+// step (all ranks launch them in the same order), so values only grow and a slot left over from an
+// earlier launch can never satisfy a later one.
+constexpr int kSeqPerStep = 128;
 
 struct PeerPtrs {
   int64_t p[kMaxWorld];
@@ -108,8 +114,8 @@ __device__ __forceinline__ bool block_barrier(const PeerPtrs flags, int kind, in
 
 __global__ void zero_reduce_scatter_kernel(PeerPtrs grads, PeerPtrs flags, int64_t shard_off, int64_t shard_len,
                                            float* __restrict__ partial, const int* __restrict__ epoch_ptr, int rank,
-                                           int world, uint64_t timeout_ns, int* err) {
-  const int epoch = *epoch_ptr + 1;
+                                           int world, int seq, uint64_t timeout_ns, int* err) {
+  const int epoch = *epoch_ptr * kSeqPerStep + seq + 1;
   float s = 0.f;
   if (block_barrier(flags, 0, rank, world, epoch, timeout_ns, err, kErrZeroReduceScatterWait)) {
     float* out = reinterpret_cast<float*>(pick(grads, rank)) + shard_off;
@@ -149,7 +155,7 @@ __global__ void zero_norm_exchange_kernel(PeerPtrs flags, const float* __restric
                                           const int* __restrict__ epoch_ptr, int rank, int world, float max_norm,
                                           float* __restrict__ grad_scale, float* __restrict__ grad_norm,
                                           uint64_t timeout_ns, int* err) {
-  const int epoch = *epoch_ptr + 1;
+  const int epoch = *epoch_ptr * kSeqPerStep + 1;
   __shared__ float local_total;
   if (threadIdx.x == 0) {
     float t = 0.f;
@@ -191,11 +197,12 @@ __global__ void zero_norm_exchange_kernel(PeerPtrs flags, const float* __restric
   }
 }
 
-__global__ void zero_all_gather_kernel(PeerPtrs data, PeerPtrs shadow, PeerPtrs flags, int64_t shard_len,
-                                       int64_t bf16_begin, int64_t total, const int* __restrict__ epoch_ptr, int rank,
-                                       int world, uint64_t timeout_ns, int* err) {
-  const int epoch = *epoch_ptr + 1;
-  const int64_t own0 = (int64_t)rank * shard_len;
+// One segment [seg_lo, seg_lo + world * shard_len): rank r owns the r-th shard_len slice of it.
+__global__ void zero_all_gather_kernel(PeerPtrs data, PeerPtrs shadow, PeerPtrs flags, int64_t seg_lo,
+                                       int64_t shard_len, int64_t bf16_begin, const int* __restrict__ epoch_ptr,
+                                       int rank, int world, int seq, uint64_t timeout_ns, int* err) {
+  const int epoch = *epoch_ptr * kSeqPerStep + seq + 1;
+  const int64_t own0 = seg_lo + (int64_t)rank * shard_len;
   // 1) push: groups of 8 elements (one uint4 of bf16, two float4 of fp32); bf16_begin and the
   //    shard bounds are multiples of 64, so a group never straddles the region boundary.
   const int64_t groups = shard_len / 8;
@@ -232,10 +239,9 @@ __global__ void zero_all_gather_kernel(PeerPtrs data, PeerPtrs shadow, PeerPtrs 
   for (int q = 1; q < world; ++q) {
     int p = rank + q;
     if (p >= world) p -= world;
-    const int64_t base = (int64_t)p * shard_len;
+    const int64_t base = seg_lo + (int64_t)p * shard_len;
     for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
       const int64_t e = base + g * 8;
-      if (e >= total) break;
       if (e >= bf16_begin) {
         const uint4 v = *reinterpret_cast<const uint4*>(sh + e);
         const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
@@ -331,7 +337,10 @@ int64_t comm_max_blocks() { return kMaxBlocks; }
 
 // ---------------------------------------------------------------------------------------- launches
 void zero_reduce_scatter(std::vector<int64_t> grad_peers, std::vector<int64_t> flag_peers, int64_t shard_off,
-                         int64_t shard_len, at::Tensor partial, at::Tensor epoch, int64_t rank, double timeout_ms) {
+                         int64_t shard_len, at::Tensor partial, at::Tensor epoch, int64_t rank, double timeout_ms,
+                         int64_t seq, int64_t threads) {
+  TORCH_CHECK(threads >= 64 && threads <= 1024 && threads % 32 == 0, "zero_reduce_scatter: 64..1024 threads, whole warps");
+  TORCH_CHECK(seq >= 0 && seq < kSeqPerStep, "zero_reduce_scatter: launch sequence number out of range");
   const int world = (int)grad_peers.size();
   TORCH_CHECK(shard_off % 64 == 0 && shard_len % 64 == 0, "zero_reduce_scatter: shard must be 64-element aligned");
   TORCH_CHECK(partial.scalar_type() == at::kFloat && partial.is_cuda() && partial.numel() >= 1 &&
@@ -341,9 +350,9 @@ void zero_reduce_scatter(std::vector<int64_t> grad_peers, std::vector<int64_t> f
   c10::cuda::CUDAGuard guard(partial.device());
   const int grid = (int)partial.numel();
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  zero_reduce_scatter_kernel<<<grid, 512, 0, stream>>>(to_peers(grad_peers, world), to_peers(flag_peers, world), shard_off,
+  zero_reduce_scatter_kernel<<<grid, (int)threads, 0, stream>>>(to_peers(grad_peers, world), to_peers(flag_peers, world), shard_off,
                                                        shard_len, partial.data_ptr<float>(), epoch.data_ptr<int>(),
-                                                       (int)rank, world, timeout_from_ms(timeout_ms),
+                                                       (int)rank, world, (int)seq, timeout_from_ms(timeout_ms),
                                                        error_word(partial.get_device()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -362,17 +371,18 @@ void zero_norm_exchange(std::vector<int64_t> flag_peers, at::Tensor partial, at:
 }
 
 void zero_all_gather(std::vector<int64_t> data_peers, std::vector<int64_t> shadow_peers, std::vector<int64_t> flag_peers,
-                     int64_t shard_len, int64_t bf16_begin, int64_t total, at::Tensor epoch, int64_t rank, int64_t blocks,
-                     double timeout_ms) {
+                     int64_t seg_lo, int64_t shard_len, int64_t bf16_begin, at::Tensor epoch, int64_t rank, int64_t blocks,
+                     double timeout_ms, int64_t seq) {
   const int world = (int)data_peers.size();
-  TORCH_CHECK(shard_len % 64 == 0 && bf16_begin % 64 == 0 && total == shard_len * world,
-              "zero_all_gather: 64-element aligned shards covering the buffer expected");
+  TORCH_CHECK(seg_lo % 64 == 0 && shard_len % 64 == 0 && bf16_begin % 64 == 0,
+              "zero_all_gather: 64-element aligned segments expected");
+  TORCH_CHECK(seq >= 0 && seq < kSeqPerStep, "zero_all_gather: launch sequence number out of range");
   TORCH_CHECK(blocks >= 1 && blocks <= kMaxBlocks, "zero_all_gather: 1..", kMaxBlocks, " blocks");
   c10::cuda::CUDAGuard guard(epoch.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   zero_all_gather_kernel<<<(int)blocks, 512, 0, stream>>>(to_peers(data_peers, world), to_peers(shadow_peers, world),
-                                                          to_peers(flag_peers, world), shard_len, bf16_begin, total,
-                                                          epoch.data_ptr<int>(), (int)rank, world,
+                                                          to_peers(flag_peers, world), seg_lo, shard_len, bf16_begin,
+                                                          epoch.data_ptr<int>(), (int)rank, world, (int)seq,
                                                           timeout_from_ms(timeout_ms), error_word(epoch.get_device()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

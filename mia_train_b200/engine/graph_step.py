@@ -63,6 +63,7 @@ class FlatParameters:
         world: int = 1,
         bf16_region: bool = False,
         allocate: Callable[[int, torch.dtype], tuple[torch.Tensor, list[int] | None]] | None = None,
+        groups: list[list[nn.Parameter]] | None = None,
     ) -> None:
         seen: set[int] = set()
         params: list[nn.Parameter] = []
@@ -77,21 +78,48 @@ class FlatParameters:
             for m in module.modules():
                 if isinstance(m, (nn.Linear, nn.modules.conv._ConvNd)) and isinstance(m.weight, nn.Parameter):
                     gemm_weights.add(id(m.weight))
-        params = [p for p in params if id(p) not in gemm_weights] + [p for p in params if id(p) in gemm_weights]
-        device = params[0].device
-        offsets, total = [], 0
-        self.bf16_begin = -1
-        for p in params:
-            if self.bf16_begin < 0 and id(p) in gemm_weights:
-                self.bf16_begin = total
-            offsets.append(total)
-            total += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
+        # groups: lists of bf16-region parameters that get segments of their own (in this order)
+        grouped: list[list[nn.Parameter]] = []
+        in_group: set[int] = set()
+        for g in groups or []:
+            members = [p for p in g if id(p) in gemm_weights and id(p) in seen and id(p) not in in_group]
+            if members:
+                grouped.append(members)
+                in_group.update(id(p) for p in members)
+        fp32_part = [p for p in params if id(p) not in gemm_weights]
+        bf16_rest = [p for p in params if id(p) in gemm_weights and id(p) not in in_group]
         unit = _ALIGN * world
+        device = params[0].device
+        offsets: dict[int, int] = {}
+        total = 0
+
+        def place(p: nn.Parameter) -> None:
+            nonlocal total
+            offsets[id(p)] = total
+            total += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
+
+        for p in fp32_part:
+            place(p)
+        self.bf16_begin = total
+        for p in bf16_rest:
+            place(p)
         total = (total + unit - 1) // unit * unit
-        if self.bf16_begin < 0:
-            self.bf16_begin = total
-        self.params = params
-        self.offsets = offsets
+        self.segments: list[tuple[int, int]] = [(0, total)]
+        for g in grouped:
+            lo = total
+            for p in g:
+                place(p)
+            total = (total + unit - 1) // unit * unit
+            self.segments.append((lo, total))
+        if total == 0:
+            total = unit
+            self.segments = [(0, unit)]
+        if not bf16_region:
+            self.bf16_begin = total  # no bf16 region: every parameter travels in fp32
+        ordered = fp32_part + bf16_rest + [p for g in grouped for p in g]
+        self.params = ordered
+        self.offsets = [offsets[id(p)] for p in ordered]
+        self.groups = grouped
         self.total = total
         self.world = world
         self.peers: dict[str, list[int]] | None = None
@@ -105,9 +133,10 @@ class FlatParameters:
             self.shadow, ps = allocate(total, torch.bfloat16)
             if pd is not None:
                 self.peers = {"data": pd, "grad": pg, "shadow": ps}
+        params = ordered
         self._hooks = []
         with torch.no_grad():
-            for p, off in zip(params, offsets, strict=True):
+            for p, off in zip(params, self.offsets, strict=True):
                 n = p.numel()
                 view = self.data[off:off + n].view_as(p)
                 view.copy_(p.data)
@@ -177,6 +206,16 @@ class DeviceSchedule:
         return self.current
 
 
+def _overlap_blocks(algorithm: nn.Module) -> list[nn.Module]:
+    """The transformer blocks declared by the model and the algorithm, in module order."""
+    from .activation_checkpoint import checkpointable_targets
+
+    try:
+        return checkpointable_targets(algorithm)
+    except ValueError:
+        return []
+
+
 def _to_static(batch: Any, device: torch.device) -> Any:
     if isinstance(batch, torch.Tensor):
         return torch.empty(batch.shape, dtype=batch.dtype, device=device)
@@ -215,6 +254,7 @@ class CapturedStep:
         process_group: Any = None,
         dp_impl: str = "p2p",
         comm_timeout_ms: float = 10_000.0,
+        overlap: bool = False,
     ) -> None:
         if not hasattr(optimizer, "grad_scale"):
             raise TypeError("CapturedStep needs the fused optimizer (FusedAdamW)")
@@ -238,9 +278,11 @@ class CapturedStep:
             from .zero import IpcBuffers, ShardedStep
 
             ipc = IpcBuffers(process_group, self.device) if self.dp_impl == "p2p" else None
+            blocks = _overlap_blocks(algorithm) if overlap else []
             self.flat = FlatParameters(
                 algorithm, world=self.world, bf16_region=config.precision == "bf16",
                 allocate=ipc.allocate if ipc is not None else None,
+                groups=[list(b.parameters()) for b in blocks],
             )
         self.schedule = DeviceSchedule(optimizer, config, start_step)
         optimizer.external_hyper = self.schedule.current  # type: ignore[attr-defined]
@@ -249,6 +291,21 @@ class CapturedStep:
                 self.flat, optimizer, process_group, "p2p" if self.dp_impl == "p2p" else "nccl",
                 config.grad_clip_norm, self.schedule.current, ipc=ipc, timeout_ms=comm_timeout_ms,
             )
+        # Reduce-scatter each block's weight gradients on a side stream as soon as the block's
+        # backward has been issued (its input gradient is the last thing it computes).
+        self._in_backward = False
+        self._block_hooks: list[Any] = []
+        self.comm_stream: torch.cuda.Stream | None = None
+        if self.zero is not None and len(self.flat.segments) > 1:
+            self.comm_stream = torch.cuda.Stream(self.device)
+            segment_of = {}
+            for gi, group in enumerate(self.flat.groups):
+                for p in group:
+                    segment_of[id(p)] = gi + 1
+            for block in blocks:
+                segs = {segment_of[id(p)] for p in block.parameters() if id(p) in segment_of}
+                if len(segs) == 1:
+                    self._block_hooks.append(block.register_full_backward_hook(self._make_hook(segs.pop())))
         self.static_batch = _to_static(example_batch, self.device)
         self.static_metrics: dict[str, torch.Tensor] = {}
         self.eager_steps = eager_steps
@@ -258,6 +315,18 @@ class CapturedStep:
         self._forward = forward or algorithm
         self._autocast_dtype = torch.bfloat16 if config.precision == "bf16" else None
 
+    def _make_hook(self, segment: int) -> Callable[..., None]:
+        def hook(module: nn.Module, grad_input: Any, grad_output: Any) -> None:
+            if not self._in_backward or self.comm_stream is None:
+                return
+            ready = torch.cuda.Event()
+            ready.record(torch.cuda.current_stream(self.device))
+            self.comm_stream.wait_event(ready)
+            with torch.cuda.stream(self.comm_stream):
+                self.zero.reduce_segment(segment)
+
+        return hook
+
     def _body(self) -> dict[str, torch.Tensor]:
         self.flat.zero_grad()
         self.schedule.advance()
@@ -266,10 +335,20 @@ class CapturedStep:
                 metrics = self._forward(self.static_batch)
         else:
             metrics = self._forward(self.static_batch)
-        metrics["loss"].backward()
+        if self.zero is not None:
+            self.zero.begin()
+            if self.comm_stream is not None:  # the side stream joins this step's stream order
+                self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self._in_backward = True
+        try:
+            metrics["loss"].backward()
+        finally:
+            self._in_backward = False
         out = {k: v.detach() for k, v in metrics.items()}
         if self.zero is not None:
-            norm = self.zero.step()
+            if self.comm_stream is not None:
+                torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+            norm = self.zero.finish()
             if self.config.grad_clip_norm is not None:
                 out["grad_norm"] = norm
             return out
@@ -321,6 +400,9 @@ class CapturedStep:
 
     def release(self) -> None:
         self.graph = None
+        for h in self._block_hooks:
+            h.remove()
+        self._block_hooks = []
         if self.zero is not None:
             self.zero.gather_masters()
         self.flat.release()

@@ -89,7 +89,14 @@ def _all_gather_cpu(t: torch.Tensor, group: Any) -> list[torch.Tensor]:
 
 
 class ShardedStep:
-    """Steps 1-4 above for a `FlatParameters` built with `world` and matching buffers."""
+    """Steps 1-4 above for a `FlatParameters` built with `world` (and optionally segments).
+
+    The flat buffer is cut into the segments of `flat.segments`; rank r owns the r-th slice of
+    every segment. `reduce_segment(i)` can run as soon as segment i's gradients are final (the
+    graph step calls it from block backward hooks on a side stream, so the reduce-scatter of late
+    layers overlaps the backward of earlier ones); `finish()` reduces what is left, exchanges the
+    norm, runs AdamW on the owned slices and all-gathers every segment.
+    """
 
     def __init__(
         self,
@@ -101,6 +108,7 @@ class ShardedStep:
         hyper: torch.Tensor,
         ipc: IpcBuffers | None = None,
         timeout_ms: float = 10_000.0,
+        overlap_blocks: int = 64,
     ) -> None:
         if impl not in IMPLS:
             raise ValueError(f"sharded step impl must be one of {IMPLS}, got {impl!r}")
@@ -113,65 +121,103 @@ class ShardedStep:
         self.timeout_ms = timeout_ms
         self.hyper = hyper
         dev = flat.data.device
-        self.shard_len = flat.total // self.world
-        self.shard_off = self.rank * self.shard_len
-        lo, hi = self.shard_off, self.shard_off + self.shard_len
+        # owned slice of every segment: (segment lo, slice length, offset of the slice in the moments)
+        self.owned: list[tuple[int, int, int]] = []
+        moment_off = 0
+        for lo, hi in flat.segments:
+            sl = (hi - lo) // self.world
+            self.owned.append((lo, sl, moment_off))
+            moment_off += sl
+        self.owned_numel = moment_off
         group_of = {id(p): gi for gi, g in enumerate(optimizer.param_groups) for p in g["params"]}
         eps = {g["eps"] for g in optimizer.param_groups}
         if len(eps) != 1:
             raise ValueError("the sharded AdamW needs one eps for all param groups")
         self.eps = float(eps.pop())
-        self.exp_avg = torch.zeros(self.shard_len, dtype=torch.float32, device=dev)
-        self.exp_avg_sq = torch.zeros(self.shard_len, dtype=torch.float32, device=dev)
+        self.exp_avg = torch.zeros(max(moment_off, 1), dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(max(moment_off, 1), dtype=torch.float32, device=dev)
         params, grads, m, v, steps, gidx, shadows = [], [], [], [], [], [], []
-        self.slices: list[tuple[Any, int, int]] = []
+        self.slices: list[tuple[Any, int, int, int]] = []  # (param, a, b, moment offset of a)
         for p, off in zip(flat.params, flat.offsets, strict=True):
-            a, b = max(off, lo), min(off + p.numel(), hi)
-            if a >= b:
-                continue
             if id(p) not in group_of:
                 raise ValueError("every flat parameter must belong to an optimizer param group")
-            params.append(flat.data[a:b])
-            grads.append(flat.grad[a:b])
-            m.append(self.exp_avg[a - lo:b - lo])
-            v.append(self.exp_avg_sq[a - lo:b - lo])
-            steps.append(torch.zeros((), dtype=torch.float32, device=dev))
-            gidx.append(group_of[id(p)])
-            shadows.append(flat.shadow[a:b])
-            self.slices.append((p, a, b))
+            for lo, sl, mo in self.owned:
+                own_lo = lo + self.rank * sl
+                a, b = max(off, own_lo), min(off + p.numel(), own_lo + sl)
+                if a >= b:
+                    continue
+                ma = mo + (a - own_lo)
+                params.append(flat.data[a:b])
+                grads.append(flat.grad[a:b])
+                m.append(self.exp_avg[ma:ma + (b - a)])
+                v.append(self.exp_avg_sq[ma:ma + (b - a)])
+                steps.append(torch.zeros((), dtype=torch.float32, device=dev))
+                gidx.append(group_of[id(p)])
+                shadows.append(flat.shadow[a:b])
+                self.slices.append((p, a, b, ma))
         self._lists = (params, grads, m, v, steps, shadows)
         self._gidx = torch.tensor(gidx, dtype=torch.int32, device=dev)
         self.grad_scale = torch.ones((), dtype=torch.float32, device=dev)
         self.grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
+        self._own_grads = [flat.grad[lo + self.rank * sl: lo + (self.rank + 1) * sl] for lo, sl, _ in self.owned]
+        self._reduced = [False] * len(self.owned)
+        self._seq = 0
         if impl == "p2p":
             if ipc is None or flat.peers is None:
                 raise ValueError("the p2p implementation needs FlatParameters allocated through IpcBuffers")
             self.ipc = ipc
             self.blocks = min(2 * torch.cuda.get_device_properties(dev).multi_processor_count,
                               int(native().comm_max_blocks()))
-            self.partial = torch.zeros(self.blocks, dtype=torch.float32, device=dev)
+            self.overlap_blocks = max(1, min(overlap_blocks, self.blocks))
+            # per-segment slices of the partial sums: the tail segment (0) uses the full grid
+            grids = [self.blocks] + [self.overlap_blocks] * (len(self.owned) - 1)
+            self._partial_off = [sum(grids[:i]) for i in range(len(grids))]
+            self._grids = grids
+            self.partial = torch.zeros(sum(grids), dtype=torch.float32, device=dev)
             self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
             _, self.flag_peers = ipc.allocate(int(native().comm_flag_bytes()) // 4, torch.int32)
-        self.grad_shard = flat.grad[lo:hi]
 
-    def step(self) -> torch.Tensor:
-        """Run after backward on every rank; returns the (device) global gradient norm."""
+    # -- reduce-scatter -------------------------------------------------------------------------
+    def begin(self) -> None:
+        """Start of a step's gradient phase (before backward)."""
+        self._reduced = [False] * len(self.owned)
+        self._seq = 0
+
+    def reduce_segment(self, i: int) -> None:
+        """Reduce-scatter segment i on the current stream (its gradients must be final)."""
+        if self._reduced[i]:
+            return
+        self._reduced[i] = True
+        lo, sl, _ = self.owned[i]
+        if self.impl == "p2p":
+            grid = self._grids[i]
+            part = self.partial[self._partial_off[i]:self._partial_off[i] + grid]
+            # Segments reduced during backward use small CTAs (128 threads, no shared memory) so they
+            # fit on an SM beside a GEMM CTA instead of displacing it.
+            threads = 512 if i == 0 else 128
+            native().zero_reduce_scatter(self.flat.peers["grad"], self.flag_peers, lo + self.rank * sl, sl, part,
+                                         self.epoch, self.rank, self.timeout_ms, self._seq, threads)
+        else:
+            dist.reduce_scatter_tensor(self._own_grads[i], self.flat.grad[lo:lo + self.world * sl], group=self.group)
+        self._seq += 1
+
+    def finish(self) -> torch.Tensor:
+        """Reduce the remaining segments, clip, AdamW on the owned slices, all-gather; returns the norm."""
+        for i in range(len(self.owned) - 1, -1, -1):
+            self.reduce_segment(i)
         params, grads, m, v, steps, shadows = self._lists
         if self.impl == "p2p":
             n = native()
-            n.zero_reduce_scatter(self.flat.peers["grad"], self.flag_peers, self.shard_off, self.shard_len,
-                                  self.partial, self.epoch, self.rank, self.timeout_ms)
             n.zero_norm_exchange(self.flag_peers, self.partial, self.epoch, self.rank, self.max_norm,
                                  self.grad_scale, self.grad_norm, self.timeout_ms)
             if params:
                 adamw_step(params, grads, m, v, steps, self._gidx, self.hyper, self.eps, self.grad_scale, shadows)
-            n.zero_all_gather(self.flat.peers["data"], self.flat.peers["shadow"], self.flag_peers, self.shard_len,
-                              self.flat.bf16_begin, self.flat.total, self.epoch, self.rank, self.blocks, self.timeout_ms)
+            for seq, (lo, sl, _) in enumerate(self.owned):
+                n.zero_all_gather(self.flat.peers["data"], self.flat.peers["shadow"], self.flag_peers, lo, sl,
+                                  self.flat.bf16_begin, self.epoch, self.rank, self.blocks, self.timeout_ms, seq)
             n.zero_advance_epoch(self.epoch)
             return self.grad_norm
-        # NCCL baseline on the same layout (in-place reduce-scatter into the owned slice)
-        dist.reduce_scatter_tensor(self.grad_shard, self.flat.grad, group=self.group)
-        sumsq = grad_sumsq([self.grad_shard])
+        sumsq = grad_sumsq(self._own_grads)
         dist.all_reduce(sumsq, group=self.group)
         norm = sumsq.sqrt() / self.world
         coef = clip_coefficient(norm, self.max_norm) if self.max_norm > 0 else torch.ones_like(norm)
@@ -179,27 +225,43 @@ class ShardedStep:
         self.grad_norm.copy_(norm)
         if params:
             adamw_step(params, grads, m, v, steps, self._gidx, self.hyper, self.eps, self.grad_scale, shadows)
-        dist.all_gather_into_tensor(self.flat.data, self.flat.data[self.shard_off:self.shard_off + self.shard_len],
-                                    group=self.group)
+        for lo, sl, _ in self.owned:
+            seg = self.flat.data[lo:lo + self.world * sl]
+            dist.all_gather_into_tensor(seg, seg[self.rank * sl:(self.rank + 1) * sl], group=self.group)
         self.flat.shadow.copy_(self.flat.data)
         return self.grad_norm
+
+    def step(self) -> torch.Tensor:
+        """Whole gradient phase after backward (no overlap)."""
+        self.begin()
+        return self.finish()
 
     @torch.no_grad()
     def gather_masters(self) -> None:
         """Make every rank's fp32 copy exact (the bf16 region is bf16-rounded off the owner)."""
-        dist.all_gather_into_tensor(self.flat.data, self.flat.data[self.shard_off:self.shard_off + self.shard_len].clone(),
-                                    group=self.group)
+        for lo, sl, _ in self.owned:
+            seg = self.flat.data[lo:lo + self.world * sl]
+            dist.all_gather_into_tensor(seg, seg[self.rank * sl:(self.rank + 1) * sl].clone(), group=self.group)
+
+    @torch.no_grad()
+    def _full_moments(self) -> dict[str, torch.Tensor]:
+        """Whole-buffer moments (flat layout) gathered from every rank's owned slices."""
+        dev = self.flat.data.device
+        out = {}
+        for name, mine in (("exp_avg", self.exp_avg), ("exp_avg_sq", self.exp_avg_sq)):
+            full = torch.zeros(self.flat.total, dtype=torch.float32, device=dev)
+            for lo, sl, mo in self.owned:
+                seg = full[lo:lo + self.world * sl]
+                dist.all_gather_into_tensor(seg, mine[mo:mo + sl].contiguous(), group=self.group)
+            out[name] = full
+        return out
 
     @torch.no_grad()
     def export_state(self, optimizer: torch.optim.Optimizer) -> None:
         """Write whole-parameter AdamW state (torch layout) into `optimizer.state` on every rank."""
         self.gather_masters()
+        full = self._full_moments()
         dev = self.flat.data.device
-        full = {}
-        for name, shard in (("exp_avg", self.exp_avg), ("exp_avg_sq", self.exp_avg_sq)):
-            buf = torch.empty(self.flat.total, dtype=torch.float32, device=dev)
-            dist.all_gather_into_tensor(buf, shard, group=self.group)
-            full[name] = buf
         step = self._lists[4][0].detach().clone() if self._lists[4] else torch.zeros((), device=dev)
         dist.broadcast(step, src=dist.get_global_rank(self.group, 0) if self.group is not None else 0, group=self.group)
         for p, off in zip(self.flat.params, self.flat.offsets, strict=True):
@@ -212,19 +274,18 @@ class ShardedStep:
 
     @torch.no_grad()
     def import_state(self, optimizer: torch.optim.Optimizer) -> bool:
-        """Load the owned slice's moments from whole-parameter state in `optimizer.state` (if any)."""
+        """Load the owned slices' moments from whole-parameter state in `optimizer.state` (if any)."""
         offsets = {id(p): off for p, off in zip(self.flat.params, self.flat.offsets, strict=True)}
         found = False
         steps = self._lists[4]
-        for i, (p, a, b) in enumerate(self.slices):
+        for i, (p, a, b, ma) in enumerate(self.slices):
             state = optimizer.state.get(p)
             if not state or "exp_avg" not in state:
                 continue
             found = True
             off = offsets[id(p)]
-            lo = self.shard_off
-            self.exp_avg[a - lo:b - lo].copy_(state["exp_avg"].reshape(-1)[a - off:b - off])
-            self.exp_avg_sq[a - lo:b - lo].copy_(state["exp_avg_sq"].reshape(-1)[a - off:b - off])
+            self.exp_avg[ma:ma + (b - a)].copy_(state["exp_avg"].reshape(-1)[a - off:b - off])
+            self.exp_avg_sq[ma:ma + (b - a)].copy_(state["exp_avg_sq"].reshape(-1)[a - off:b - off])
             steps[i].copy_(state["step"])
         optimizer.state.clear()  # the shards are the live state now
         return found
