@@ -527,6 +527,7 @@ __global__ void rope_qk_fwd_kernel(const bf16* __restrict__ qkv, const float* __
   if (token >= BN) return;
   const int b = token / N, n = token % N;
   const uint4* src = reinterpret_cast<const uint4*>(qkv + ((size_t)token * 3 + which) * HD);
+#pragma unroll 8
   for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(xs)[c] = src[c];
   const float* ang = angles + (size_t)b * angle_bstride + (size_t)n * P;
   rope_roles_warp(roles, pairs, P, D, cs, sn, ang);
@@ -572,9 +573,11 @@ __global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16*
   if (active && !(P == 0 && which == 1)) {  // without RoPE the dk slot is already final
     if (which == 0) {
       const float4* g4 = reinterpret_cast<const float4*>(dq_acc + (size_t)token * HD);
+#pragma unroll 8
       for (int c = lane; c < HD / 4; c += 32) reinterpret_cast<float4*>(gs)[c] = g4[c];
     } else {
       const uint4* g8 = reinterpret_cast<const uint4*>(dst);
+#pragma unroll 4
       for (int c = lane; c < HD / 8; c += 32) {
         const uint4 u = g8[c];
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -587,6 +590,7 @@ __global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16*
     }
     if (P > 0) {
       const uint4* y8 = reinterpret_cast<const uint4*>(y + (size_t)token * y_token_stride + (size_t)which * HD);
+#pragma unroll 8
       for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(ys)[c] = y8[c];
       rope_roles_warp(roles, pairs, P, D, cs, sn, angles + (size_t)b * angle_bstride + (size_t)n * P);
     } else {

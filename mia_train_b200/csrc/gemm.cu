@@ -91,8 +91,11 @@ struct GemmSmem {
 //   kEpiAll    everything (single-CTA kernel)
 enum Epi : int { kEpiPlain = 0, kEpiGelu = 1, kEpiDGelu = 2, kEpiAll = 3 };
 
+// `side`: when non-null, the chunk's 32 bf16 of the GELU' input (kEpiDGelu) or of the residual
+// (kEpiPlain), loaded ahead by the caller so their latency overlaps the previous chunk.
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n, const uint32_t (&r)[32],
+                                               const uint4* side = nullptr) {
   if (m >= p.M || n >= p.N) return;
   float v[32];
 #pragma unroll
@@ -149,7 +152,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
       const uint4* src = reinterpret_cast<const uint4*>(p.aux + row + n);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        uint4 u = __ldg(src + q);
+        uint4 u = side != nullptr ? side[q] : __ldg(src + q);
         uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
@@ -182,7 +185,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
       const uint4* src = reinterpret_cast<const uint4*>(p.residual + row + n);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        uint4 u = __ldg(src + q);
+        uint4 u = side != nullptr ? side[q] : __ldg(src + q);
         uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
@@ -626,11 +629,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_half * (BN / 2);
       uint32_t r[2][32];
       tmem_ld_32x32b_x32(t_row, r[0]);
+      // side input (GELU' pre-activation or residual) prefetched one chunk ahead
+      const __nv_bfloat16* side = EPI == kEpiDGelu ? p.aux : (EPI == kEpiPlain ? p.residual : nullptr);
+      const bool side_ok = side != nullptr && m < p.M && n0 + kChunks * 32 <= p.N;
+      uint4 sbuf[2][4];
+      if (side_ok) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sbuf[0][q] = __ldg(reinterpret_cast<const uint4*>(side + (size_t)m * p.N + n0) + q);
+      }
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
+        if (side_ok && c + 1 < kChunks) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            sbuf[(c + 1) & 1][q] = __ldg(reinterpret_cast<const uint4*>(side + (size_t)m * p.N + n0 + (c + 1) * 32) + q);
+        }
         tmem_ld_wait_regs(r[c & 1]);
         if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, r[(c + 1) & 1]);
-        epilogue_chunk<EPI>(p, m, n0 + c * 32, r[c & 1]);
+        epilogue_chunk<EPI>(p, m, n0 + c * 32, r[c & 1], side_ok ? sbuf[c & 1] : nullptr);
       }
       tc_fence_before();
       __syncwarp();
