@@ -516,10 +516,11 @@ __global__ void rope_qk_fwd_kernel(const bf16* __restrict__ qkv, const float* __
   const int HD = H * D;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int slot = warp;  // (token in CTA) * 2 + which
-  const size_t per_warp = (size_t)HD * 2 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16;
+  const size_t per_warp = (size_t)HD * 4 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16;
   uint8_t* base = smem_raw + slot * ((per_warp + 15) / 16 * 16);
   bf16* xs = reinterpret_cast<bf16*>(base);
-  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 2);
+  bf16* os = xs + HD;
+  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 4);
   float* sn = cs + P;
   RopeRole* roles = reinterpret_cast<RopeRole*>(sn + P);
   const int token = blockIdx.x * kRopeTokensPerCta + warp / 2;
@@ -531,21 +532,17 @@ __global__ void rope_qk_fwd_kernel(const bf16* __restrict__ qkv, const float* __
   for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(xs)[c] = src[c];
   const float* ang = angles + (size_t)b * angle_bstride + (size_t)n * P;
   rope_roles_warp(roles, pairs, P, D, cs, sn, ang);
-  uint4* dst = reinterpret_cast<uint4*>(qk + ((size_t)token * 2 + which) * HD);
-  for (int c = lane; c < HD / 8; c += 32) {
-    const int h = (c * 8) / D, d0 = (c * 8) % D;
-    const bf16* x = xs + h * D;
-    float o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = d0 + j;
-      const float xi = __bfloat162float(x[d]);
-      const RopeRole r = roles[d];
-      o[j] = r.partner >= 0 ? xi * cs[r.pair] + r.sign * __bfloat162float(x[r.partner]) * sn[r.pair] : xi;
-    }
-    dst[c] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
-                        pack_bf16x2(o[6], o[7]));
+  // element e = lane + 32 j: consecutive lanes touch consecutive channels (no bank conflicts)
+  for (int e = lane; e < HD; e += 32) {
+    const int d = e % D;
+    const RopeRole r = roles[d];
+    const float xi = __bfloat162float(xs[e]);
+    const float o = r.partner >= 0 ? xi * cs[r.pair] + r.sign * __bfloat162float(xs[e - d + r.partner]) * sn[r.pair] : xi;
+    os[e] = __float2bfloat16_rn(o);
   }
+  __syncwarp();
+  uint4* dst = reinterpret_cast<uint4*>(qk + ((size_t)token * 2 + which) * HD);
+  for (int c = lane; c < HD / 8; c += 32) dst[c] = reinterpret_cast<const uint4*>(os)[c];
 }
 
 // dq_acc (B, N, H, D) fp32; dqkv (B, N, 3, H, D) with the rotated-space dk in slot 1 and dv in
@@ -557,11 +554,12 @@ __global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16*
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int HD = H * D;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const size_t per_warp = (size_t)HD * 4 + (size_t)HD * 2 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16;
+  const size_t per_warp = (size_t)HD * 4 + (size_t)HD * 4 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16;
   uint8_t* base = smem_raw + warp * ((per_warp + 15) / 16 * 16);
   float* gs = reinterpret_cast<float*>(base);
   bf16* ys = reinterpret_cast<bf16*>(base + (size_t)HD * 4);
-  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 6);
+  bf16* os = ys + HD;
+  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 8);
   float* sn = cs + P;
   float* dpart = sn + P;
   RopeRole* roles = reinterpret_cast<RopeRole*>(dpart + P);
@@ -596,24 +594,18 @@ __global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16*
     } else {
       __syncwarp();
     }
-    for (int c = lane; c < HD / 8; c += 32) {
-      const int h = (c * 8) / D, d0 = (c * 8) % D;
-      const float* g = gs + h * D;
-      float o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int d = d0 + j;
-        if (P > 0) {
-          const RopeRole r = roles[d];
-          // inverse rotation: the transpose of [[c, -s], [s, c]] acting on (first, second)
-          o[j] = r.partner >= 0 ? g[d] * cs[r.pair] - r.sign * g[r.partner] * sn[r.pair] : g[d];
-        } else {
-          o[j] = g[d];
-        }
+    for (int e = lane; e < HD; e += 32) {
+      const int d = e % D;
+      float o = gs[e];
+      if (P > 0) {
+        const RopeRole r = roles[d];
+        // inverse rotation: the transpose of [[c, -s], [s, c]] acting on (first, second)
+        if (r.partner >= 0) o = gs[e] * cs[r.pair] - r.sign * gs[e - d + r.partner] * sn[r.pair];
       }
-      reinterpret_cast<uint4*>(dst)[c] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                                    pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+      os[e] = __float2bfloat16_rn(o);
     }
+    __syncwarp();
+    for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(os)[c];
     if (dangles != nullptr && P > 0) {
       for (int p = lane; p < P; p += 32) {
         const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
@@ -628,7 +620,7 @@ __global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16*
   if (active && dangles != nullptr && P > 0 && which == 0) {
     // partner warp (the token's k) is warp + 1, same CTA
     const uint8_t* kbase = smem_raw + (warp + 1) * ((per_warp + 15) / 16 * 16);
-    const float* kpart = reinterpret_cast<const float*>(kbase + (size_t)HD * 6) + 2 * P;
+    const float* kpart = reinterpret_cast<const float*>(kbase + (size_t)HD * 8) + 2 * P;
     for (int p = lane; p < P; p += 32) dangles[(size_t)token * P + p] = dpart[p] + kpart[p];
   }
 }
@@ -716,12 +708,12 @@ void attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
 }
 
 static size_t rope_fwd_smem(int H, int D, int P) {
-  const size_t per_warp = ((size_t)H * D * 2 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
+  const size_t per_warp = ((size_t)H * D * 4 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
   return per_warp * 2 * kRopeTokensPerCta;
 }
 
 static size_t rope_bwd_smem(int H, int D, int P) {
-  const size_t per_warp = ((size_t)H * D * 6 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
+  const size_t per_warp = ((size_t)H * D * 8 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
   return per_warp * 2 * kRopeTokensPerCta;
 }
 
