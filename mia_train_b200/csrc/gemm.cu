@@ -6,18 +6,17 @@
 // (K x N). The transposed reads serve the backward pass: dX = dY W reads W N-major and
 // dW = dY^T X reads both operands M/N-major, so no transpose is ever materialised.
 //
-// CTA = 6 warps, one CTA per SM, persistent over output tiles of 128 x BN:
+// CTA = 2 + kEpiWarps warps, one CTA per SM, persistent over output tiles of 128 x BN:
 //   warp 0      TMA producer: one thread streams 128x64 A and BNx64 B tiles (128-byte swizzle)
 //               into a STAGES-deep shared-memory ring, one mbarrier per stage.
 //   warp 1      MMA issuer: allocates 2*BN TMEM columns (two fp32 accumulators), one thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) per 16-wide K slice and commits each consumed stage
 //               back to the producer and each finished tile to the epilogue.
-//   warps 2..9  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32*(w%4)..+31,
-//               i.e. output rows; warps 2-5 take the first half of the tile's columns, 6-9 the
-//               second), bias / GELU (keeping the pre-activation) / GELU' / LayerScale / residual /
-//               accumulate-into-output, then 16-byte stores. TMEM loads are double-buffered so the
-//               next 32 columns are in flight while the current ones are processed. While the
-//               epilogue drains one accumulator the MMA warp fills the other.
+//   warps 2..   epilogue (kEpiWarps of them): tcgen05.ld of the accumulator (warp w owns TMEM
+//               lanes 32*(w%4)..+31, i.e. output rows; each group of four warps takes one part of
+//               the tile's columns), bias / GELU (keeping the pre-activation) / GELU' / LayerScale / residual /
+//               accumulate-into-output, then 16-byte stores. Latency is hidden across the epilogue
+//               warps. While the epilogue drains one accumulator the MMA warp fills the other.
 //
 // All waits are bounded (see common.cuh); on a timeout the kernel records an error code, drains
 // the copies and MMAs it issued, frees its tensor memory and returns.
@@ -37,7 +36,9 @@ namespace mia {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 320;  // producer warp, MMA warp, 8 epilogue warps
+constexpr int kEpiWarps = 16;                   // epilogue warps: 4 per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;   // producer warp, MMA warp, epilogue warps
+constexpr int kColParts = kEpiWarps / 4;        // the tile's columns are split this many ways
 constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
 
 enum Act : int { kActNone = 0, kActGelu = 1, kActDGelu = 2 };
@@ -91,11 +92,11 @@ struct GemmSmem {
 //   kEpiAll    everything (single-CTA kernel)
 enum Epi : int { kEpiPlain = 0, kEpiGelu = 1, kEpiDGelu = 2, kEpiAll = 3 };
 
-// `side`: when non-null, the chunk's 32 bf16 of the GELU' input (kEpiDGelu) or of the residual
-// (kEpiPlain), loaded ahead by the caller so their latency overlaps the previous chunk.
+// `side` (when `use_side`): the chunk's 32 bf16 of the GELU' input (kEpiDGelu) or of the residual
+// (kEpiPlain), loaded by the caller while its TMEM load is in flight.
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n, const uint32_t (&r)[32],
-                                               const uint4* side = nullptr) {
+                                               bool use_side, const uint4 (&side)[4]) {
   if (m >= p.M || n >= p.N) return;
   float v[32];
 #pragma unroll
@@ -152,7 +153,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
       const uint4* src = reinterpret_cast<const uint4*>(p.aux + row + n);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        uint4 u = side != nullptr ? side[q] : __ldg(src + q);
+        uint4 u = use_side ? side[q] : __ldg(src + q);
         uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
@@ -185,7 +186,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
       const uint4* src = reinterpret_cast<const uint4*>(p.residual + row + n);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        uint4 u = side != nullptr ? side[q] : __ldg(src + q);
+        uint4 u = use_side ? side[q] : __ldg(src + q);
         uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
@@ -247,6 +248,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n
   }
 }
 
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m, int n, const uint32_t (&r)[32]) {
+  const uint4 none[4] = {};
+  epilogue_chunk<EPI>(p, m, n, r, false, none);
+}
+
 template <int BN, bool A_MN, bool B_MN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -275,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 256);
+      mbar_init(&tempty_bar[a], 32 * kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -399,8 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue warps 2..9
     const int lane_group = warp % 4;         // TMEM lanes 32*lane_group .. +31
-    const int col_half = (warp - 2) / 4;     // which half of the tile's columns
-    constexpr int kChunks = BN / 64;         // 32-column chunks per half
+    const int col_part = (warp - 2) / 4;     // which part of the tile's columns
+    constexpr int kPartCols = BN / kColParts;
+    constexpr int kChunks = kPartCols / 32;  // 32-column chunks per part
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
@@ -408,16 +416,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const TileCoord tc = tile_coord(p, tile, BN, (p.K + kBK - 1) / kBK);
       const int m0 = tc.m0;
-      const int n0 = tc.n0 + col_half * (BN / 2);
+      const int n0 = tc.n0 + col_part * kPartCols;
       const int m = m0 + lane_group * 32 + lane;
-      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_half * (BN / 2);
-      uint32_t r[2][32];
-      tmem_ld_32x32b_x32(t_row, r[0]);
+      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_part * kPartCols;
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
-        tmem_ld_wait_regs(r[c & 1]);
-        if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, r[(c + 1) & 1]);
-        epilogue_chunk<kEpiAll>(p, m, n0 + c * 32, r[c & 1]);
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait_regs(r);
+        epilogue_chunk<kEpiAll>(p, m, n0 + c * 32, r);
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -492,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 16);  // 8 epilogue warps x 2 CTAs (even CTA only)
+      mbar_init(&tempty_bar[a], 2 * kEpiWarps);  // every epilogue warp of both CTAs (even CTA only)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -616,8 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue warps 2..9 (both CTAs, own 128 rows)
     const int lane_group = warp % 4;
-    const int col_half = (warp - 2) / 4;
-    constexpr int kChunks = BN / 64;
+    const int col_part = (warp - 2) / 4;
+    constexpr int kPartCols = BN / kColParts;
+    constexpr int kChunks = kPartCols / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < p.num_tiles; tile += num_pairs) {
@@ -625,28 +633,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const TileCoord tc = pair_tile_coord(p, tile, BN, num_k);
       const int m = tc.m0 + 128 * (int)rank + lane_group * 32 + lane;
-      const int n0 = tc.n0 + col_half * (BN / 2);
-      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_half * (BN / 2);
-      uint32_t r[2][32];
-      tmem_ld_32x32b_x32(t_row, r[0]);
-      // side input (GELU' pre-activation or residual) prefetched one chunk ahead
+      const int n0 = tc.n0 + col_part * kPartCols;
+      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_part * kPartCols;
+      // With kEpiWarps warps per CTA the TMEM and side-input latencies are hidden across warps, so
+      // each warp keeps one chunk in flight: its accumulator columns and, loaded while the TMEM
+      // load is pending, the side input (GELU' pre-activation or residual).
       const __nv_bfloat16* side = EPI == kEpiDGelu ? p.aux : (EPI == kEpiPlain ? p.residual : nullptr);
       const bool side_ok = side != nullptr && m < p.M && n0 + kChunks * 32 <= p.N;
-      uint4 sbuf[2][4];
-      if (side_ok) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) sbuf[0][q] = __ldg(reinterpret_cast<const uint4*>(side + (size_t)m * p.N + n0) + q);
-      }
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
-        if (side_ok && c + 1 < kChunks) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        uint4 sbuf[4] = {};
+        if (side_ok) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            sbuf[(c + 1) & 1][q] = __ldg(reinterpret_cast<const uint4*>(side + (size_t)m * p.N + n0 + (c + 1) * 32) + q);
+            sbuf[q] = __ldg(reinterpret_cast<const uint4*>(side + (size_t)m * p.N + n0 + c * 32) + q);
         }
-        tmem_ld_wait_regs(r[c & 1]);
-        if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, r[(c + 1) & 1]);
-        epilogue_chunk<EPI>(p, m, n0 + c * 32, r[c & 1], side_ok ? sbuf[c & 1] : nullptr);
+        tmem_ld_wait_regs(r);
+        epilogue_chunk<EPI>(p, m, n0 + c * 32, r, side_ok, sbuf);
       }
       tc_fence_before();
       __syncwarp();
@@ -808,9 +813,14 @@ static int choose_bn(int M, int N, int sms) {
   return eff(256) >= 0.85 * eff(128) ? 256 : 128;
 }
 
-// Same rule for 256 x BN tiles over CTA pairs.
+// Same rule for 256 x BN tiles over CTA pairs. MIA_GEMM_BN=128|256 pins the choice (tuning runs).
 static int choose_bn_pair(int M, int N, int sms) {
+  static const int forced = [] {
+    const char* v = std::getenv("MIA_GEMM_BN");
+    return v == nullptr ? 0 : std::atoi(v);
+  }();
   if (N <= 128) return 128;
+  if (forced == 128 || forced == 256) return forced;
   const int pairs = sms / 2;
   auto eff = [&](int bn) {
     const long tiles = (long)((M + 255) / 256) * ((N + bn - 1) / bn);
@@ -887,7 +897,18 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
       (d.scalar_type() == at::kFloat || gamma.has_value() || residual.has_value() || accumulate))
     pair_ok = false;
   const bool use_pair = pair_mode() != 0 && M >= 256 && pair_ok;
-  const int bn = use_pair ? choose_bn_pair((int)M, (int)N, num_sms(device)) : choose_bn((int)M, (int)N, num_sms(device));
+  int bn = use_pair ? choose_bn_pair((int)M, (int)N, num_sms(device)) : choose_bn((int)M, (int)N, num_sms(device));
+  static const bool bn_pinned = std::getenv("MIA_GEMM_BN") != nullptr;
+  if (use_pair && !bn_pinned && N > 128) {
+    // Measured per shape on the ViT-L MAE training step: activation epilogues are the slow part of
+    // their GEMMs, so more, narrower tiles win; split-K weight gradients (fp32 out) prefer the wider
+    // tile; plain GEMMs with a short K are epilogue-heavy too.
+    const bool plain_f32_out = d.scalar_type() == at::kFloat && !bias.has_value() && !gamma.has_value() &&
+                               !residual.has_value() && act == kActNone;
+    if (act != kActNone) bn = 128;
+    else if (plain_f32_out) bn = 256;
+    else if (K <= 512) bn = 128;
+  }
   // Split K when the output alone cannot fill the SMs and nothing in the epilogue needs the full
   // sum (the weight-gradient GEMMs: tokens are K, the output is a small fp32 matrix).
   p.splits = 1;
