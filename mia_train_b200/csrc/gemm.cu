@@ -844,7 +844,12 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   TORCH_CHECK(K == Kb, "gemm: K mismatch ", K, " vs ", Kb);
   TORCH_CHECK(d.size(0) == M && d.size(1) == N, "gemm: output shape mismatch");
   TORCH_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "gemm: bf16 or fp32 output");
-  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && M % 8 == 0, "gemm: M, N, K must be multiples of 8");
+  // TMA needs 16-byte aligned rows: the contiguous extent of each operand (K for K-major, M or N
+  // for MN-major) and the output's N must be multiples of 8 elements; the other extents are free
+  // (out-of-range rows are zero-filled on load and skipped on store).
+  TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
+  TORCH_CHECK(a_kmajor ? K % 8 == 0 : M % 8 == 0, "gemm: A's contiguous extent must be a multiple of 8");
+  TORCH_CHECK(!b_kmajor || K % 8 == 0, "gemm: B's contiguous extent must be a multiple of 8");
   TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm: leading dimensions must be multiples of 8");
   TORCH_CHECK(aligned16(a.data_ptr()) && aligned16(b.data_ptr()) && aligned16(d.data_ptr()),
               "gemm: 16-byte aligned base addresses expected");

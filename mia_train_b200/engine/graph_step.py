@@ -307,6 +307,9 @@ class CapturedStep:
                 if len(segs) == 1:
                     self._block_hooks.append(block.register_full_backward_hook(self._make_hook(segs.pop())))
         self.static_batch = _to_static(example_batch, self.device)
+        self._staging: Any = None
+        self._copy_stream: torch.cuda.Stream | None = None
+        self._prefetched = False
         self.static_metrics: dict[str, torch.Tensor] = {}
         self.eager_steps = eager_steps
         self.capture = capture
@@ -385,10 +388,34 @@ class CapturedStep:
     def load_batch(self, batch: Any) -> None:
         _copy_into(self.static_batch, batch)
 
+    def prefetch(self, batch: Any) -> None:
+        """Start copying the next step's (pinned host) batch to the device on a side stream.
+
+        The copy overlaps the step that is running; the next `__call__()` without a batch waits for
+        it and moves it into the captured input buffers with one device-to-device copy.
+        """
+        if self._staging is None:
+            self._staging = _to_static(batch, self.device)
+            self._copy_stream = torch.cuda.Stream(self.device)
+        self._copy_stream.wait_stream(torch.cuda.current_stream(self.device))  # staging is free again
+        with torch.cuda.stream(self._copy_stream):
+            _copy_into(self._staging, batch)
+        self._prefetched = True
+
+    def wait_prefetch(self) -> None:
+        """Make the current stream wait for an outstanding `prefetch` copy."""
+        if self._copy_stream is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
+
     def __call__(self, batch: Any | None = None) -> dict[str, torch.Tensor]:
-        """Run one step on `batch` (host tensors are copied in; None reuses the static batch)."""
+        """Run one step on `batch` (host tensors are copied in; None reuses the static batch or
+        takes the batch handed to `prefetch`)."""
         if batch is not None:
             self.load_batch(batch)
+        elif self._prefetched:
+            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
+            _copy_into(self.static_batch, self._staging)
+            self._prefetched = False
         self.calls += 1
         if not self.capture or self.calls <= self.eager_steps:
             self._store(self._body())

@@ -60,6 +60,23 @@ def test_gemm_layouts(a_k, b_k, mnk, pair_mode):
     _no_errors()
 
 
+@pytest.mark.parametrize("b_k", [True, False])
+def test_gemm_ragged_rows(b_k, pair_mode):
+    """M not a multiple of 8 (token counts like B * (prefix + patches)), K-major A."""
+    m, n, k = 1034, 384, 264
+    torch.manual_seed(2)
+    a = torch.randn(m, k, device=DEV).bfloat16()
+    b = torch.randn(n, k, device=DEV).bfloat16()
+    bias = torch.randn(n, device=DEV)
+    out = gemm(a, b if b_k else b.t().contiguous(), b_kmajor=b_k, bias=bias, out_dtype=torch.float32)
+    _close(out, a.float() @ b.float().t() + bias, rel=1e-2, atol=1e-2 * math.sqrt(k))
+    # weight-gradient form: the 1034 tokens are the K dimension, both operands read M/N-major
+    dy = torch.randn(m, n, device=DEV).bfloat16()
+    dw = gemm(dy, a, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32)
+    _close(dw, dy.float().t() @ a.float(), rel=1e-2, atol=1e-2 * math.sqrt(m))
+    _no_errors()
+
+
 def test_gemm_epilogues(pair_mode):
     torch.manual_seed(1)
     m, n, k = 512, 768, 320
