@@ -21,6 +21,7 @@
 
 #include <utility>
 
+#include "attention_tc.h"
 #include "common.cuh"
 
 namespace mia {
@@ -52,10 +53,6 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
                : "r"(smem_u32(p)));
 }
 
-// Element strides of a (B, H, N, D) view whose rows of D are contiguous.
-struct Strides3 {
-  int64_t b, h, n;
-};
 
 // 2^x with the hardware approximation (relative error ~2^-22, flushes denormals), for softmax terms.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -236,26 +233,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const bf16* __re
   }
 }
 
-// delta[b, h, i] = sum_d dO[b, i, h, d] * O[b, i, h, d]
+// delta[b, h, i] = sum_d dO[b, i, h, d] * O[b, i, h, d]. One thread per (b, i, h) row in memory
+// order, so a warp reads 32 consecutive rows with 16-byte loads.
 template <int D>
 __global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout, float* __restrict__ delta,
                                   int H, int N, int rows) {
-  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-  const int lane = threadIdx.x % 32;
-  if (warp_global >= rows) return;
-  const int b = warp_global / (H * N);
-  const int rem = warp_global % (H * N);
-  const int h = rem / N, i = rem % N;
-  const size_t off = (((size_t)b * N + i) * H + h) * D;
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const uint4* a4 = reinterpret_cast<const uint4*>(o + (size_t)row * D);
+  const uint4* c4 = reinterpret_cast<const uint4*>(dout + (size_t)row * D);
   float s = 0.f;
-  for (int d = lane * 2; d < D; d += 64) {
-    const uint32_t a = *reinterpret_cast<const uint32_t*>(o + off + d);
-    const uint32_t c = *reinterpret_cast<const uint32_t*>(dout + off + d);
-    s += bf16_lo(a) * bf16_lo(c) + bf16_hi(a) * bf16_hi(c);
-  }
 #pragma unroll
-  for (int x = 16; x > 0; x >>= 1) s += __shfl_xor_sync(0xffffffffu, s, x);
-  if (lane == 0) delta[((size_t)b * H + h) * N + i] = s;
+  for (int i = 0; i < D / 8; ++i) {
+    const uint4 a = a4[i], c = c4[i];
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wc[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += bf16_lo(wa[j]) * bf16_lo(wc[j]) + bf16_hi(wa[j]) * bf16_hi(wc[j]);
+  }
+  const int h = row % H;
+  const int bn = row / H;
+  const int b = bn / N, i = bn % N;
+  delta[((size_t)b * H + h) * N + i] = s;
 }
 
 template <int D>
@@ -639,6 +637,8 @@ static constexpr float kLog2e = 1.4426950408889634f;
 // Strides of a (B, H, N, D) tensor and of a (B, N, H, D) view presented as (B, H, N, D).
 static Strides3 bhnd_strides(const torch::Tensor& t) { return Strides3{t.stride(0), t.stride(1), t.stride(2)}; }
 static Strides3 bnhd_strides(const torch::Tensor& t) { return Strides3{t.stride(0), t.stride(2), t.stride(1)}; }
+// Strides of a contiguous (B, N, H, D) buffer (e.g. dO) presented as (B, H, N, D).
+static Strides3 bnhd_contiguous(int N, int H, int D) { return Strides3{(int64_t)N * H * D, D, (int64_t)H * D}; }
 
 void attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse, double scale) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
@@ -648,6 +648,9 @@ void attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
   c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (Nq == 0) return;
+  if (attention_fwd_tc(q, k, v, bhnd_strides(q), bhnd_strides(k), bhnd_strides(v), B, H, Nq, Nk, D, o, lse,
+                       (float)scale * kLog2e))
+    return;
   DISPATCH_HEAD_DIM(D, [&] {
     constexpr int S = HD + 8;
     const size_t smem = (size_t)(kAttnBlockM + 4 * kAttnBlockN) * S * 2;
@@ -673,10 +676,14 @@ static void attention_bwd_core(torch::Tensor q, torch::Tensor k, torch::Tensor v
   C10_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * 4, stream));
   DISPATCH_HEAD_DIM(D, [&] {
     const int rows = B * H * Nq;
-    attn_delta_kernel<HD><<<(rows * 32 + 255) / 256, 256, 0, stream>>>(
+    attn_delta_kernel<HD><<<(rows + 255) / 256, 256, 0, stream>>>(
         reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
         delta.data_ptr<float>(), H, Nq, rows);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    if (attention_bwd_tc(q, k, v, dout, bhnd_strides(q), bhnd_strides(k), bhnd_strides(v), bnhd_contiguous(Nq, H, D),
+                         lse, delta, dq_acc, bhnd_strides(dq_acc), dk, bhnd_strides(dk), dv, bhnd_strides(dv), B, H,
+                         Nq, Nk, D, (float)scale))
+      return;
     constexpr int S = HD + 8;
     const size_t smem = (size_t)(2 * kAttnBlockN + 2 * kAttnBlockM) * S * 2 + (size_t)kAttnBlockN * (kAttnBlockM + 8) * 2 +
                         2 * kAttnBlockM * 4;
@@ -767,6 +774,9 @@ void attention_fwd_strided(torch::Tensor q, torch::Tensor k, torch::Tensor v, to
   c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (Nq == 0) return;
+  if (attention_fwd_tc(q, k, v, bnhd_strides(q), bnhd_strides(k), bnhd_strides(v), B, H, Nq, Nk, D, o, lse,
+                       (float)scale * kLog2e))
+    return;
   DISPATCH_HEAD_DIM(D, [&] {
     constexpr int S = HD + 8;
     const size_t smem = (size_t)(kAttnBlockM + 4 * kAttnBlockN) * S * 2;
@@ -802,10 +812,14 @@ void rope_attention_bwd_packed(torch::Tensor q, torch::Tensor k, torch::Tensor v
   auto delta = torch::empty({B, H, N}, q.options().dtype(at::kFloat));
   DISPATCH_HEAD_DIM(D, [&] {
     const int rows = B * H * N;
-    attn_delta_kernel<HD><<<(rows * 32 + 255) / 256, 256, 0, stream>>>(
+    attn_delta_kernel<HD><<<(rows + 255) / 256, 256, 0, stream>>>(
         reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
         delta.data_ptr<float>(), H, N, rows);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    if (attention_bwd_tc(q, k, v, dout, bnhd_strides(q), bnhd_strides(k), bnhd_strides(v), bnhd_contiguous(N, H, D),
+                         lse, delta, dq_acc, bnhd_strides(dq_acc), dk_view, bnhd_strides(dk_view), dv_view,
+                         bnhd_strides(dv_view), B, H, N, N, D, (float)scale))
+      return;
     constexpr int S = HD + 8;
     const size_t smem = (size_t)(2 * kAttnBlockN + 2 * kAttnBlockM) * S * 2 + (size_t)kAttnBlockN * (kAttnBlockM + 8) * 2 +
                         2 * kAttnBlockM * 4;
@@ -890,7 +904,7 @@ int noalloc_launch(const mia::bf16* q, const mia::bf16* k, const mia::bf16* v, c
   float* delta = scratch + dq_elems;
   if (cudaMemsetAsync(dq_acc, 0, dq_elems * sizeof(float), stream) != cudaSuccess) return MIA_NOALLOC_ERR_CUDA;
   const int rows = B * H * Nq;
-  attn_delta_kernel<D><<<(rows * 32 + 255) / 256, 256, 0, stream>>>(o, dout, delta, H, Nq, rows);
+  attn_delta_kernel<D><<<(rows + 255) / 256, 256, 0, stream>>>(o, dout, delta, H, Nq, rows);
   constexpr int S = D + 8;
   const size_t smem = (size_t)(2 * kAttnBlockN + 2 * kAttnBlockM) * S * 2 + (size_t)kAttnBlockN * (kAttnBlockM + 8) * 2 +
                       2 * kAttnBlockM * 4;

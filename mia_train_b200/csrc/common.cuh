@@ -106,6 +106,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 4-D tile load (coordinates innermost first), no multicast.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -259,6 +269,23 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
   d |= (uint64_t)2 << 61;  // SWIZZLE_128B
   return d;
 }
+
+// Same, with the swizzle chosen by the row width in bytes: 128 -> SWIZZLE_128B (2), 64 -> SWIZZLE_64B (4).
+template <int kRowBytes>
+__device__ __forceinline__ uint64_t make_sdesc_sw(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  static_assert(kRowBytes == 128 || kRowBytes == 64, "swizzle width");
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(kRowBytes == 128 ? 2 : 4) << 61;
+  return d;
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy (tensor core
+// operand reads, TMA); issued before the barrier arrive that hands the data to an MMA issuer.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }

@@ -391,3 +391,88 @@ def test_gemm_split_k_weight_gradient(mnk, pair_mode):
     fresh = gemm(dy, x, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32)
     _close(fresh, dy.float().t() @ x.float(), rel=1e-2, atol=1e-2 * math.sqrt(k))
     _no_errors()
+
+
+@pytest.fixture(params=[0, 1], ids=["warp_mma", "tcgen05"])
+def tc_attention(request):
+    from mia_train_b200.ops._native import native
+
+    previous = native().tc_attention_mode()
+    native().set_tc_attention_mode(request.param)
+    yield request.param
+    native().set_tc_attention_mode(previous)
+
+
+@pytest.mark.parametrize(
+    "b,nq,nk,h,d",
+    [(2, 128, 128, 4, 64), (1, 1, 1, 2, 64), (2, 77, 200, 3, 32), (1, 513, 513, 2, 32), (2, 300, 1000, 2, 64),
+     (16, 128, 128, 16, 64)],
+)
+def test_attention_forward_paths(b, nq, nk, h, d, tc_attention):
+    """Both forward kernels against fp32 SDPA, incl. ragged query / key tails and a key count
+    that is not a multiple of the key block; the tcgen05 path must actually launch."""
+    from mia_train_b200.ops._native import native
+
+    torch.manual_seed(11)
+    q = torch.randn(b, h, nq, d, device=DEV).bfloat16()
+    k = torch.randn(b, h, nk, d, device=DEV).bfloat16()
+    v = torch.randn(b, h, nk, d, device=DEV).bfloat16()
+    o = torch.empty(b, nq, h, d, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(b, h, nq, device=DEV)
+    before = native().tc_attention_launches()
+    native().attention_fwd(q, k, v, o, lse, d**-0.5)
+    torch.cuda.synchronize()
+    assert native().tc_attention_launches() - before == tc_attention
+    ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), scale=d**-0.5)
+    _close(o, ref.transpose(1, 2))
+    s = (q.float() @ k.float().transpose(-1, -2)) * d**-0.5
+    ref_lse = torch.logsumexp(s, dim=-1) / math.log(2.0)
+    torch.testing.assert_close(lse, ref_lse, atol=2e-2, rtol=1e-3)
+    _no_errors()
+
+
+@pytest.mark.parametrize("b,n,h,d", [(2, 128, 16, 64), (2, 512, 16, 32), (3, 70, 4, 64)])
+def test_attention_packed_views(b, n, h, d, tc_attention):
+    """Strided q / k / v straight out of a packed (B, N, 3, H, D) projection, forward and backward."""
+    from mia_train_b200.ops import attention as attn_ops
+
+    torch.manual_seed(12)
+    qkv = torch.randn(b, n, 3, h, d, device=DEV).bfloat16().requires_grad_(True)
+    out = attn_ops.rope_attention(qkv, None, None, d**-0.5)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    qkv32 = qkv.detach().float().requires_grad_(True)
+    q, k, v = (qkv32[:, :, i].transpose(1, 2) for i in range(3))
+    ref = F.scaled_dot_product_attention(q, k, v, scale=d**-0.5).transpose(1, 2)
+    ref.reshape(out.shape).backward(dout.float())
+    _close(out.reshape(ref.shape), ref)
+    _close(qkv.grad, qkv32.grad, rel=3e-2, atol=3e-2)
+    _no_errors()
+
+
+@pytest.mark.parametrize(
+    "b,nq,nk,h,d", [(2, 128, 128, 4, 64), (2, 77, 200, 3, 32), (1, 513, 513, 2, 32), (2, 300, 260, 2, 64), (1, 1, 1, 1, 64)]
+)
+def test_attention_backward_paths(b, nq, nk, h, d, tc_attention):
+    """Both backward kernels (dq, dk, dv) against fp32 autograd through SDPA, ragged tails incl."""
+    from mia_train_b200.ops._native import native
+
+    torch.manual_seed(13)
+    q = torch.randn(b, h, nq, d, device=DEV).bfloat16()
+    k = torch.randn(b, h, nk, d, device=DEV).bfloat16()
+    v = torch.randn(b, h, nk, d, device=DEV).bfloat16()
+    o = torch.empty(b, nq, h, d, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(b, h, nq, device=DEV)
+    native().attention_fwd(q, k, v, o, lse, d**-0.5)
+    dout = torch.randn(b, nq, h, d, device=DEV).bfloat16()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    before = native().tc_attention_launches()
+    native().attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, d**-0.5)
+    torch.cuda.synchronize()
+    assert native().tc_attention_launches() - before == tc_attention
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    ref = F.scaled_dot_product_attention(qf, kf, vf, scale=d**-0.5)
+    ref.backward(dout.float().transpose(1, 2))
+    for g, rg in ((dq, qf.grad), (dk, kf.grad), (dv, vf.grad)):
+        _close(g, rg, rel=3e-2, atol=3e-2)
+    _no_errors()
