@@ -29,6 +29,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 #include "attention_tc.h"
 #include "common.cuh"
@@ -42,6 +43,8 @@ constexpr int kTcBM = 128;  // queries per forward CTA
 constexpr int kTcBN = 128;  // keys per forward block
 constexpr int kTcSoftmaxThreads = 128;
 constexpr int kTcThreads = 64 + kTcSoftmaxThreads;
+constexpr int kBwdSoftmaxThreads = 256;  // two warps per TMEM lane quarter, one per half of the columns
+constexpr int kBwdThreads = 64 + kBwdSoftmaxThreads;
 constexpr uint32_t kTcTmemCols = 256;
 
 template <int D>
@@ -244,54 +247,63 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       }
       tc_fence_after();
       const int kbase = j * kTcBN;
-      float mx = -INFINITY;
+      // Full key blocks skip the per-element key mask (only the last block can be ragged).
+      auto softmax_block = [&](auto full_tag) -> bool {
+        constexpr bool kFull = decltype(full_tag)::value;
+        float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kTcBN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
-        tmem_ld_wait_regs(v);
+        for (int c = 0; c < kTcBN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
+          tmem_ld_wait_regs(v);
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (kbase + c * 32 + e < Nk) mx = fmaxf(mx, __uint_as_float(v[e]));
-      }
-      const float m_new = fmaxf(m, mx * scale_log2);
-      const float alpha = (m == -INFINITY) ? 0.f : fast_exp2f(m - m_new);
-      if (j > 0) {
-        if (!warp_wait(o_full, (j - 1) & 1, abort_flag, err)) {
-          ok = false;
-          break;
+          for (int e = 0; e < 32; ++e)
+            if (kFull || kbase + c * 32 + e < Nk) mx = fmaxf(mx, __uint_as_float(v[e]));
         }
-        tc_fence_after();
-        fold(alpha_prev);
-      }
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < kTcBN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
-        tmem_ld_wait_regs(v);
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int key = kbase + c * 32 + 2 * e;
-          const float p0 = key < Nk ? fast_exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, -m_new)) : 0.f;
-          const float p1 = key + 1 < Nk ? fast_exp2f(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, -m_new)) : 0.f;
-          rs += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
+        const float m_new = fmaxf(m, mx * scale_log2);
+        const float alpha = (m == -INFINITY) ? 0.f : fast_exp2f(m - m_new);
+        if (j > 0) {
+          if (!warp_wait(o_full, (j - 1) & 1, abort_flag, err)) return false;
+          tc_fence_after();
+          fold(alpha_prev);
         }
+        float rs = 0.f;
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          const int ci = (c & 1) * 4 + qd;  // 16-byte chunk within the 128-byte row of this key block
-          uint4* dst = reinterpret_cast<uint4*>(P + (c >> 1) * 16384 + r * 128 + ((ci ^ (r & 7)) << 4));
-          *dst = make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
+        for (int c = 0; c < kTcBN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
+          tmem_ld_wait_regs(v);
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int key = kbase + c * 32 + 2 * e;
+            const float p0 =
+                (kFull || key < Nk) ? fast_exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, -m_new)) : 0.f;
+            const float p1 =
+                (kFull || key + 1 < Nk) ? fast_exp2f(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, -m_new)) : 0.f;
+            rs += p0 + p1;
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            const int ci = (c & 1) * 4 + qd;  // 16-byte chunk within the 128-byte row of this key block
+            uint4* dst = reinterpret_cast<uint4*>(P + (c >> 1) * 16384 + r * 128 + ((ci ^ (r & 7)) << 4));
+            *dst = make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
+          }
         }
+        l = l * alpha + rs;
+        m = m_new;
+        alpha_prev = alpha;
+        return true;
+      };
+      const bool done = (kbase + kTcBN <= Nk) ? softmax_block(std::true_type{}) : softmax_block(std::false_type{});
+      if (!done) {
+        ok = false;
+        break;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
-      l = l * alpha + rs;
-      m = m_new;
-      alpha_prev = alpha;
     }
     if (ok && nb > 0) {
       if (warp_wait(o_full, (nb - 1) & 1, abort_flag, err)) {
@@ -329,10 +341,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 //               K = D) into TMEM; after the softmax warps have written P^T and dS^T to shared memory:
 //               dV += P^T dO_i, dK += dS^T Q_i (accumulated in TMEM over all query blocks) and
 //               dQ_i = dS K (dS^T read as an MN-major operand).
-//   warps 2-5   thread = key row: P^T = exp2(S^T * scale_log2 - lse_q), dS^T = P^T (dP^T - delta_q)
-//               into double-buffered shared memory (128-byte swizzled, K-major over queries); then
-//               the previous block's dQ rows (thread = query row) from TMEM into the fp32 dQ
-//               buffer with vector atomics; at the end dK and dV rows from TMEM as bf16.
+//   warps 2-9   thread = key row (two warps per row, one per half of the block's queries):
+//               P^T = exp2(S^T * scale_log2 - lse_q), dS^T = P^T (dP^T - delta_q) into
+//               double-buffered shared memory (128-byte swizzled, K-major over queries); then the
+//               previous block's dQ rows (thread = query row, half of the columns) from TMEM into
+//               the fp32 dQ buffer with vector atomics; at the end dK and dV rows as bf16.
 // TMEM columns: S^T [0, 128), dP^T [128, 256), dV, dK, dQ (D each) from 256; 1 CTA per SM.
 // The softmax of block i + 1 overlaps the dV / dK / dQ MMAs of block i. Queries past Nq read
 // zero Q / dO rows and lse = +inf, so they contribute nothing; keys past Nk are not stored.
@@ -353,7 +366,7 @@ struct TcBwdSmem {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                        const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq_acc,
@@ -394,11 +407,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&buf_free[s], 1);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(pds_full, kTcSoftmaxThreads);
+    mbar_init(pds_full, kBwdSoftmaxThreads);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, kTcSoftmaxThreads);
+    mbar_init(dq_free, kBwdSoftmaxThreads);
     mbar_init(drain, 1);
-    mbar_init(stat_full, kTcSoftmaxThreads);
+    mbar_init(stat_full, kBwdSoftmaxThreads);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&tmQ);
@@ -516,26 +529,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // -------------------------------------------------------------------- softmax / epilogue warps
+    // Warps 2..9: lane quarter lg = warp & 3 (the TMEM lanes the warp may read), column half
+    // `half` = (warp - 2) / 4: queries 64 * half .. +63 of a block (P / dS column block `half`),
+    // and columns D / 2 * half .. of dQ / dK / dV.
     const int lg = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = lg * 32 + lane;  // key row (S^T, dP^T, dK, dV) or query row (dQ)
     const int st = threadIdx.x - 64;
     const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
-    const float* lse_bh = lse + (size_t)bh * Nq;
-    const float* delta_bh = delta + (size_t)bh * Nq;
+    constexpr int kHalfD = D / 2;
+    // One statistic per thread: threads 0..127 hold lse, 128..255 delta, of query st % 128.
+    const float* stat_src = (st < 128 ? lse : delta) + (size_t)bh * Nq;
+    const float stat_pad = st < 128 ? INFINITY : 0.f;
+    auto load_stat = [&](int i) -> float {
+      const int q = i * 128 + (st & 127);
+      return (i < nq && q < Nq) ? stat_src[q] : stat_pad;
+    };
     auto dq_epilogue = [&](int i) -> bool {
       if (!warp_wait(dq_full, i & 1, abort_flag, err)) return false;
       tc_fence_after();
       const int qi = i * 128 + r;
-      float* dst = dq_acc + (size_t)b * dqs.b + (size_t)h * dqs.h + (size_t)(qi < Nq ? qi : 0) * dqs.n;
+      float* dst = dq_acc + (size_t)b * dqs.b + (size_t)h * dqs.h + (size_t)(qi < Nq ? qi : 0) * dqs.n + half * kHalfD;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_dq + lane_off + c * 32, v);
-        tmem_ld_wait_regs(v);
+      for (int c = 0; c < kHalfD / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(t_dq + lane_off + half * kHalfD + c * 16, v);
+        tmem_ld_wait_regs16(v);
         if (qi < Nq) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e),
+          for (int e = 0; e < 16; e += 4)
+            atomicAdd(reinterpret_cast<float4*>(dst + c * 16 + e),
                       make_float4(__uint_as_float(v[e]) * scale, __uint_as_float(v[e + 1]) * scale,
                                   __uint_as_float(v[e + 2]) * scale, __uint_as_float(v[e + 3]) * scale));
         }
@@ -545,18 +568,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       return true;
     };
     bool ok = true;
+    float stat_next = load_stat(0);
     for (int i = 0; i < nq; ++i) {
       const int s = i & 1;
-      // Per-query statistics of block i (one slot per thread; +inf lse zeroes P past Nq). The
-      // slots are rewritten only after every softmax thread has finished block i - 1, which the
-      // completed phase i - 1 of pds_full shows (each thread arrives there after its last read).
+      // Statistics of block i go to shared memory only after every softmax thread has finished
+      // block i - 1, which the completed phase i - 1 of pds_full shows (each thread arrives there
+      // after its last read); block i + 1's value is fetched now, off the critical path.
       if (i > 0 && !warp_wait(pds_full, (i - 1) & 1, abort_flag, err)) {
         ok = false;
         break;
       }
-      const int qs = i * 128 + st;
-      s_lse[st] = qs < Nq ? lse_bh[qs] : INFINITY;
-      s_delta[st] = qs < Nq ? delta_bh[qs] : 0.f;
+      (st < 128 ? s_lse : s_delta)[st & 127] = stat_next;
+      stat_next = load_stat(i + 1);
       mbar_arrive(stat_full);
       if (!warp_wait(stat_full, i & 1, abort_flag, err)) {
         ok = false;
@@ -571,30 +594,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      uint8_t* P = smem + L::kP + s * L::kPBytes;
-      uint8_t* DS = smem + L::kDS + s * L::kPBytes;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {  // 32 queries per chunk
+      uint8_t* P = smem + L::kP + s * L::kPBytes + half * 16384;
+      uint8_t* DS = smem + L::kDS + s * L::kPBytes + half * 16384;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {  // 32 queries per chunk
+        const int c = half * 2 + cc;
         uint32_t sv[32], dpv[32];
         tmem_ld_32x32b_x32(t_s + lane_off + c * 32, sv);
         tmem_ld_32x32b_x32(t_dp + lane_off + c * 32, dpv);
         tmem_ld_wait_regs(sv);
         tmem_ld_wait_regs(dpv);
         uint32_t pk[16], dk2[16];
+        const float4* l4 = reinterpret_cast<const float4*>(s_lse + c * 32);
+        const float4* d4 = reinterpret_cast<const float4*>(s_delta + c * 32);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int q = c * 32 + 2 * e;
-          const float p0 = fast_exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, -s_lse[q]));
-          const float p1 = fast_exp2f(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, -s_lse[q + 1]));
-          const float d0 = p0 * (__uint_as_float(dpv[2 * e]) - s_delta[q]);
-          const float d1 = p1 * (__uint_as_float(dpv[2 * e + 1]) - s_delta[q + 1]);
-          pk[e] = pack_bf16x2(p0, p1);
-          dk2[e] = pack_bf16x2(d0, d1);
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 lq = l4[e4], dq4 = d4[e4];
+          const float ls[4] = {lq.x, lq.y, lq.z, lq.w}, ds[4] = {dq4.x, dq4.y, dq4.z, dq4.w};
+#pragma unroll
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int e = e4 * 2 + e2;
+            const float p0 = fast_exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, -ls[2 * e2]));
+            const float p1 = fast_exp2f(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, -ls[2 * e2 + 1]));
+            const float d0 = p0 * (__uint_as_float(dpv[2 * e]) - ds[2 * e2]);
+            const float d1 = p1 * (__uint_as_float(dpv[2 * e + 1]) - ds[2 * e2 + 1]);
+            pk[e] = pack_bf16x2(p0, p1);
+            dk2[e] = pack_bf16x2(d0, d1);
+          }
         }
 #pragma unroll
         for (int qd = 0; qd < 4; ++qd) {
-          const int ci = (c & 1) * 4 + qd;
-          const uint32_t off = (c >> 1) * 16384 + r * 128 + ((ci ^ (r & 7)) << 4);
+          const int ci = cc * 4 + qd;
+          const uint32_t off = r * 128 + ((ci ^ (r & 7)) << 4);
           *reinterpret_cast<uint4*>(P + off) = make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
           *reinterpret_cast<uint4*>(DS + off) =
               make_uint4(dk2[4 * qd], dk2[4 * qd + 1], dk2[4 * qd + 2], dk2[4 * qd + 3]);
@@ -612,24 +643,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (ok) {
       // dq_full of the last block follows every MMA of this CTA: dV and dK are final.
       const int key = k0 + r;
-      bf16* dv_row = dv + (size_t)b * dvs.b + (size_t)h * dvs.h + (size_t)(key < Nk ? key : 0) * dvs.n;
-      bf16* dk_row = dk + (size_t)b * dks.b + (size_t)h * dks.h + (size_t)(key < Nk ? key : 0) * dks.n;
+      const size_t key_c = (size_t)(key < Nk ? key : 0);
+      bf16* dv_row = dv + (size_t)b * dvs.b + (size_t)h * dvs.h + key_c * dvs.n + half * kHalfD;
+      bf16* dk_row = dk + (size_t)b * dks.b + (size_t)h * dks.h + key_c * dks.n + half * kHalfD;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32], w[32];
-        tmem_ld_32x32b_x32(t_dv + lane_off + c * 32, v);
-        tmem_ld_32x32b_x32(t_dk + lane_off + c * 32, w);
-        tmem_ld_wait_regs(v);
-        tmem_ld_wait_regs(w);
+      for (int c = 0; c < kHalfD / 16; ++c) {
+        uint32_t v[16], w[16];
+        tmem_ld_32x32b_x16(t_dv + lane_off + half * kHalfD + c * 16, v);
+        tmem_ld_32x32b_x16(t_dk + lane_off + half * kHalfD + c * 16, w);
+        tmem_ld_wait_regs16(v);
+        tmem_ld_wait_regs16(w);
         if (key < Nk) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            *reinterpret_cast<uint4*>(dv_row + c * 32 + e) =
+          for (int e = 0; e < 16; e += 8) {
+            *reinterpret_cast<uint4*>(dv_row + c * 16 + e) =
                 make_uint4(pack_bf16x2(__uint_as_float(v[e]), __uint_as_float(v[e + 1])),
                            pack_bf16x2(__uint_as_float(v[e + 2]), __uint_as_float(v[e + 3])),
                            pack_bf16x2(__uint_as_float(v[e + 4]), __uint_as_float(v[e + 5])),
                            pack_bf16x2(__uint_as_float(v[e + 6]), __uint_as_float(v[e + 7])));
-            *reinterpret_cast<uint4*>(dk_row + c * 32 + e) =
+            *reinterpret_cast<uint4*>(dk_row + c * 16 + e) =
                 make_uint4(pack_bf16x2(__uint_as_float(w[e]) * scale, __uint_as_float(w[e + 1]) * scale),
                            pack_bf16x2(__uint_as_float(w[e + 2]) * scale, __uint_as_float(w[e + 3]) * scale),
                            pack_bf16x2(__uint_as_float(w[e + 4]) * scale, __uint_as_float(w[e + 5]) * scale),
@@ -704,7 +736,7 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   const int k_tiles = (Nk + 127) / 128;
   const long grid = (long)k_tiles * B * H;
   constexpr float kLog2e = 1.4426950408889634f;
-  kern<<<(unsigned)grid, kTcThreads, L::kBytes, stream>>>(
+  kern<<<(unsigned)grid, kBwdThreads, L::kBytes, stream>>>(
       mq, mk, mv, mdo, lse.data_ptr<float>(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), dqs,
       reinterpret_cast<bf16*>(dk.data_ptr()), dks, reinterpret_cast<bf16*>(dv.data_ptr()), dvs, H, Nq, Nk, k_tiles,
       scale, scale * kLog2e, error_word(device));

@@ -76,23 +76,31 @@ def mae_step_gemms(batch: int = 16) -> list[tuple[str, int, int, int, str, bool]
     return shapes
 
 
-def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20) -> dict:
+def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20, tc_mode: int = 1) -> dict:
+    """Native attention forward / backward on (b, h, n, d) bf16; tc_mode 1 = tcgen05 kernels where
+    they apply, 0 = warp-level kernels. FLOPs: 4 b h n^2 d forward, 2.5x that backward."""
     from . import _native
 
     dev = torch.device("cuda")
-    q, k, v = (torch.randn(b, h, n, d, device=dev).bfloat16() for _ in range(3))
-    o = torch.empty(b, n, h, d, device=dev, dtype=torch.bfloat16)
-    lse = torch.empty(b, h, n, device=dev)
-    scale = d**-0.5
     ext = _native.native()
-    fwd_us = _time(lambda: ext.attention_fwd(q, k, v, o, lse, scale), iters)
-    do = torch.randn_like(o)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    bwd_us = _time(lambda: ext.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, scale), iters)
-    sdpa_us = _time(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=scale), iters)
+    previous = ext.tc_attention_mode()
+    ext.set_tc_attention_mode(tc_mode)
+    try:
+        q, k, v = (torch.randn(b, h, n, d, device=dev).bfloat16() for _ in range(3))
+        o = torch.empty(b, n, h, d, device=dev, dtype=torch.bfloat16)
+        lse = torch.empty(b, h, n, device=dev)
+        scale = d**-0.5
+        fwd_us = _time(lambda: ext.attention_fwd(q, k, v, o, lse, scale), iters)
+        do = torch.randn_like(o)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        bwd_us = _time(lambda: ext.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, scale), iters)
+        sdpa_us = _time(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=scale), iters)
+    finally:
+        ext.set_tc_attention_mode(previous)
     flops = 4.0 * b * h * n * n * d
-    return {"fwd_us": fwd_us, "fwd_tflops": flops / fwd_us / 1e6, "bwd_us": bwd_us,
-            "bwd_tflops": 2.5 * flops / bwd_us / 1e6, "sdpa_fwd_us": sdpa_us}
+    return {"tc_mode": tc_mode, "fwd_us": round(fwd_us, 2), "fwd_tflops": round(flops / fwd_us / 1e6, 1),
+            "bwd_us": round(bwd_us, 2), "bwd_tflops": round(2.5 * flops / bwd_us / 1e6, 1),
+            "sdpa_fwd_us": round(sdpa_us, 2)}
 
 
 def step_gemms(depth: int = 24, batch: int = 16) -> str:
@@ -170,6 +178,7 @@ def main() -> None:
     at = sub.add_parser("attention")
     for name, default in (("b", 16), ("h", 16), ("n", 512), ("d", 32), ("iters", 20)):
         at.add_argument(f"--{name}", type=int, default=default)
+    at.add_argument("--modes", default="1,0", help="attention kernels: 1 = tcgen05, 0 = warp-level mma")
     args = ap.parse_args()
     if args.cmd == "step-gemms":
         print(step_gemms(args.depth, args.batch))
@@ -177,7 +186,8 @@ def main() -> None:
     if args.cmd == "gemm":
         print(bench_gemm(args.m, args.n, args.k, args.layout, args.iters, args.fp32_out, args.act))
     elif args.cmd == "attention":
-        print(bench_attention(args.b, args.h, args.n, args.d, args.iters))
+        for mode in (int(x) for x in args.modes.split(",")):
+            print(bench_attention(args.b, args.h, args.n, args.d, args.iters, mode))
     else:
         from . import _native
 
