@@ -1,0 +1,32 @@
+"""Tensor parallelism on 2 GPUs with the native kernels (NCCL collectives) against the dense model."""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORKER = Path(__file__).with_name("tp_worker.py")
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_dinov3_matches_dense():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29533", str(WORKER)]
+    out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
+    assert out.returncode == 0, out.stderr[-4000:]
+    res = json.loads([x for x in out.stdout.splitlines() if x.startswith("{")][-1])
+    assert res["errors"] == 0
+    assert res["sharded_layers"] == 2 * 5  # qkv, proj, SwiGLU w1 / w2 / w3 per block
+    assert abs(res["loss"] - res["ref"]) < 2e-2 * max(1.0, abs(res["ref"]))
+    assert res["grad_rel"] < 0.1, res
+    assert res["shard_rel"] < 0.1, res
+    assert res["sd_diff"] == 0.0
