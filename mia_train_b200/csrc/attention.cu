@@ -234,12 +234,19 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const bf16* __re
 }
 
 // delta[b, h, i] = sum_d dO[b, i, h, d] * O[b, i, h, d]. One thread per (b, i, h) row in memory
-// order, so a warp reads 32 consecutive rows with 16-byte loads.
+// order, so a warp reads 32 consecutive rows with 16-byte loads. When `zero_rows` is given (an
+// fp32 (B, N, H, D) buffer, e.g. the dQ accumulator of the backward that follows), the same row of
+// it is cleared, which saves a separate fill.
 template <int D>
 __global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout, float* __restrict__ delta,
-                                  int H, int N, int rows) {
+                                  int H, int N, int rows, float* __restrict__ zero_rows = nullptr) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
+  if (zero_rows != nullptr) {
+    float4* z = reinterpret_cast<float4*>(zero_rows + (size_t)row * D);
+#pragma unroll
+    for (int i = 0; i < D / 4; ++i) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   const uint4* a4 = reinterpret_cast<const uint4*>(o + (size_t)row * D);
   const uint4* c4 = reinterpret_cast<const uint4*>(dout + (size_t)row * D);
   float s = 0.f;
@@ -806,7 +813,7 @@ void rope_attention_bwd_packed(torch::Tensor q, torch::Tensor k, torch::Tensor v
   TORCH_CHECK(k.size(1) == N, "rope_attention_bwd_packed: self-attention (Nq == Nk) expected");
   c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  auto dq_acc = torch::zeros({B, N, H, D}, q.options().dtype(at::kFloat));
+  auto dq_acc = torch::empty({B, N, H, D}, q.options().dtype(at::kFloat));  // cleared by the delta kernel
   auto dk_view = dqkv.select(2, 1);
   auto dv_view = dqkv.select(2, 2);
   auto delta = torch::empty({B, H, N}, q.options().dtype(at::kFloat));
@@ -814,7 +821,7 @@ void rope_attention_bwd_packed(torch::Tensor q, torch::Tensor k, torch::Tensor v
     const int rows = B * H * N;
     attn_delta_kernel<HD><<<(rows + 255) / 256, 256, 0, stream>>>(
         reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
-        delta.data_ptr<float>(), H, N, rows);
+        delta.data_ptr<float>(), H, N, rows, dq_acc.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     if (attention_bwd_tc(q, k, v, dout, bnhd_strides(q), bnhd_strides(k), bnhd_strides(v), bnhd_contiguous(N, H, D),
                          lse, delta, dq_acc, bnhd_strides(dq_acc), dk_view, bnhd_strides(dk_view), dv_view,

@@ -945,8 +945,9 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
 // -------------------------------------------------------------- column sums (bias gradients)
 // out[n] (+)= sum_m x[m, n]; x bf16 (M, N) row-major, N % 8 == 0. A CTA owns 256 columns (8 per
 // lane) and a slab of rows split across its 8 warps; the warps are combined in shared memory and
-// the CTA adds one partial per column. The slab height keeps the CTA count near the SM count, so
-// each column sees only a few dozen atomics.
+// the CTA adds one partial per column. Each thread keeps 8 row loads in flight and the slab height
+// gives about 4 CTAs per SM (the input is usually still in L2, so the kernel is latency- rather
+// than bandwidth-bound); each column sees a few hundred atomics at most.
 __global__ void __launch_bounds__(256) column_sum_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ out,
                                                          int M, int N, int rows_per_cta) {
   __shared__ float part[8][256];
@@ -957,12 +958,12 @@ __global__ void __launch_bounds__(256) column_sum_kernel(const __nv_bfloat16* __
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (n < N) {
     int m = m_begin + warp;
-    for (; m + 24 < m_end; m += 32) {
-      uint4 u[4];
+    for (; m + 56 < m_end; m += 64) {
+      uint4 u[8];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) u[r] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(m + 8 * r) * N + n));
+      for (int r = 0; r < 8; ++r) u[r] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(m + 8 * r) * N + n));
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
+      for (int r = 0; r < 8; ++r) {
         const uint32_t w[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
@@ -1005,7 +1006,7 @@ void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate) {
   const int M = (int)x.size(0), N = (int)x.size(1);
   if (M == 0) return;
   const int gx = (N + 255) / 256;
-  const int gy = std::max(1, std::min((M + 63) / 64, (num_sms(x.get_device()) + gx - 1) / gx));
+  const int gy = std::max(1, std::min((M + 63) / 64, (4 * num_sms(x.get_device()) + gx - 1) / gx));
   const int rows = (M + gy - 1) / gy;
   column_sum_kernel<<<dim3(gx, gy), 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
                                                       out.data_ptr<float>(), M, N, rows);

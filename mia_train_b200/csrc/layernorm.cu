@@ -221,15 +221,30 @@ __global__ void __launch_bounds__(256) layernorm_bwd_param_kernel(const T* __res
   const int r_end = min(rows, r_begin + rows_per_cta);
   float aw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ab[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (c < n) {
-    for (int r = r_begin + warp; r < r_end; r += 8) {
-      float xv[8], gv[8];
-      Vec8<T>::load(x + (size_t)r * n + c, xv);
-      Vec8<T>::load(dy + (size_t)r * n + c, gv);
-      const float mean = mean_in[r], rstd = rstd_in[r];
+    // 4 rows per warp per iteration: their 8 vector loads are all in flight before the math.
+    for (int r = r_begin + warp; r < r_end; r += 32) {
+      float xv[4][8], gv[4][8], mean[4], rstd[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        aw[j] += gv[j] * (xv[j] - mean) * rstd;
-        ab[j] += gv[j];
+      for (int u = 0; u < 4; ++u) {
+        const int rr = r + 8 * u;
+        if (rr < r_end) {
+          Vec8<T>::load(x + (size_t)rr * n + c, xv[u]);
+          Vec8<T>::load(dy + (size_t)rr * n + c, gv[u]);
+          mean[u] = mean_in[rr];
+          rstd[u] = rstd_in[rr];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[u][j] = gv[u][j] = 0.f;
+          mean[u] = rstd[u] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          aw[j] += gv[u][j] * (xv[u][j] - mean[u]) * rstd[u];
+          ab[j] += gv[u][j];
+        }
       }
     }
   }

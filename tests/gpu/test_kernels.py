@@ -117,11 +117,15 @@ def test_gelu_epilogue_matches_exact_erf_gelu():
     _no_errors()
 
 
-def test_column_sum():
+@pytest.mark.parametrize("m,n", [(3000, 520), (8192, 512), (7, 64), (2048, 4096), (130, 1032), (65, 8)])
+def test_column_sum(m, n):
     from mia_train_b200.ops.linear import column_sum
 
-    x = torch.randn(3000, 520, device=DEV).bfloat16()
+    x = torch.randn(m, n, device=DEV).bfloat16()
     _close(column_sum(x), x.float().sum(0), rel=1e-3, atol=1e-2)
+    acc = torch.ones(n, device=DEV)
+    column_sum(x, out=acc, accumulate=True)
+    _close(acc, x.float().sum(0) + 1.0, rel=1e-3, atol=1e-2)
     _no_errors()
 
 
