@@ -482,35 +482,20 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restri
 // Token-major RoPE around the attention kernels. The fused projection qkv (B, N, 3, H, D) is never
 // split: v is read in place, q and k are rotated into qk (B, N, 2, H, D) by `rope_qk_fwd_kernel`,
 // and the attention kernels take strided (B, N, H, D) views. One warp per (token, q|k): the warp
-// stages the token's H*D channels in shared memory with 16-byte loads, computes cos/sin of the
-// token's P angles once, builds the channel -> (partner, pair, sign) table from `pairs`, then writes
-// rotated 16-byte chunks, so every global access is contiguous.
+// stages the token's H*D channels in shared memory with 16-byte loads; lane p owns pair p
+// (channels i1, i2 of `pairs`, the sine and cosine of the token's angle p in registers) and
+// rotates that pair in every head in place; the row is written back with 16-byte stores. Channels
+// outside every pair pass through unchanged.
 //
 // Backward (`rope_qk_bwd_kernel`): the attention backward leaves dq (fp32, token-major) and the
-// rotated-space dk in the dqkv slot; the warp un-rotates both into dqkv (B, N, 3, H, D) and the two
-// warps of a token sum d(angle_p) = sum_heads (g2 y1 - g1 y2) over q and k in shared memory, so the
-// token's angle gradient is written once, without atomics.
+// rotated-space dk in the dqkv slot; the warp un-rotates both into dqkv (B, N, 3, H, D), lane p
+// accumulating d(angle_p) = sum_heads (g2 y1 - g1 y2) in a register, and the two warps of a token
+// add their parts through shared memory, so the token's angle gradient is written once.
 constexpr int kRopeTokensPerCta = 4;  // warps = 2 * tokens
 
-struct RopeRole {
-  int16_t partner;  // -1: channel not rotated
-  int16_t pair;
-  float sign;       // -1 for the first channel of its pair, +1 for the second
-};
-
-__device__ __forceinline__ void rope_roles_warp(RopeRole* roles, const int* __restrict__ pairs, int P, int D,
-                                                float* cs, float* sn, const float* ang) {
-  const int lane = threadIdx.x % 32;
-  for (int d = lane; d < D; d += 32) roles[d] = RopeRole{-1, 0, 0.f};
-  __syncwarp();
-  for (int p = lane; p < P; p += 32) {
-    const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
-    roles[i1] = RopeRole{(int16_t)i2, (int16_t)p, -1.f};
-    roles[i2] = RopeRole{(int16_t)i1, (int16_t)p, 1.f};
-    const float a = ang != nullptr ? ang[p] : 0.f;
-    sincosf(a, &sn[p], &cs[p]);
-  }
-  __syncwarp();
+__device__ __forceinline__ size_t rope_fwd_warp_bytes(int HD) { return ((size_t)HD * 2 + 15) / 16 * 16; }
+__device__ __forceinline__ size_t rope_bwd_warp_bytes(int HD, int P) {
+  return ((size_t)HD * 6 + (size_t)P * 4 + 15) / 16 * 16;
 }
 
 // qkv (B, N, 3, H, D) -> qk (B, N, 2, H, D); angles (B or 1, N, P) fp32.
@@ -520,34 +505,31 @@ __global__ void rope_qk_fwd_kernel(const bf16* __restrict__ qkv, const float* __
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int HD = H * D;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int slot = warp;  // (token in CTA) * 2 + which
-  const size_t per_warp = (size_t)HD * 4 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16;
-  uint8_t* base = smem_raw + slot * ((per_warp + 15) / 16 * 16);
-  bf16* xs = reinterpret_cast<bf16*>(base);
-  bf16* os = xs + HD;
-  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 4);
-  float* sn = cs + P;
-  RopeRole* roles = reinterpret_cast<RopeRole*>(sn + P);
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw + warp * rope_fwd_warp_bytes(HD));
   const int token = blockIdx.x * kRopeTokensPerCta + warp / 2;
   const int which = warp % 2;
-  if (token >= BN) return;
+  if (token >= BN) return;  // no CTA-wide barrier below
   const int b = token / N, n = token % N;
   const uint4* src = reinterpret_cast<const uint4*>(qkv + ((size_t)token * 3 + which) * HD);
-#pragma unroll 8
+#pragma unroll 4
   for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(xs)[c] = src[c];
   const float* ang = angles + (size_t)b * angle_bstride + (size_t)n * P;
-  rope_roles_warp(roles, pairs, P, D, cs, sn, ang);
-  // element e = lane + 32 j: consecutive lanes touch consecutive channels (no bank conflicts)
-  for (int e = lane; e < HD; e += 32) {
-    const int d = e % D;
-    const RopeRole r = roles[d];
-    const float xi = __bfloat162float(xs[e]);
-    const float o = r.partner >= 0 ? xi * cs[r.pair] + r.sign * __bfloat162float(xs[e - d + r.partner]) * sn[r.pair] : xi;
-    os[e] = __float2bfloat16_rn(o);
+  __syncwarp();
+  for (int p = lane; p < P; p += 32) {
+    const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
+    float sn, cs;
+    sincosf(ang[p], &sn, &cs);
+    for (int h = 0; h < H; ++h) {
+      bf16* row = xs + h * D;
+      const float a = __bfloat162float(row[i1]), c2 = __bfloat162float(row[i2]);
+      row[i1] = __float2bfloat16_rn(a * cs - c2 * sn);
+      row[i2] = __float2bfloat16_rn(c2 * cs + a * sn);
+    }
   }
   __syncwarp();
   uint4* dst = reinterpret_cast<uint4*>(qk + ((size_t)token * 2 + which) * HD);
-  for (int c = lane; c < HD / 8; c += 32) dst[c] = reinterpret_cast<const uint4*>(os)[c];
+#pragma unroll 4
+  for (int c = lane; c < HD / 8; c += 32) dst[c] = reinterpret_cast<const uint4*>(xs)[c];
 }
 
 // dq_acc (B, N, H, D) fp32; dqkv (B, N, 3, H, D) with the rotated-space dk in slot 1 and dv in
@@ -559,15 +541,11 @@ __global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16*
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int HD = H * D;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const size_t per_warp = (size_t)HD * 4 + (size_t)HD * 4 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16;
-  uint8_t* base = smem_raw + warp * ((per_warp + 15) / 16 * 16);
+  const size_t per_warp = rope_bwd_warp_bytes(HD, P);
+  uint8_t* base = smem_raw + warp * per_warp;
   float* gs = reinterpret_cast<float*>(base);
   bf16* ys = reinterpret_cast<bf16*>(base + (size_t)HD * 4);
-  bf16* os = ys + HD;
-  float* cs = reinterpret_cast<float*>(base + (size_t)HD * 8);
-  float* sn = cs + P;
-  float* dpart = sn + P;
-  RopeRole* roles = reinterpret_cast<RopeRole*>(dpart + P);
+  float* dpart = reinterpret_cast<float*>(base + (size_t)HD * 6);
   const int token = blockIdx.x * kRopeTokensPerCta + warp / 2;
   const int which = warp % 2;
   const bool active = token < BN;
@@ -576,56 +554,52 @@ __global__ void rope_qk_bwd_kernel(const float* __restrict__ dq_acc, const bf16*
   if (active && !(P == 0 && which == 1)) {  // without RoPE the dk slot is already final
     if (which == 0) {
       const float4* g4 = reinterpret_cast<const float4*>(dq_acc + (size_t)token * HD);
-#pragma unroll 8
+#pragma unroll 4
       for (int c = lane; c < HD / 4; c += 32) reinterpret_cast<float4*>(gs)[c] = g4[c];
     } else {
       const uint4* g8 = reinterpret_cast<const uint4*>(dst);
 #pragma unroll 4
       for (int c = lane; c < HD / 8; c += 32) {
         const uint4 u = g8[c];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int hh = 0; hh < 4; ++hh) {
-          gs[c * 8 + 2 * hh] = bf16_lo(w[hh]);
-          gs[c * 8 + 2 * hh + 1] = bf16_hi(w[hh]);
-        }
+        reinterpret_cast<float4*>(gs)[2 * c] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+        reinterpret_cast<float4*>(gs)[2 * c + 1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
       }
     }
     if (P > 0) {
       const uint4* y8 = reinterpret_cast<const uint4*>(y + (size_t)token * y_token_stride + (size_t)which * HD);
-#pragma unroll 8
+#pragma unroll 4
       for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(ys)[c] = y8[c];
-      rope_roles_warp(roles, pairs, P, D, cs, sn, angles + (size_t)b * angle_bstride + (size_t)n * P);
-    } else {
       __syncwarp();
-    }
-    for (int e = lane; e < HD; e += 32) {
-      const int d = e % D;
-      float o = gs[e];
-      if (P > 0) {
-        const RopeRole r = roles[d];
-        // inverse rotation: the transpose of [[c, -s], [s, c]] acting on (first, second)
-        if (r.partner >= 0) o = gs[e] * cs[r.pair] - r.sign * gs[e - d + r.partner] * sn[r.pair];
-      }
-      os[e] = __float2bfloat16_rn(o);
-    }
-    __syncwarp();
-    for (int c = lane; c < HD / 8; c += 32) reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(os)[c];
-    if (dangles != nullptr && P > 0) {
+      const float* ang = angles + (size_t)b * angle_bstride + (size_t)n * P;
       for (int p = lane; p < P; p += 32) {
         const int i1 = pairs[2 * p], i2 = pairs[2 * p + 1];
+        float sn, cs;
+        sincosf(ang[p], &sn, &cs);
         float acc = 0.f;
-        for (int h = 0; h < H; ++h)
-          acc += gs[h * D + i2] * __bfloat162float(ys[h * D + i1]) - gs[h * D + i1] * __bfloat162float(ys[h * D + i2]);
+        for (int h = 0; h < H; ++h) {
+          float* g = gs + h * D;
+          const bf16* yr = ys + h * D;
+          const float g1 = g[i1], g2 = g[i2];
+          acc += g2 * __bfloat162float(yr[i1]) - g1 * __bfloat162float(yr[i2]);
+          // inverse rotation: the transpose of [[c, -s], [s, c]] acting on (first, second)
+          g[i1] = g1 * cs + g2 * sn;
+          g[i2] = g2 * cs - g1 * sn;
+        }
         dpart[p] = acc;
       }
+    }
+    __syncwarp();
+#pragma unroll 4
+    for (int c = lane; c < HD / 8; c += 32) {
+      const float4 a = reinterpret_cast<const float4*>(gs)[2 * c], e = reinterpret_cast<const float4*>(gs)[2 * c + 1];
+      reinterpret_cast<uint4*>(dst)[c] =
+          make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(e.x, e.y), pack_bf16x2(e.z, e.w));
     }
   }
   __syncthreads();
   if (active && dangles != nullptr && P > 0 && which == 0) {
     // partner warp (the token's k) is warp + 1, same CTA
-    const uint8_t* kbase = smem_raw + (warp + 1) * ((per_warp + 15) / 16 * 16);
-    const float* kpart = reinterpret_cast<const float*>(kbase + (size_t)HD * 8) + 2 * P;
+    const float* kpart = reinterpret_cast<const float*>(smem_raw + (warp + 1) * per_warp + (size_t)HD * 6);
     for (int p = lane; p < P; p += 32) dangles[(size_t)token * P + p] = dpart[p] + kpart[p];
   }
 }
@@ -722,13 +696,12 @@ void attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
 }
 
 static size_t rope_fwd_smem(int H, int D, int P) {
-  const size_t per_warp = ((size_t)H * D * 4 + (size_t)P * 8 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
-  return per_warp * 2 * kRopeTokensPerCta;
+  (void)P;
+  return ((size_t)H * D * 2 + 15) / 16 * 16 * 2 * kRopeTokensPerCta;
 }
 
 static size_t rope_bwd_smem(int H, int D, int P) {
-  const size_t per_warp = ((size_t)H * D * 8 + (size_t)P * 12 + (size_t)D * sizeof(RopeRole) + 16 + 15) / 16 * 16;
-  return per_warp * 2 * kRopeTokensPerCta;
+  return ((size_t)H * D * 6 + (size_t)P * 4 + 15) / 16 * 16 * 2 * kRopeTokensPerCta;
 }
 
 static std::pair<const float*, int64_t> rope_angles(const c10::optional<torch::Tensor>& angles, int N, int P,
