@@ -16,7 +16,7 @@ void layernorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w, c10::optiona
                    torch::Tensor mean, torch::Tensor rstd, double eps, bool rms);
 void layernorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> w, torch::Tensor mean,
                    torch::Tensor rstd, torch::Tensor dx, c10::optional<torch::Tensor> dw,
-                   c10::optional<torch::Tensor> db, bool rms);
+                   c10::optional<torch::Tensor> db, bool rms, c10::optional<torch::Tensor> dres);
 void attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse, double scale);
 void attention_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, double scale);
@@ -70,7 +70,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &mia::gemm, "tcgen05 bf16 GEMM with fused epilogue");
   m.def("column_sum", &mia::column_sum);
   m.def("layernorm_fwd", &mia::layernorm_fwd);
-  m.def("layernorm_bwd", &mia::layernorm_bwd);
+  m.def("layernorm_bwd", &mia::layernorm_bwd, "LayerNorm / RMSNorm backward; dres (optional) is added to dX",
+        py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("mean"), py::arg("rstd"), py::arg("dx"), py::arg("dw"),
+        py::arg("db"), py::arg("rms"), py::arg("dres") = py::none());
   m.def("attention_fwd", &mia::attention_fwd);
   m.def("attention_bwd", &mia::attention_bwd);
   m.def("rope_qk_fwd", &mia::rope_qk_fwd, "rotate q and k of a packed (B, N, 3, H, D) projection into (B, N, 2, H, D)");

@@ -159,11 +159,13 @@ __global__ void layernorm_fwd_kernel(const T* __restrict__ x, const float* __res
   }
 }
 
-// dX: one warp per row, the row held in registers (NCH chunks of 8 columns per lane).
+// dX: one warp per row, the row held in registers (NCH chunks of 8 columns per lane). `dres`, when
+// given, is the gradient that reaches x through a residual branch; it is added to dX here, which
+// saves autograd's separate sum of the two gradients.
 template <typename T, int NCH>
 __global__ void layernorm_bwd_dx_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
                                         const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
-                                        T* __restrict__ dx, int rows, int n, int rms) {
+                                        T* __restrict__ dx, int rows, int n, int rms, const T* __restrict__ dres) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
@@ -196,9 +198,15 @@ __global__ void layernorm_bwd_dx_kernel(const T* __restrict__ dy, const T* __res
     for (int ch = 0; ch < NCH; ++ch) {
       const int c = lane * 8 + ch * 256;
       if (c < n) {
-        float o[8];
+        float o[8], rg[8];
+        if (dres != nullptr) {
+          Vec8<T>::load(dres + (size_t)row * n + c, rg);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = rstd * (g[ch][j] - mg - xh[ch][j] * mgx);
+          for (int j = 0; j < 8; ++j) rg[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = rstd * (g[ch][j] - mg - xh[ch][j] * mgx) + rg[j];
         Vec8<T>::store(dr + c, o);
       }
     }
@@ -326,8 +334,11 @@ void layernorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w, c10::optiona
 
 void layernorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> w, torch::Tensor mean,
                    torch::Tensor rstd, torch::Tensor dx, c10::optional<torch::Tensor> dw,
-                   c10::optional<torch::Tensor> db, bool rms) {
+                   c10::optional<torch::Tensor> db, bool rms, c10::optional<torch::Tensor> dres) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.sizes() == x.sizes(), "layernorm_bwd: shapes");
+  TORCH_CHECK(!dres.has_value() || (dres->is_contiguous() && dres->sizes() == x.sizes() &&
+                                    dres->scalar_type() == x.scalar_type()),
+              "layernorm_bwd: residual gradient must match x");
   const int rows = (int)x.size(0), n = (int)x.size(1);
   c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -346,7 +357,8 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tenso
     constexpr int NCH = decltype(nch)::value;
     layernorm_bwd_dx_kernel<T, NCH><<<dx_grid, 256, 0, stream>>>(
         reinterpret_cast<const T*>(dy.data_ptr()), reinterpret_cast<const T*>(x.data_ptr()), wp, mean.data_ptr<float>(),
-        rstd.data_ptr<float>(), reinterpret_cast<T*>(dx.data_ptr()), rows, n, rms ? 1 : 0);
+        rstd.data_ptr<float>(), reinterpret_cast<T*>(dx.data_ptr()), rows, n, rms ? 1 : 0,
+        dres.has_value() ? reinterpret_cast<const T*>(dres->data_ptr()) : nullptr);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     if (dwp != nullptr || dbp != nullptr) {
       layernorm_bwd_param_kernel<T><<<dim3(gx, gy), 256, 0, stream>>>(

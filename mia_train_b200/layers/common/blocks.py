@@ -12,7 +12,7 @@ import torch
 import torch.nn as nn
 
 from ...ops.mlp import mlp
-from ...ops.norm import layer_norm
+from ...ops.norm import layer_norm, layer_norm_residual
 from .attention import SelfAttention
 from .lora import apply_linear, needs_per_layer
 from .rope import AxialRotaryEmbedding
@@ -39,10 +39,10 @@ class TransformerBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, coords: torch.Tensor | None = None) -> torch.Tensor:
         rope = self.rotary(coords) if (self.rotary is not None and coords is not None) else None
-        h = layer_norm(x, self.norm1.weight, self.norm1.bias, self.norm1.eps)
-        x = self.attn(h, rope=rope, residual=x)
-        h = layer_norm(x, self.norm2.weight, self.norm2.bias, self.norm2.eps)
+        h, r = layer_norm_residual(x, self.norm1.weight, self.norm1.bias, self.norm1.eps)
+        x = self.attn(h, rope=rope, residual=r)
+        h, r = layer_norm_residual(x, self.norm2.weight, self.norm2.bias, self.norm2.eps)
         fc1, fc2 = self.mlp[0], self.mlp[2]
         if needs_per_layer(fc1) or needs_per_layer(fc2):
-            return apply_linear(fc2, apply_linear(fc1, h, activation="gelu"), residual=x)
-        return mlp(h, fc1.weight, fc1.bias, fc2.weight, fc2.bias, residual=x)
+            return apply_linear(fc2, apply_linear(fc1, h, activation="gelu"), residual=r)
+        return mlp(h, fc1.weight, fc1.bias, fc2.weight, fc2.bias, residual=r)

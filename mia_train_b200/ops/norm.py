@@ -2,7 +2,9 @@
 
 Forward saves the per-row mean and reciprocal standard deviation; backward recomputes the
 normalised row from them and produces dX in the same pass, with the weight and bias gradients
-reduced per CTA and summed across CTAs by a second small kernel. On CPU this is `F.layer_norm`.
+reduced per CTA and summed across CTAs by a second small kernel. `layer_norm_residual` also hands back the
+input for a residual branch, so the backward adds that branch's gradient to dX in the same kernel
+instead of a separate add. On CPU this is `F.layer_norm`.
 Outputs keep the input dtype (the reference's autocast would have produced fp32 and cast again
 in the next matmul).
 """
@@ -44,7 +46,7 @@ class _NativeLayerNorm(torch.autograd.Function):
         w_sink, b_sink = ctx.sinks
         dw = (w_sink if w_sink is not None else torch.zeros(n, device=x2.device, dtype=torch.float32)) if has_w else None
         db = (b_sink if b_sink is not None else torch.zeros(n, device=x2.device, dtype=torch.float32)) if has_b else None
-        native().layernorm_bwd(dy2, x2, w, mean, rstd, dx, dw, db, bool(rms))
+        native().layernorm_bwd(dy2, x2, w, mean, rstd, dx, dw, db, bool(rms), None)
         return (
             dx.reshape(shape),
             dw.to(wdtype) if (dw is not None and w_sink is None) else None,
@@ -52,6 +54,44 @@ class _NativeLayerNorm(torch.autograd.Function):
             None,
             None,
         )
+
+
+class _NativeLayerNormResidual(torch.autograd.Function):
+    """(LN(x), x): the second output feeds a residual branch; backward returns LN'(dy) + d_residual."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):  # type: ignore[override]
+        y = _NativeLayerNorm.forward(ctx, x, weight, bias, eps, False)
+        return y, x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, dy, dres):  # type: ignore[override]
+        x2, w, mean, rstd = ctx.saved_tensors
+        shape, has_w, has_b, rms, wdtype, bdtype = ctx.meta
+        n = x2.shape[1]
+        dy2 = torch.zeros_like(x2) if dy is None else dy.reshape(x2.shape).to(x2.dtype).contiguous()
+        dres2 = None if dres is None else dres.reshape(x2.shape).to(x2.dtype).contiguous()
+        dx = torch.empty_like(x2)
+        w_sink, b_sink = ctx.sinks
+        dw = (w_sink if w_sink is not None else torch.zeros(n, device=x2.device, dtype=torch.float32)) if has_w else None
+        db = (b_sink if b_sink is not None else torch.zeros(n, device=x2.device, dtype=torch.float32)) if has_b else None
+        native().layernorm_bwd(dy2, x2, w, mean, rstd, dx, dw, db, bool(rms), dres2)
+        return (
+            dx.reshape(shape),
+            dw.to(wdtype) if (dw is not None and w_sink is None) else None,
+            db.to(bdtype) if (db is not None and b_sink is None) else None,
+            None,
+        )
+
+
+def layer_norm_residual(
+    x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None, eps: float = 1e-5
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """`(layer_norm(x), x)` for a pre-norm residual block, `h, r = layer_norm_residual(x, ...)`,
+    `out = r + f(h)`: both gradients of x are summed inside the LayerNorm backward kernel."""
+    if use_native(x) and x.dtype in (torch.bfloat16, torch.float32) and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048:
+        return _NativeLayerNormResidual.apply(x, weight, bias, eps)
+    return F.layer_norm(x, (x.shape[-1],), weight, bias, eps), x
 
 
 def layer_norm(

@@ -480,3 +480,27 @@ def test_attention_backward_paths(b, nq, nk, h, d, tc_attention):
     for g, rg in ((dq, qf.grad), (dk, kf.grad), (dv, vf.grad)):
         _close(g, rg, rel=3e-2, atol=3e-2)
     _no_errors()
+
+
+@pytest.mark.parametrize("width", [512, 1024, 1280])
+def test_layer_norm_residual_fuses_both_gradients(width):
+    """(LN(x), x) with the residual gradient added inside the LayerNorm backward kernel, against
+    fp32 autograd of LN(x) and x used separately (weight / bias gradients included)."""
+    from mia_train_b200.ops.norm import layer_norm_residual
+
+    torch.manual_seed(21)
+    x = (torch.randn(333, width, device=DEV) * 2).bfloat16().requires_grad_(True)
+    w = torch.randn(width, device=DEV, requires_grad=True)
+    b = torch.randn(width, device=DEV, requires_grad=True)
+    dh, dr = torch.randn(333, width, device=DEV).bfloat16(), torch.randn(333, width, device=DEV).bfloat16()
+    h, r = layer_norm_residual(x, w, b, 1e-5)
+    torch.autograd.backward((h, r), (dh, dr))
+    xf = x.detach().float().requires_grad_(True)
+    wf, bf = w.detach().clone().requires_grad_(True), b.detach().clone().requires_grad_(True)
+    hf = F.layer_norm(xf, (width,), wf, bf, 1e-5)
+    torch.autograd.backward((hf, xf * 1.0), (dh.float(), dr.float()))
+    _close(h, hf)
+    _close(x.grad, xf.grad, rel=2e-2, atol=5e-2)
+    _close(w.grad, wf.grad, rel=1e-2, atol=1e-1)
+    _close(b.grad, bf.grad, rel=1e-2, atol=1e-1)
+    _no_errors()
