@@ -93,8 +93,8 @@ def make_pool(n: int, seed: int) -> torch.Tensor:
     return torch.stack(vols)[:, None, None].contiguous()
 
 
-def zscore_u8(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
-    """Per-volume z-score of a uint8 batch (B, L, C, X, Y, Z) on the device."""
+def zscore_u8_torch(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Per-volume z-score of a uint8 batch (B, L, C, X, Y, Z) in torch ops (the reference arm)."""
     v = x.float()
     dims = tuple(range(1, v.dim()))
     mean = v.mean(dim=dims, keepdim=True)
@@ -192,6 +192,8 @@ def native_arm(args: argparse.Namespace, rank: int, world: int, local: int) -> d
     pool_cpu = make_pool(2 * args.batch, seed=rank + 1)
     pool_pinned = pool_cpu.pin_memory()
     pool_dev = pool_cpu.to(dev)
+
+    from mia_train_b200.ops.data import zscore_u8  # native per-volume z-score (uint8 -> bf16)
 
     def forward(batch):
         return alg({"img": zscore_u8(batch["img"], torch.bfloat16)})
@@ -321,7 +323,7 @@ def reference_arm(args: argparse.Namespace, rank: int, world: int, local: int) -
 
     dev = torch.device("cuda", local)
     pool = make_pool(2 * args.batch, seed=rank + 1)
-    vols = zscore_u8(pool, torch.float32)  # float volumes, the reference's input contract
+    vols = zscore_u8_torch(pool, torch.float32)  # float volumes, the reference's input contract
 
     class SyntheticVolumes(RefBase):
         """A synthetic dataset registered the way the reference's own tests do."""

@@ -9,6 +9,7 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
           c10::optional<torch::Tensor> aux_out, bool a_kmajor, bool b_kmajor, int64_t act, bool accumulate);
 void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate);
 int64_t set_gemm_pair_mode(int64_t mode);
+void zscore_u8(torch::Tensor x, torch::Tensor out);
 void set_tc_attention_mode(int64_t mode);
 int64_t tc_attention_mode();
 int64_t tc_attention_launches();
@@ -104,6 +105,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_tc_attention_mode", &mia::set_tc_attention_mode, "1: tcgen05 attention where it applies (head dim 32 / 64); 0: warp-level kernels");
   m.def("tc_attention_mode", &mia::tc_attention_mode);
   m.def("tc_attention_launches", &mia::tc_attention_launches);
+  m.def("zscore_u8", &mia::zscore_u8, "per-volume z-score of a uint8 batch into bf16 / fp32 (exact integer moments)");
   m.def("set_gemm_pair_mode", &mia::set_gemm_pair_mode, "0: single-CTA GEMM tiles; else CTA pairs when M >= 256; returns the previous mode");
   m.def("axial_angles_fwd", &mia::axial_angles_fwd, "angles[r, p] = coords[r, axis(p)] * freq(p)");
   m.def("axial_angles_bwd", &mia::axial_angles_bwd, "accumulate the frequency gradients of axial_angles_fwd");

@@ -504,3 +504,19 @@ def test_layer_norm_residual_fuses_both_gradients(width):
     _close(w.grad, wf.grad, rel=1e-2, atol=1e-1)
     _close(b.grad, bf.grad, rel=1e-2, atol=1e-1)
     _no_errors()
+
+
+@pytest.mark.parametrize("shape", [(4, 1, 1, 32, 32, 32), (3, 2, 16, 16, 16), (1, 7, 9, 5)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_zscore_u8(shape, dtype):
+    """Native per-volume z-score of uint8 volumes against the float64 torch formula."""
+    from mia_train_b200.ops.data import zscore_u8, zscore_u8_reference
+
+    torch.manual_seed(31)
+    x = torch.randint(0, 256, shape, dtype=torch.uint8, device=DEV)
+    x[0].fill_(7)  # a constant volume: std clamps to 1e-6 -> zeros
+    got = zscore_u8(x, dtype)
+    ref = zscore_u8_reference(x, torch.float64)
+    assert got.dtype == dtype
+    _close(got, ref, rel=1e-2 if dtype == torch.bfloat16 else 1e-5, atol=1e-2 if dtype == torch.bfloat16 else 1e-5)
+    _no_errors()
