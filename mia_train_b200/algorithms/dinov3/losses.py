@@ -4,7 +4,9 @@
 * `sinkhorn_knopp(logits, T, n_iter)`: Q = exp(logits / T)^T in fp32, normalised by its global sum
   (all-reduced), then `n_iter` rounds of: rows summed globally (all-reduced) and divided by K,
   columns summed locally and divided by the global batch; finally scaled by the batch. The
-  exponent is not clamped, as in the reference.
+  exponent is not clamped, as in the reference. On CUDA the same iterates run as two scaling
+  vectors over native reductions (`_sinkhorn_native`): 2 n_iter + 2 passes over the logits
+  instead of about ten full-matrix passes per iteration.
 * `DINOLoss`: cross-entropy of the student's temperature-softened log-softmax against the teacher
   probabilities over all (student, teacher) view pairs, optionally ignoring same-view pairs.
 * `IBOTPatchLoss`: the same on masked patches, each sample's patches weighted by 1 / its count; the
@@ -31,9 +33,47 @@ def _all_reduce(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
+def _sinkhorn_native(logits: torch.Tensor, temperature: float, n_iterations: int, total: float) -> torch.Tensor:
+    """The iterates of `sinkhorn_knopp` as scaling vectors, P[b, k] = E[b, k] r[k] s[b] with
+    E = exp(x / T): start r = 1, s = 1 / S0 (S0 = global sum of E); each iteration sets
+    r[k] = 1 / (K A[k]) with A[k] = sum_b E[b, k] s[b] (all-reduced, as the reference's row sums)
+    and s[b] = 1 / (B T[b]) with T[b] = sum_k E[b, k] r[k]; the result is E r s B. Native kernels
+    (`csrc/sinkhorn.cu`) do the two reductions and the final write, recomputing E each pass."""
+    from ...ops._native import native
+
+    ext = native()
+    x = logits.contiguous()
+    b, k = x.shape
+    a = torch.empty(k, device=x.device, dtype=torch.float32)
+    t = torch.empty(b, device=x.device, dtype=torch.float32)
+    ext.sinkhorn_colsum(x, float(temperature), None, a)  # sum_b E[b, k]
+    _all_reduce(a)
+    s0 = a.sum()
+    r = torch.ones(k, device=x.device, dtype=torch.float32)
+    s = torch.ones(b, device=x.device, dtype=torch.float32) / s0
+    for it in range(n_iterations):
+        if it == 0:
+            r = s0 / (k * a)  # A = a / S0 with s = 1 / S0
+        else:
+            ext.sinkhorn_colsum(x, float(temperature), s, a)
+            _all_reduce(a)
+            r = 1.0 / (k * a)
+        ext.sinkhorn_rowsum(x, float(temperature), r, t)
+        s = 1.0 / (total * t)
+    out = torch.empty(b, k, device=x.device, dtype=torch.float32)
+    ext.sinkhorn_scale(x, float(temperature), r.contiguous(), (s * total).contiguous(), 1.0, out)
+    return out
+
+
 def sinkhorn_knopp(
     logits: torch.Tensor, temperature: float, n_iterations: int = 3, batch_size: float | None = None
 ) -> torch.Tensor:
+    from ...ops._native import use_native
+
+    if (use_native(logits) and logits.dim() == 2 and logits.shape[1] % 8 == 0
+            and logits.dtype in (torch.float32, torch.bfloat16)):
+        total = float(logits.shape[0] * _world_size()) if batch_size is None else float(batch_size)
+        return _sinkhorn_native(logits, temperature, n_iterations, total)
     q = torch.exp(logits.float() / temperature).t()  # (K, B_local)
     k, b_local = q.shape
     total = float(b_local * _world_size()) if batch_size is None else float(batch_size)

@@ -10,6 +10,10 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
 void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate);
 int64_t set_gemm_pair_mode(int64_t mode);
 void zscore_u8(torch::Tensor x, torch::Tensor out);
+void sinkhorn_colsum(torch::Tensor x, double temperature, c10::optional<torch::Tensor> s, torch::Tensor out);
+void sinkhorn_rowsum(torch::Tensor x, double temperature, torch::Tensor r, torch::Tensor out);
+void sinkhorn_scale(torch::Tensor x, double temperature, torch::Tensor r, torch::Tensor s, double factor,
+                    torch::Tensor out);
 void set_tc_attention_mode(int64_t mode);
 int64_t tc_attention_mode();
 int64_t tc_attention_launches();
@@ -105,6 +109,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_tc_attention_mode", &mia::set_tc_attention_mode, "1: tcgen05 attention where it applies (head dim 32 / 64); 0: warp-level kernels");
   m.def("tc_attention_mode", &mia::tc_attention_mode);
   m.def("tc_attention_launches", &mia::tc_attention_launches);
+  m.def("sinkhorn_colsum", &mia::sinkhorn_colsum, "sum_b exp(x/T) s_b per prototype");
+  m.def("sinkhorn_rowsum", &mia::sinkhorn_rowsum, "sum_k exp(x/T) r_k per sample");
+  m.def("sinkhorn_scale", &mia::sinkhorn_scale, "exp(x/T) r_k s_b factor");
   m.def("zscore_u8", &mia::zscore_u8, "per-volume z-score of a uint8 batch into bf16 / fp32 (exact integer moments)");
   m.def("set_gemm_pair_mode", &mia::set_gemm_pair_mode, "0: single-CTA GEMM tiles; else CTA pairs when M >= 256; returns the previous mode");
   m.def("axial_angles_fwd", &mia::axial_angles_fwd, "angles[r, p] = coords[r, axis(p)] * freq(p)");

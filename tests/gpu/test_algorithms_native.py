@@ -104,3 +104,20 @@ def test_dinov3_ssl_step_and_ema():
     moved = any(not torch.equal(a, b) for a, b in zip(before, alg.teacher.parameters(), strict=True))
     assert moved or all(torch.equal(p, q) for p, q in zip(alg.teacher.parameters(), alg.student.parameters()))
     assert _native.native().check_errors(0) == 0
+
+
+@pytest.mark.parametrize("b,k,iters", [(37, 4096, 3), (3, 65536, 3), (64, 1024, 0), (16, 2048, 1)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_sinkhorn_native_matches_reference(b, k, iters, dtype):
+    """Scaling-vector Sinkhorn on native reductions against the reference's matrix iteration."""
+    from mia_train_b200.algorithms.dinov3.losses import sinkhorn_knopp
+    from mia_train_b200.ops import _native as _nat
+
+    torch.manual_seed(41)
+    logits = (torch.randn(b, k, device="cuda") * 0.3).to(dtype)  # exp(x / T) stays finite, as the reference needs
+    got = sinkhorn_knopp(logits, 0.07, iters)
+    with _nat.reference_math():
+        ref = sinkhorn_knopp(logits, 0.07, iters)
+    assert got.shape == ref.shape and got.dtype == torch.float32
+    torch.testing.assert_close(got, ref, rtol=1e-3, atol=1e-6 * float(ref.abs().max()))
+    torch.testing.assert_close(got.sum(dim=1), ref.sum(dim=1), rtol=1e-4, atol=1e-4)
