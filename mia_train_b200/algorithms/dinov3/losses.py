@@ -70,7 +70,8 @@ def sinkhorn_knopp(
 ) -> torch.Tensor:
     from ...ops._native import use_native
 
-    if (use_native(logits) and logits.dim() == 2 and logits.shape[1] % 8 == 0
+    # Below ~64 rows the iteration is bound by launch overhead either way and PyTorch's is shorter.
+    if (use_native(logits) and logits.dim() == 2 and logits.shape[0] >= 64 and logits.shape[1] % 8 == 0
             and logits.dtype in (torch.float32, torch.bfloat16)):
         total = float(logits.shape[0] * _world_size()) if batch_size is None else float(batch_size)
         return _sinkhorn_native(logits, temperature, n_iterations, total)

@@ -103,6 +103,19 @@ def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20, tc_mode: in
             "sdpa_fwd_us": round(sdpa_us, 2)}
 
 
+def bench_sinkhorn(b: int, k: int, iters: int = 3, reps: int = 20) -> dict:
+    """Sinkhorn-Knopp centring of (b, k) fp32 teacher logits: native scaling-vector kernels against
+    the matrix iteration in PyTorch ops (`reference_math`)."""
+    from ..algorithms.dinov3.losses import sinkhorn_knopp
+    from . import _native
+
+    logits = torch.randn(b, k, device="cuda") * 0.3
+    native_us = _time(lambda: sinkhorn_knopp(logits, 0.07, iters), reps)
+    with _native.reference_math():
+        torch_us = _time(lambda: sinkhorn_knopp(logits, 0.07, iters), reps)
+    return {"shape": (b, k), "iterations": iters, "native_us": round(native_us, 1), "torch_us": round(torch_us, 1)}
+
+
 def step_gemms(depth: int = 24, batch: int = 16) -> str:
     """Device time of each GEMM launched by one eager ViT-L MAE training step, grouped by shape."""
     from collections import defaultdict
@@ -179,7 +192,14 @@ def main() -> None:
     for name, default in (("b", 16), ("h", 16), ("n", 512), ("d", 32), ("iters", 20)):
         at.add_argument(f"--{name}", type=int, default=default)
     at.add_argument("--modes", default="1,0", help="attention kernels: 1 = tcgen05, 0 = warp-level mma")
+    sk = sub.add_parser("sinkhorn")
+    sk.add_argument("--b", type=int, default=2048)
+    sk.add_argument("--k", type=int, default=65536)
+    sk.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
+    if args.cmd == "sinkhorn":
+        print(bench_sinkhorn(args.b, args.k, args.iters))
+        return
     if args.cmd == "step-gemms":
         print(step_gemms(args.depth, args.batch))
         return

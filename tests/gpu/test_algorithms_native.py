@@ -106,16 +106,16 @@ def test_dinov3_ssl_step_and_ema():
     assert _native.native().check_errors(0) == 0
 
 
-@pytest.mark.parametrize("b,k,iters", [(37, 4096, 3), (3, 65536, 3), (64, 1024, 0), (16, 2048, 1)])
+@pytest.mark.parametrize("b,k,iters", [(37, 4096, 3), (3, 65536, 3), (64, 1024, 0), (16, 2048, 1), (300, 8192, 3)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_sinkhorn_native_matches_reference(b, k, iters, dtype):
     """Scaling-vector Sinkhorn on native reductions against the reference's matrix iteration."""
-    from mia_train_b200.algorithms.dinov3.losses import sinkhorn_knopp
+    from mia_train_b200.algorithms.dinov3.losses import _sinkhorn_native, sinkhorn_knopp
     from mia_train_b200.ops import _native as _nat
 
     torch.manual_seed(41)
     logits = (torch.randn(b, k, device="cuda") * 0.3).to(dtype)  # exp(x / T) stays finite, as the reference needs
-    got = sinkhorn_knopp(logits, 0.07, iters)
+    got = _sinkhorn_native(logits, 0.07, iters, float(b))
     with _nat.reference_math():
         ref = sinkhorn_knopp(logits, 0.07, iters)
     assert got.shape == ref.shape and got.dtype == torch.float32
