@@ -27,6 +27,6 @@ def test_tp_dinov3_matches_dense():
     assert res["errors"] == 0
     assert res["sharded_layers"] == 2 * 5  # qkv, proj, SwiGLU w1 / w2 / w3 per block
     assert abs(res["loss"] - res["ref"]) < 2e-2 * max(1.0, abs(res["ref"]))
-    assert res["grad_rel"] < 0.1, res
-    assert res["shard_rel"] < 0.1, res
+    assert res["grad_rel"] < 0.05, res  # relative L2 error of every replicated parameter's gradient
+    assert res["shard_rel"] < 0.05, res
     assert res["sd_diff"] == 0.0
