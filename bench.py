@@ -15,10 +15,11 @@ by a barrier and a synchronize; the batch, weights and activations are far large
 L2, so no flush is needed. `e2e` is the same metric through the framework's public step API with a
 pinned host->device copy of each step's batch and a device->host read of each step's loss.
 
-Native arm: this framework (native sm_100a kernels, one CUDA graph per step, fused AdamW; with
-N > 1 the flat gradient is all-reduced inside the graph). Reference arm: the unmodified reference
-package installed in baseline/_ref, driven through its own Trainer/algorithm/optimizer objects and
-its stock eager step (FSDP2 dp_shard = N when N > 1).
+Both arms receive the same uint8 volumes (16 MiB per step per rank over PCIe) and z-score them on
+the device inside the timed step. Native arm: this framework (native sm_100a kernels, one CUDA
+graph per step, fused AdamW; with N > 1 a sharded optimizer over peer memory). Reference arm: the
+unmodified reference package installed in baseline/_ref, driven through its own
+Trainer/algorithm/optimizer objects and its stock eager step (FSDP2 dp_shard = N when N > 1).
 """
 
 from __future__ import annotations
@@ -103,29 +104,66 @@ def zscore_u8_torch(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+    """Samples SM clocks and throttle reasons while the timed region runs (read-only queries).
 
-    FIELDS = (
-        "clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-        "clocks_event_reasons.sw_power_cap"
-    )
+    NVML is polled every 10 ms from a thread (the timed region of a default run is a few tenths of
+    a second, too short for `nvidia-smi`'s ~200 ms cadence); the device is matched to the CUDA
+    device by PCI bus id. Falls back to `nvidia-smi` polling when NVML is unavailable.
+    """
 
-    def __init__(self, index: int) -> None:
-        self.index = index
-        self.samples: list[list[str]] = []
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, cuda_index: int, period_s: float = 0.01) -> None:
+        self.cuda_index = cuda_index
+        self.period_s = period_s
+        self.samples: list[tuple[float, float | None, tuple[str, ...]]] = []  # (sm MHz, max MHz, reasons)
         self._stop = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
+        self.source = "nvml"
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        try:
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # noqa: BLE001 - domain formatting differs between drivers
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus[4:])
 
     def _run(self) -> None:
+        try:
+            nv, handle = self._nvml_handle()
+            bits = {
+                "hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap,
+            }
+            max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM))
+            while not self._stop.is_set():
+                sm = float(nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self.samples.append((sm, max_mhz, tuple(k for k, b in bits.items() if mask & b)))
+                self._stop.wait(self.period_s)
+        except Exception:  # noqa: BLE001
+            self.source = "nvidia-smi"
+            self._run_smi()
+
+    def _run_smi(self) -> None:
+        fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         while not self._stop.is_set():
             try:
                 out = subprocess.run(
-                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                    ["nvidia-smi", f"--id={self.cuda_index}", f"--query-gpu={fields}", "--format=csv,noheader,nounits"],
                     capture_output=True, text=True, timeout=5,
                 ).stdout.strip()
-                if out:
-                    self.samples.append([s.strip() for s in out.split(",")])
+                v = [x.strip() for x in out.split(",")]
+                if len(v) >= 6 and v[0].replace(".", "").isdigit():
+                    reasons = tuple(n for n, x in zip(self.REASONS, v[2:6], strict=True) if x == "Active")
+                    self.samples.append((float(v[0]), float(v[1]) if v[1].replace(".", "").isdigit() else None, reasons))
             except Exception:  # noqa: BLE001
                 pass
             self._stop.wait(0.2)
@@ -140,12 +178,12 @@ class ClockSampler:
 
     def summary(self) -> dict:
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
-        mx = max((float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()), default=None)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 3 + i and s[3 + i] == "Active"})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons, "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = sorted(s[0] for s in self.samples)
+        mx = max((s[1] for s in self.samples if s[1] is not None), default=None)
+        reasons = sorted({r for s in self.samples for r in s[2]})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": reasons, "samples": len(self.samples),
+                "source": self.source}
 
 
 def max_over_ranks(x: float, world: int) -> float:
@@ -284,7 +322,8 @@ def count_native_launches(fn, module) -> int | None:
 
 
 def kernel_table(fn, steps: int) -> str:
-    """Per-kernel device time of `steps` eager calls of `fn`, sorted by total time."""
+    """Per-kernel device time of `steps` eager calls of `fn`, sorted by total time, with the share of
+    device time spent in this framework's own kernels (`mia::`) against PyTorch / library kernels."""
     from collections import defaultdict
 
     from torch.profiler import ProfilerActivity, profile
@@ -301,10 +340,16 @@ def kernel_table(fn, steps: int) -> str:
             agg[e.name][0] += e.device_time_total / 1000.0
             agg[e.name][1] += 1
     total = sum(v[0] for v in agg.values()) / steps
+    mine = sum(v[0] for k, v in agg.items() if "mia::" in k) / steps
+    n_mine = sum(v[1] for k, v in agg.items() if "mia::" in k) // steps
+    n_all = sum(v[1] for v in agg.values()) // steps
     rows = sorted(agg.items(), key=lambda kv: -kv[1][0])
-    lines = [f"kernel table: {total:.3f} ms device time per step, {sum(v[1] for v in agg.values()) // steps} launches per step"]
+    lines = [f"kernel table: {total:.3f} ms device time per step, {n_all} launches per step",
+             f"  native (mia::) kernels: {mine:.3f} ms ({100 * mine / max(total, 1e-9):.1f}%), {n_mine} launches; "
+             f"other (PyTorch / library): {total - mine:.3f} ms, {n_all - n_mine} launches"]
     for name, (ms, n) in rows[:40]:
-        lines.append(f"  {ms / steps:8.3f} ms {100 * ms / steps / total:5.1f}%  x{n // steps:<4d} {name[:110]}")
+        tag = "native" if "mia::" in name else "other "
+        lines.append(f"  {ms / steps:8.3f} ms {100 * ms / steps / total:5.1f}%  x{n // steps:<4d} {tag} {name[:100]}")
     return "\n".join(lines)
 
 
@@ -322,8 +367,8 @@ def reference_arm(args: argparse.Namespace, rank: int, world: int, local: int) -
     from models.vit import ViT3D as RefViT3D  # type: ignore
 
     dev = torch.device("cuda", local)
-    pool = make_pool(2 * args.batch, seed=rank + 1)
-    vols = zscore_u8_torch(pool, torch.float32)  # float volumes, the reference's input contract
+    pool = make_pool(2 * args.batch, seed=rank + 1)  # uint8, as the native arm receives them
+    vols = zscore_u8_torch(pool, torch.float32)  # the dataset object's float contract (not timed)
 
     class SyntheticVolumes(RefBase):
         """A synthetic dataset registered the way the reference's own tests do."""
@@ -350,7 +395,9 @@ def reference_arm(args: argparse.Namespace, rank: int, world: int, local: int) -
     trainer = RefTrainer(alg, ds, tcfg, out_dir, dims=dims, mesh=mesh, device=dev)
 
     def one_step(batch: dict) -> torch.Tensor:
-        # the body of the reference's Trainer.train loop (src/engine/trainer.py:249-280)
+        # the per-volume z-score of the uint8 batch (the same input work the native arm does on the
+        # device), then the body of the reference's Trainer.train loop (src/engine/trainer.py:249-280)
+        batch = {"img": zscore_u8_torch(batch["img"], torch.float32)}
         with trainer._autocast():
             metrics = trainer.algorithm(batch)
         metrics["loss"].backward()
@@ -360,8 +407,8 @@ def reference_arm(args: argparse.Namespace, rank: int, world: int, local: int) -
         trainer.optimizer.zero_grad(set_to_none=True)
         return metrics["loss"]
 
-    vols_dev = vols.to(dev)
-    vols_pinned = vols.pin_memory()
+    vols_dev = pool.to(dev)
+    vols_pinned = pool.pin_memory()
 
     def device_batch(i: int) -> dict:
         j = (i * args.batch) % vols_dev.shape[0]
@@ -396,12 +443,13 @@ def reference_arm(args: argparse.Namespace, rank: int, world: int, local: int) -
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
         e2e = {"value": round(args.batch * world * 1000.0 / e2e_ms, 3), "unit": "samples/s",
-               "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": args.batch * 128**3 * 4, "d2h_bytes_per_step": 4,
+               "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": args.batch * 128**3, "d2h_bytes_per_step": 4,
                "api": "reference Trainer objects, eager step"}
     # FLOPs with the reference's own counter (SDPA is visible to it)
     from engine.mfu import measure_step_flops as ref_flops  # type: ignore
 
-    step_flops = ref_flops(trainer.algorithm, device_batch(0), trainer._autocast)
+    step_flops = ref_flops(trainer.algorithm, {"img": zscore_u8_torch(device_batch(0)["img"], torch.float32)},
+                           trainer._autocast)
     return {"ms": ms, "flops": step_flops, "loss": float(loss.item()), "clocks": clocks.summary(), "e2e": e2e}
 
 

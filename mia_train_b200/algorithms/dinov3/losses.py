@@ -70,14 +70,16 @@ def sinkhorn_knopp(
 ) -> torch.Tensor:
     from ...ops._native import use_native
 
-    # Below ~64 rows the iteration is bound by launch overhead either way and PyTorch's is shorter.
-    if (use_native(logits) and logits.dim() == 2 and logits.shape[0] >= 64 and logits.shape[1] % 8 == 0
+    world = _world_size()
+    total = float(logits.shape[0] * world) if batch_size is None else float(batch_size)
+    # Below ~64 rows per rank the iteration is bound by launch overhead either way and PyTorch's is
+    # shorter. The two paths issue different collectives, so the choice is made from the global
+    # row count (the same on every rank), never from this rank's own, possibly uneven, share.
+    if (use_native(logits) and logits.dim() == 2 and total >= 64 * world and logits.shape[1] % 8 == 0
             and logits.dtype in (torch.float32, torch.bfloat16)):
-        total = float(logits.shape[0] * _world_size()) if batch_size is None else float(batch_size)
         return _sinkhorn_native(logits, temperature, n_iterations, total)
     q = torch.exp(logits.float() / temperature).t()  # (K, B_local)
-    k, b_local = q.shape
-    total = float(b_local * _world_size()) if batch_size is None else float(batch_size)
+    k = q.shape[0]
     q /= _all_reduce(torch.sum(q))
     for _ in range(n_iterations):
         q /= _all_reduce(torch.sum(q, dim=1, keepdim=True))

@@ -885,6 +885,7 @@ int noalloc_launch(const mia::bf16* q, const mia::bf16* k, const mia::bf16* v, c
   if (cudaMemsetAsync(dq_acc, 0, dq_elems * sizeof(float), stream) != cudaSuccess) return MIA_NOALLOC_ERR_CUDA;
   const int rows = B * H * Nq;
   attn_delta_kernel<D><<<(rows + 255) / 256, 256, 0, stream>>>(o, dout, delta, H, Nq, rows);
+  if (cudaGetLastError() != cudaSuccess) return MIA_NOALLOC_ERR_CUDA;
   constexpr int S = D + 8;
   const size_t smem = (size_t)(2 * kAttnBlockN + 2 * kAttnBlockM) * S * 2 + (size_t)kAttnBlockN * (kAttnBlockM + 8) * 2 +
                       2 * kAttnBlockM * 4;
@@ -894,6 +895,7 @@ int noalloc_launch(const mia::bf16* q, const mia::bf16* k, const mia::bf16* v, c
   const Strides3 sq{(int64_t)H * Nq * D, (int64_t)Nq * D, D}, sk{(int64_t)H * Nk * D, (int64_t)Nk * D, D};
   attn_bwd_kernel<D><<<grid, kAttnThreads, smem, stream>>>(q, k, v, dout, lse, delta, dq_acc, dk, dv, H, Nq, Nk, scale,
                                                           scale * kLog2e, sq, sk, sk, sq, sk, sk);
+  if (cudaGetLastError() != cudaSuccess) return MIA_NOALLOC_ERR_CUDA;
   f32_to_bf16_kernel<<<(unsigned)((dq_elems / 2 + 255) / 256 + 1), 256, 0, stream>>>(dq_acc, dq, dq_elems);
   return cudaGetLastError() == cudaSuccess ? MIA_NOALLOC_OK : MIA_NOALLOC_ERR_CUDA;
 }
@@ -918,6 +920,23 @@ extern "C" __attribute__((visibility("default"))) int mia_attention_bwd_noalloc(
                  "fixed maximum of %d floats; split the batch or use the allocating entry point\n",
                  need, MIA_ATTN_NOALLOC_SCRATCH_FLOATS);
     return MIA_NOALLOC_ERR_TOO_LARGE;
+  }
+  const void* tensors[8] = {q, k, v, o, dout, dq, dk, dv};
+  for (const void* t : tensors) {
+    if (t == nullptr || (reinterpret_cast<uintptr_t>(t) & 15) != 0) {
+      std::fprintf(stderr, "mia_attention_bwd_noalloc: q, k, v, o, dout, dq, dk and dv must be non-null and "
+                           "16-byte aligned\n");
+      return MIA_NOALLOC_ERR_ARGS;
+    }
+  }
+  if (lse == nullptr || (reinterpret_cast<uintptr_t>(lse) & 3) != 0) {
+    std::fprintf(stderr, "mia_attention_bwd_noalloc: lse must be non-null and 4-byte aligned\n");
+    return MIA_NOALLOC_ERR_ARGS;
+  }
+  // An error left by earlier work belongs to its owner: report it without consuming it.
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    std::fprintf(stderr, "mia_attention_bwd_noalloc: a CUDA error is already pending; nothing launched\n");
+    return MIA_NOALLOC_ERR_CUDA;
   }
   int device = -1;
   float* scratch = noalloc_scratch_for_current_device(&device);

@@ -31,6 +31,9 @@ enum ErrorCode : int {
   kErrZeroReduceScatterWait = 401,
   kErrZeroNormWait = 402,
   kErrZeroAllGatherWait = 403,
+  kErrSymmBarrierWait = 501,
+  kErrTpChunkWait = 502,
+  kErrTpSlotWait = 503,
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

@@ -1,83 +1,122 @@
-"""Dataset contract and dataloader construction (reference `src/data/base.py:11-181`).
+"""The dataset contract every `[data]` implementation fulfils, and its dataloader.
 
-A `BaseDataset` builds its torch dataset lazily so transforms can be attached first; attached
-transforms compose in attachment order. Loaders shard with `DistributedSampler` over the
-data-parallel plane (tensor-parallel peers read the same batch), drop the last partial batch, pin
-memory when workers exist, and hold each worker to one intra-op thread so that workers do not
-oversubscribe the host that is issuing kernels.
+Interface of reference `src/data/base.py:11-181` (the methods the engine calls); the code is this
+framework's own.
+
+* A dataset is built lazily on first use of `.dataset`, so per-sample transforms (augmentation,
+  the algorithm's own `sample_transform`) can be attached first; once built, attaching is refused
+  because samples already handed out would have skipped the transform. Transforms run in the order
+  they were attached, inside the worker processes.
+* The loader shards indices over the data-parallel ranks only (tensor-parallel peers read the same
+  samples), drops the last partial batch (a short batch would change the step's shapes and, in
+  graph mode, force a re-capture), pins host memory when worker processes produce the batches, and
+  limits each worker to one intra-op thread so they do not compete with the host thread that
+  launches kernels.
 """
 
 from __future__ import annotations
 
 import abc
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any
 
 import torch
-import torch.utils.data as data
+from torch.utils.data import DataLoader, Dataset, DistributedSampler
+
+Transform = Callable[[dict[str, Any]], dict[str, Any]]
 
 
-def _single_threaded_worker(worker_id: int) -> None:
+class _Chain:
+    """Picklable composition of per-sample transforms (workers receive it by pickling)."""
+
+    def __init__(self, steps: Sequence[Transform]) -> None:
+        self.steps = tuple(steps)
+
+    def __call__(self, sample: dict[str, Any]) -> dict[str, Any]:
+        for step in self.steps:
+            sample = step(sample)
+        return sample
+
+
+class _WithTransform(Dataset):
+    def __init__(self, inner: Dataset, chain: _Chain) -> None:
+        self.inner = inner
+        self.chain = chain
+
+    def __len__(self) -> int:
+        return len(self.inner)  # type: ignore[arg-type]
+
+    def __getitem__(self, i: int) -> dict[str, Any]:
+        return self.chain(self.inner[i])
+
+
+def _one_thread_per_worker(_: int) -> None:
     torch.set_num_threads(1)
 
 
-class TransformedDataset(data.Dataset):
-    def __init__(self, source: data.Dataset, transforms: tuple[Any, ...]) -> None:
-        self.source = source
-        self.transforms = transforms
+@dataclass(frozen=True)
+class LoaderPlan:
+    """How batches are drawn for one rank of the data-parallel plane."""
 
-    def __len__(self) -> int:
-        return len(self.source)  # type: ignore[arg-type]
+    batch_size: int
+    rank: int
+    world_size: int
+    shuffle: bool = True
+    num_workers: int = 0
+    drop_last: bool = True
+    persistent_workers: bool = False
+    prefetch_factor: int = 2
 
-    def __getitem__(self, index: int) -> dict[str, Any]:
-        sample = self.source[index]
-        for transform in self.transforms:
-            sample = transform(sample)
-        return sample
+    def loader_kwargs(self) -> dict[str, Any]:
+        workers = self.num_workers > 0
+        kwargs: dict[str, Any] = {"batch_size": self.batch_size, "num_workers": self.num_workers,
+                                  "drop_last": self.drop_last, "pin_memory": workers}
+        if workers:
+            kwargs.update(worker_init_fn=_one_thread_per_worker, persistent_workers=self.persistent_workers,
+                          prefetch_factor=self.prefetch_factor)
+        return kwargs
 
 
 class BaseDataset(abc.ABC):
     def __init__(self) -> None:
-        self._dataset: data.Dataset | None = None
-        self._transforms: tuple[Any, ...] = ()
+        self._built: Dataset | None = None
+        self._steps: list[Transform] = []
 
     @abc.abstractmethod
-    def build_dataset(self) -> data.Dataset:
-        """Construct the underlying map-style dataset of sample dicts."""
+    def build_dataset(self) -> Dataset:
+        """The map-style dataset of sample dicts (called once, on first use)."""
 
-    def attach_transform(self, transform: Any) -> None:
-        """Append a per-sample transform; refused once the dataset has been materialised."""
-        if self._dataset is not None:
-            raise RuntimeError(
-                "attach_transform must be called before the dataset is built; samples already "
-                "handed out would not see it"
-            )
-        self._transforms = (*self._transforms, transform)
+    def attach_transform(self, transform: Transform) -> None:
+        if self._built is not None:
+            raise RuntimeError("the dataset is already built; transforms have to be attached before first use")
+        self._steps.append(transform)
 
     @property
-    def transforms(self) -> tuple[Any, ...]:
-        return self._transforms
+    def transforms(self) -> tuple[Transform, ...]:
+        return tuple(self._steps)
 
     @property
-    def dataset(self) -> data.Dataset:
-        if self._dataset is None:
-            source = self.build_dataset()
-            self._dataset = TransformedDataset(source, self._transforms) if self._transforms else source
-        return self._dataset
+    def dataset(self) -> Dataset:
+        if self._built is None:
+            raw = self.build_dataset()
+            self._built = _WithTransform(raw, _Chain(self._steps)) if self._steps else raw
+        return self._built
 
     @property
     def sample_axes(self) -> str | None:
-        """Per-sample axis order (batch excluded), e.g. "lcxyz"; None if the data declares none."""
+        """Axis letters of one sample (no batch axis), e.g. "lcxyz"; None when undeclared."""
         return None
 
     @classmethod
     def resolve_settings(cls, **kwargs: Any) -> dict[str, Any]:
-        """The dataset's settings fully expanded, for `resolved_config.json`."""
+        """The complete settings (after defaults) to record in `resolved_config.json`."""
         return dict(kwargs)
 
     @classmethod
     def referenced_files(cls, **kwargs: Any) -> tuple[Path, ...]:
-        """Files the settings point at, copied into the run directory."""
+        """Files named by the settings, copied into the run directory for provenance."""
         return ()
 
     def build_dataloader(
@@ -91,18 +130,8 @@ class BaseDataset(abc.ABC):
         drop_last: bool = True,
         persistent_workers: bool = False,
         prefetch_factor: int = 2,
-    ) -> data.DataLoader:
-        sampler = data.DistributedSampler(
-            self.dataset, num_replicas=world_size, rank=rank, shuffle=shuffle
-        )
-        return data.DataLoader(
-            self.dataset,
-            batch_size=batch_size,
-            sampler=sampler,
-            num_workers=num_workers,
-            drop_last=drop_last,
-            pin_memory=num_workers > 0,
-            worker_init_fn=_single_threaded_worker if num_workers > 0 else None,
-            persistent_workers=persistent_workers and num_workers > 0,
-            prefetch_factor=prefetch_factor if num_workers > 0 else None,
-        )
+    ) -> DataLoader:
+        plan = LoaderPlan(batch_size, rank, world_size, shuffle, num_workers, drop_last, persistent_workers,
+                          prefetch_factor)
+        sampler = DistributedSampler(self.dataset, num_replicas=plan.world_size, rank=plan.rank, shuffle=plan.shuffle)
+        return DataLoader(self.dataset, sampler=sampler, **plan.loader_kwargs())

@@ -1,32 +1,33 @@
-"""`hf_semantic_seg`: semantic-segmentation datasets from the HuggingFace Hub
-(reference `src/data/huggingface.py:43-312`).
+"""`hf_semantic_seg`: 2-D / 3-D semantic-segmentation crops read from HuggingFace Hub tables.
 
-A dataset is a `Preset` (repo, spatial rank, column encoding, image / label / shape columns, the
-column naming correlated row groups and how many of its "/"-separated levels form a group, hub
-split) or the same fields given inline; any inline field overrides the preset. Encodings:
-`"image"` (PNG bytes or decoded images) and `"raw"` (uint8 buffers plus a shape column).
+Config interface of reference `src/data/huggingface.py:43-312` (keys, preset names and the public
+Hub repositories and columns they point at); the implementation is this framework's own.
 
-* Splits hold out whole groups (`hold_out_groups`), never rows: `split = "val"` reads exactly the
-  held-out groups, `"train"` the rest.
-* `row_filters` keeps rows whose column value is in an allowed list.
-* Every sample draws a row and a `patch_size` window (zero-padded where the row is smaller) from a
-  generator seeded by `(seed, index)`, so samples are reproducible and workers never repeat.
-* `samples_per_epoch` fixes the epoch length independently of the row count.
-* Samples are `{"img": (1, 1, *patch) float in [0, 1], "label": (1, *patch) int64}` with axes
-  `"lcxy"` / `"lcxyz"`; a label id >= `num_classes` is an error.
+A table is described by a `Preset`: repository, spatial rank, how images are stored
+(`"image"`: PNG bytes or decoded images; `"raw"`: uint8 buffers next to a shape column), the
+image / label / shape columns, a group column whose first `group_levels` "/"-separated parts name
+a group of correlated rows, and the Hub split to read. Inline keys override a named preset.
 
-`datasets` is imported in `build_dataset`, so the registry does not need it.
+Row selection is one pass that computes a keep-mask: `row_filters` (column -> allowed values)
+and the group hold-out (`split = "val"` keeps exactly the rows of `hold_out_groups`, `"train"` the
+others), so no group ever appears on both sides. Each sample index seeds its own generator with
+`(seed, index)`, picks a row and a `patch_size` window from it (axes shorter than the window are
+zero-filled past their end) -- reproducible, and different in every worker. `samples_per_epoch`
+fixes the epoch length whatever the number of rows. Samples are `{"img": (1, 1, *patch) float in
+[0, 1], "label": (1, *patch) int64}` with axes `"lcxy"` / `"lcxyz"`; a label id beyond
+`num_classes - 1` raises. The `datasets` package is imported only when the table is first read.
 """
 
 from __future__ import annotations
 
+import dataclasses
 import io
-from dataclasses import asdict, dataclass
+from dataclasses import dataclass
 from typing import Any
 
 import numpy as np
 import torch
-import torch.utils.data as data
+from torch.utils.data import Dataset
 
 from .base import BaseDataset
 from .registry import DataRegistry
@@ -47,77 +48,78 @@ class Preset:
     hub_split: str = "train"
 
 
-def _decode_image(row: dict[str, Any], preset: Preset) -> tuple[np.ndarray, np.ndarray]:
-    from PIL import Image
-
-    def load(v: Any) -> np.ndarray:
-        if isinstance(v, dict):
-            return np.array(Image.open(io.BytesIO(v["bytes"])))
-        return np.array(v)
-
-    return load(row[preset.image_key]), load(row[preset.label_key])
-
-
-def _decode_raw(row: dict[str, Any], preset: Preset) -> tuple[np.ndarray, np.ndarray]:
-    if preset.shape_key is None:
-        raise ValueError("the 'raw' encoding needs shape_key, the column holding each array's shape")
-    shape = tuple(int(s) for s in row[preset.shape_key])
-    img = np.frombuffer(row[preset.image_key], dtype=np.uint8).reshape(shape)
-    lab = np.frombuffer(row[preset.label_key], dtype=np.uint8).reshape(shape)
-    return img, lab
-
-
-DECODERS = {"image": _decode_image, "raw": _decode_raw}
+PRESETS: dict[str, Preset] = {
+    "cellmap_3d": Preset(repo="eminorhan/cellmap-3d", spatial_rank=3, encoding="raw", image_key="volume",
+                         shape_key="shape", group_key="crop_name"),
+    "cellmap_2d": Preset(repo="eminorhan/cellmap-2d", spatial_rank=2, encoding="image", group_key="crop_name"),
+}
+_PRESET_FIELDS = tuple(f.name for f in dataclasses.fields(Preset))
+ENCODINGS = ("image", "raw")
 
 
 def group_of(name: str, levels: int) -> str:
-    return "/".join(name.split("/")[:levels])
+    """The group a row belongs to: the first `levels` parts of its "/"-separated name."""
+    parts = name.split("/")
+    return "/".join(parts[: max(1, levels)])
 
 
-def random_crop(
-    image: np.ndarray, label: np.ndarray, size: tuple[int, ...], rng: np.random.Generator
-) -> tuple[np.ndarray, np.ndarray]:
-    """The same random `size` window of both arrays; short axes are zero-padded at the end."""
-    pads, starts = [], []
-    for n, want in zip(image.shape, size, strict=True):
-        if n < want:
-            pads.append((0, want - n))
-            starts.append(0)
-        else:
-            pads.append((0, 0))
-            starts.append(int(rng.integers(0, n - want + 1)))
-    if any(p != (0, 0) for p in pads):
-        image, label = np.pad(image, pads), np.pad(label, pads)
-    window = tuple(slice(s, s + w) for s, w in zip(starts, size, strict=True))
-    return image[window], label[window]
+def random_crop(image: np.ndarray, label: np.ndarray, size: tuple[int, ...],
+                rng: np.random.Generator) -> tuple[np.ndarray, np.ndarray]:
+    """The same window of `size` from both arrays, at a random start; where an axis is shorter than
+    the window, the window starts at 0 and the part past the array's end is zero."""
+    starts = [int(rng.integers(0, n - w + 1)) if n >= w else 0 for n, w in zip(image.shape, size, strict=True)]
+    src = tuple(slice(s, s + min(w, n)) for s, w, n in zip(starts, size, image.shape, strict=True))
+    dst = tuple(slice(0, min(w, n)) for w, n in zip(size, image.shape, strict=True))
+    out_img = np.zeros(size, dtype=image.dtype)
+    out_lab = np.zeros(size, dtype=label.dtype)
+    out_img[dst] = image[src]
+    out_lab[dst] = label[src]
+    return out_img, out_lab
 
 
-class _Rows(data.Dataset):
-    def __init__(self, rows: Any, owner: HuggingFaceSemanticSegmentation) -> None:
+def _decode(row: dict[str, Any], layout: Preset) -> tuple[np.ndarray, np.ndarray]:
+    """(image, label) arrays of one table row."""
+    if layout.encoding == "raw":
+        if layout.shape_key is None:
+            raise ValueError("raw-encoded tables need shape_key (the column with each array's shape)")
+        shape = [int(n) for n in row[layout.shape_key]]
+        return tuple(np.frombuffer(row[k], dtype=np.uint8).reshape(shape)  # type: ignore[return-value]
+                     for k in (layout.image_key, layout.label_key))
+    from PIL import Image
+
+    def as_array(cell: Any) -> np.ndarray:
+        if isinstance(cell, dict) and "bytes" in cell:
+            cell = Image.open(io.BytesIO(cell["bytes"]))
+        return np.asarray(cell)
+
+    return as_array(row[layout.image_key]), as_array(row[layout.label_key])
+
+
+class _Crops(Dataset):
+    def __init__(self, rows: Any, source: HuggingFaceSemanticSegmentation) -> None:
         self.rows = rows
-        self.owner = owner
+        self.layout = source.preset
+        self.patch = source.patch_size
+        self.classes = source.num_classes
+        self.seed = source.seed
+        self.length = source.samples_per_epoch or len(rows)
 
     def __len__(self) -> int:
-        return self.owner.samples_per_epoch or len(self.rows)
+        return self.length
 
     def __getitem__(self, index: int) -> dict[str, torch.Tensor]:
-        rng = np.random.default_rng((self.owner.seed, index))
-        row = self.rows[int(rng.integers(0, len(self.rows)))]
-        image, label = DECODERS[self.owner.preset.encoding](row, self.owner.preset)
-        image, label = random_crop(image, label, self.owner.patch_size, rng)
-        if label.max() >= self.owner.num_classes:
-            raise ValueError(f"label id {int(label.max())} >= num_classes={self.owner.num_classes}")
-        return {
-            "img": torch.from_numpy(np.ascontiguousarray(image)).float().div_(255.0)[None, None],
-            "label": torch.from_numpy(np.ascontiguousarray(label)).long()[None],
-        }
+        rng = np.random.default_rng([self.seed, index])
+        image, label = _decode(self.rows[int(rng.integers(len(self.rows)))], self.layout)
+        image, label = random_crop(image, label, self.patch, rng)
+        top = int(label.max(initial=0))
+        if top >= self.classes:
+            raise ValueError(f"a label holds class id {top}, but num_classes = {self.classes}")
+        img = torch.as_tensor(np.ascontiguousarray(image), dtype=torch.float32) / 255.0
+        return {"img": img.reshape(1, 1, *self.patch), "label": torch.as_tensor(label.astype(np.int64))[None]}
 
 
 @DataRegistry.register("hf_semantic_seg")
 class HuggingFaceSemanticSegmentation(BaseDataset):
-    _PRESET_FIELDS = ("repo", "spatial_rank", "encoding", "image_key", "label_key", "shape_key", "group_key",
-                      "group_levels", "hub_split")
-
     def __init__(
         self,
         patch_size: tuple[int, ...] | list[int],
@@ -140,31 +142,31 @@ class HuggingFaceSemanticSegmentation(BaseDataset):
         samples_per_epoch: int | None = None,
     ) -> None:
         super().__init__()
-        self.preset = self._resolve_preset(
-            preset, repo=repo, spatial_rank=spatial_rank, encoding=encoding, image_key=image_key,
-            label_key=label_key, shape_key=shape_key, group_key=group_key, group_levels=group_levels,
-            hub_split=hub_split,
-        )
-        if self.preset.encoding not in DECODERS:
-            raise ValueError(f"unknown encoding {self.preset.encoding!r}; expected one of {sorted(DECODERS)}")
-        if self.preset.spatial_rank not in SAMPLE_AXES:
-            raise ValueError(f"spatial_rank must be 2 or 3, got {self.preset.spatial_rank}")
-        if len(patch_size) != self.preset.spatial_rank:
-            raise ValueError(
-                f"{self.preset.repo} is {self.preset.spatial_rank}-D, so patch_size needs {self.preset.spatial_rank} "
-                f"entries, got {list(patch_size)}"
-            )
+        overrides = dict(repo=repo, spatial_rank=spatial_rank, encoding=encoding, image_key=image_key,
+                         label_key=label_key, shape_key=shape_key, group_key=group_key, group_levels=group_levels,
+                         hub_split=hub_split)
+        self.preset = self._resolve_preset(preset, **overrides)
+        layout = self.preset
+        problems = []
+        if layout.encoding not in ENCODINGS:
+            problems.append(f"encoding {layout.encoding!r} is not one of {', '.join(ENCODINGS)}")
+        if layout.spatial_rank not in SAMPLE_AXES:
+            problems.append(f"spatial_rank {layout.spatial_rank} is not 2 or 3")
+        elif len(patch_size) != layout.spatial_rank:
+            problems.append(f"patch_size {list(patch_size)} needs {layout.spatial_rank} entries for {layout.repo}")
         if split not in ("train", "val"):
-            raise ValueError(f"split must be 'train' or 'val', got {split!r}")
+            problems.append(f"split {split!r} is neither 'train' nor 'val'")
         if split == "val" and not hold_out_groups:
-            raise ValueError("split='val' needs hold_out_groups: the validation side is exactly the held-out groups")
-        if hold_out_groups and self.preset.group_key is None:
-            raise ValueError("hold_out_groups needs group_key, the column to split on")
+            problems.append("split = 'val' reads the held-out groups, so hold_out_groups cannot be empty")
+        if hold_out_groups and layout.group_key is None:
+            problems.append("hold_out_groups needs a group_key column to decide group membership")
+        if problems:
+            raise ValueError("hf_semantic_seg: " + "; ".join(problems))
         self.patch_size = tuple(int(p) for p in patch_size)
         self.hold_out_groups = tuple(hold_out_groups)
         self.split = split
         self.num_classes = int(num_classes)
-        self.row_filters = dict(row_filters or {})
+        self.row_filters = {k: list(v) for k, v in (row_filters or {}).items()}
         self.cache_dir = cache_dir
         self.seed = int(seed)
         self.samples_per_epoch = samples_per_epoch
@@ -172,46 +174,44 @@ class HuggingFaceSemanticSegmentation(BaseDataset):
     @staticmethod
     def _resolve_preset(name: str | None, **fields: Any) -> Preset:
         given = {k: v for k, v in fields.items() if v is not None}
-        if name is not None:
-            if name not in PRESETS:
-                raise ValueError(f"unknown preset {name!r}; expected one of {sorted(PRESETS)}")
-            return Preset(**{**asdict(PRESETS[name]), **given})
-        missing = [k for k in ("repo", "spatial_rank", "encoding") if k not in given]
-        if missing:
-            raise ValueError(f"without a preset, {missing} must be given; presets: {sorted(PRESETS)}")
-        return Preset(**given)
+        if name is None:
+            needed = [k for k in ("repo", "spatial_rank", "encoding") if k not in given]
+            if needed:
+                raise ValueError(f"hf_semantic_seg: name a preset ({', '.join(sorted(PRESETS))}) or give "
+                                 f"{', '.join(needed)}")
+            return Preset(**given)
+        if name not in PRESETS:
+            raise ValueError(f"hf_semantic_seg: preset {name!r} is unknown (known: {', '.join(sorted(PRESETS))})")
+        return dataclasses.replace(PRESETS[name], **given)
 
     def select_rows(self, rows: Any) -> Any:
-        """Apply row filters and the group hold-out to a `datasets.Dataset`-like table."""
+        """The rows of this split that pass the filters (`rows` is a `datasets.Dataset`-like table)."""
+        n = len(rows)
+        keep = np.ones(n, dtype=bool)
         for column, allowed in self.row_filters.items():
             if column not in rows.column_names:
-                raise ValueError(
-                    f"row_filters names column {column!r}, which {self.preset.repo} lacks; columns: {rows.column_names}"
-                )
-            values = rows[column]
-            rows = rows.select([i for i, v in enumerate(values) if v in allowed])
+                raise ValueError(f"row_filters: {self.preset.repo} has no column {column!r} "
+                                 f"(columns: {', '.join(rows.column_names)})")
+            accepted = set(allowed)
+            keep &= np.fromiter((v in accepted for v in rows[column]), dtype=bool, count=n)
         if self.preset.group_key is not None:
             held = set(self.hold_out_groups)
-            groups = [group_of(n, self.preset.group_levels) for n in rows[self.preset.group_key]]
-            val = self.split == "val"
-            keep = [i for i, g in enumerate(groups) if (g in held) == val]
-            if not keep:
-                raise ValueError(
-                    f"no rows left for split={self.split!r} after holding out {sorted(held)}; groups present: "
-                    f"{sorted(set(groups))}"
-                )
-            rows = rows.select(keep)
-        if len(rows) == 0:
-            raise ValueError(f"{self.preset.repo} yielded no rows after filtering")
-        return rows
+            names = rows[self.preset.group_key]
+            in_held = np.fromiter((group_of(v, self.preset.group_levels) in held for v in names), dtype=bool, count=n)
+            keep &= in_held if self.split == "val" else ~in_held
+        chosen = np.flatnonzero(keep).tolist()
+        if not chosen:
+            raise ValueError(f"hf_semantic_seg: no rows of {self.preset.repo} remain for split {self.split!r} "
+                             f"(held-out groups {sorted(self.hold_out_groups)}, filters {self.row_filters})")
+        return rows.select(chosen)
 
-    def build_dataset(self) -> data.Dataset:
+    def build_dataset(self) -> Dataset:
         try:
             import datasets
         except ImportError as error:
-            raise ImportError("hf_semantic_seg reads the Hub through the `datasets` package, which is missing") from error
-        rows = datasets.load_dataset(self.preset.repo, split=self.preset.hub_split, cache_dir=self.cache_dir)
-        return _Rows(self.select_rows(rows), self)
+            raise ImportError("hf_semantic_seg needs the `datasets` package to read Hub tables") from error
+        table = datasets.load_dataset(self.preset.repo, split=self.preset.hub_split, cache_dir=self.cache_dir)
+        return _Crops(self.select_rows(table), self)
 
     @property
     def sample_axes(self) -> str:
@@ -219,12 +219,5 @@ class HuggingFaceSemanticSegmentation(BaseDataset):
 
     @classmethod
     def resolve_settings(cls, **kwargs: Any) -> dict[str, Any]:
-        preset = cls._resolve_preset(kwargs.get("preset"), **{k: kwargs.get(k) for k in cls._PRESET_FIELDS})
-        return {**kwargs, **asdict(preset)}
-
-
-PRESETS: dict[str, Preset] = {
-    "cellmap_3d": Preset(repo="eminorhan/cellmap-3d", spatial_rank=3, encoding="raw", image_key="volume",
-                         shape_key="shape", group_key="crop_name"),
-    "cellmap_2d": Preset(repo="eminorhan/cellmap-2d", spatial_rank=2, encoding="image", group_key="crop_name"),
-}
+        layout = cls._resolve_preset(kwargs.get("preset"), **{k: kwargs.get(k) for k in _PRESET_FIELDS})
+        return {**kwargs, **dataclasses.asdict(layout)}

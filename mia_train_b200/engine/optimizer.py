@@ -1,15 +1,19 @@
 """AdamW over (lr multiplier, wd multiplier) parameter groups, and the warmup/decay schedule.
 
-Grouping and schedule follow the reference's `src/engine/optimizer.py:17-251`:
+The `[trainer]` keys and their meaning are the reference's (`src/engine/optimizer.py:17-251`); the
+code is this framework's own. Every trainable parameter gets a role from its dotted name:
 
-* layerwise LR decay by block depth (`blocks.N.` in the name); the stem (`patch_embed`,
-  `pos_embed`, `patch_proj`, `level_embed`) and tokens sit at depth 0, everything above the
-  stack (final norms, heads, an algorithm's decoder) is not discounted; only parameters under
-  `model.` have a depth when the root is an algorithm;
-* `patch_embed_lr_mult` on the patch projection;
-* weight decay exempted by rank (ndim < 2) and for LoRA factors;
-* linear warmup, then linear or cosine decay to `min_lr_ratio`, times an unfreeze ramp; weight decay
-  follows its own cosine from `weight_decay` to `final_weight_decay`.
+* `stem`  -- the input adapter (`patch_embed`, `pos_embed`, `patch_proj`, `level_embed`) and learned
+  tokens (`*_token`, `*tokens*`): depth 0;
+* `block` -- inside `blocks.<i>.`: depth i + 1;
+* `top`   -- everything above the stack (final norms, heads) and, when the root is an algorithm,
+  every parameter outside its backbone (`model.`): depth n_blocks + 1, never discounted.
+
+The learning-rate multiplier is `layerwise_lr_decay ** (n_blocks + 1 - depth)` (times
+`patch_embed_lr_mult` on the patch projection); weight decay is off for LoRA factors and for
+parameters of rank < 2 when those switches are on. Parameters with equal multipliers share one
+AdamW group. The schedule is a linear warmup, then linear or cosine decay to `min_lr_ratio`, times
+the unfreeze ramp; weight decay follows its own cosine from `weight_decay` to `final_weight_decay`.
 
 `build_optimizer` returns `torch.optim.AdamW` unless the fused optimizer is requested and
 available; `FusedAdamW` (in `fused_adamw.py`) keeps AdamW's update rule and its
@@ -20,6 +24,7 @@ from __future__ import annotations
 
 import math
 import re
+from collections import defaultdict
 from typing import Any
 
 import torch
@@ -29,71 +34,71 @@ from torch.optim.lr_scheduler import LambdaLR
 
 from .config import LR_SCHEDULES, TrainerConfig
 
-_BLOCK_INDEX = re.compile(r"(?:^|\.)blocks\.(\d+)\.")
-_STEM_MARKERS = ("patch_embed", "pos_embed", "patch_proj", "level_embed")
-_BACKBONE_PREFIX = "model."
+_BLOCK = re.compile(r"(?:^|\.)blocks\.(\d+)\.")
+STEM_NAMES = ("patch_embed", "pos_embed", "patch_proj", "level_embed")
+_PATCH_PROJECTIONS = ("patch_embed", "patch_proj")
+_BACKBONE = "model."
 
 
 def is_stem(name: str) -> bool:
-    return any(marker in name for marker in _STEM_MARKERS)
+    """True for the input adapter's parameters (also what the frozen-backbone warm-up keeps trainable)."""
+    return any(part in name for part in STEM_NAMES)
 
 
-def _block_count(model: nn.Module) -> int:
-    depths = [int(m.group(1)) for name, _ in model.named_parameters() if (m := _BLOCK_INDEX.search(name))]
-    return max(depths) + 1 if depths else 0
+def _block_of(name: str) -> int | None:
+    hit = _BLOCK.search(name)
+    return None if hit is None else int(hit.group(1))
 
 
 def parameter_depth(name: str, n_blocks: int, backbone_scoped: bool = False) -> int:
-    if backbone_scoped and not name.startswith(_BACKBONE_PREFIX):
-        return n_blocks + 1
-    match = _BLOCK_INDEX.search(name)
-    if match is not None:
-        return int(match.group(1)) + 1
-    if is_stem(name) or name.endswith("_token") or "tokens" in name:
-        return 0
-    return n_blocks + 1
+    """0 for the stem and tokens, i + 1 inside block i, n_blocks + 1 above the stack."""
+    top = n_blocks + 1
+    if backbone_scoped and not name.startswith(_BACKBONE):
+        return top
+    block = _block_of(name)
+    if block is not None:
+        return block + 1
+    learned_token = name.endswith("_token") or "tokens" in name
+    return 0 if (is_stem(name) or learned_token) else top
 
 
 def lr_scale(name: str, n_blocks: int, config: TrainerConfig, backbone_scoped: bool = False) -> float:
-    if config.layerwise_lr_decay >= 1.0 and config.patch_embed_lr_mult == 1.0:
+    decay, patch_mult = config.layerwise_lr_decay, config.patch_embed_lr_mult
+    if decay >= 1.0 and patch_mult == 1.0:
         return 1.0
-    depth = parameter_depth(name, n_blocks, backbone_scoped)
-    scale = config.layerwise_lr_decay ** (n_blocks + 1 - depth)
-    if "patch_embed" in name or "patch_proj" in name:
-        scale *= config.patch_embed_lr_mult
-    return scale
+    steps_below_top = n_blocks + 1 - parameter_depth(name, n_blocks, backbone_scoped)
+    mult = decay**steps_below_top
+    return mult * patch_mult if any(p in name for p in _PATCH_PROJECTIONS) else mult
 
 
 def wd_scale(name: str, parameter: nn.Parameter, config: TrainerConfig) -> float:
-    if name.endswith((".lora_a", ".lora_b")) and config.zero_weight_decay_on_lora:
+    if config.zero_weight_decay_on_lora and (name.endswith(".lora_a") or name.endswith(".lora_b")):
         return 0.0
-    if not config.zero_weight_decay_on_norm_and_bias:
-        return 1.0
-    return 0.0 if parameter.ndim < 2 else 1.0
+    if config.zero_weight_decay_on_norm_and_bias and parameter.dim() < 2:
+        return 0.0
+    return 1.0
 
 
 def build_param_groups(model: nn.Module, config: TrainerConfig) -> list[dict[str, Any]]:
-    n_blocks = _block_count(model)
-    scoped = any(name.startswith(_BACKBONE_PREFIX) for name, _ in model.named_parameters())
-    buckets: dict[tuple[float, float], dict[str, Any]] = {}
-    for name, parameter in model.named_parameters():
-        if not parameter.requires_grad:
-            continue
-        key = (lr_scale(name, n_blocks, config, scoped), wd_scale(name, parameter, config))
-        group = buckets.setdefault(
-            key,
-            {
-                "params": [],
-                "lr": config.lr * key[0],
-                "weight_decay": config.weight_decay * key[1],
-                "lr_multiplier": key[0],
-                "wd_multiplier": key[1],
-            },
-        )
-        group["params"].append(parameter)
-    if not buckets:
-        raise ValueError("model has no parameters that require grad, so there is nothing to train")
-    return [buckets[key] for key in sorted(buckets, reverse=True)]
+    named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+    if not named:
+        raise ValueError("nothing to optimise: no parameter of the model requires a gradient")
+    blocks = [b for n, _ in model.named_parameters() if (b := _block_of(n)) is not None]
+    n_blocks = max(blocks) + 1 if blocks else 0
+    scoped = any(n.startswith(_BACKBONE) for n, _ in model.named_parameters())
+    members: dict[tuple[float, float], list[nn.Parameter]] = defaultdict(list)
+    for name, param in named:
+        members[(lr_scale(name, n_blocks, config, scoped), wd_scale(name, param, config))].append(param)
+    groups = []
+    for lr_mult, wd_mult in sorted(members, reverse=True):
+        groups.append({
+            "params": members[(lr_mult, wd_mult)],
+            "lr": config.lr * lr_mult,
+            "weight_decay": config.weight_decay * wd_mult,
+            "lr_multiplier": lr_mult,
+            "wd_multiplier": wd_mult,
+        })
+    return groups
 
 
 def _fused_wanted(config: TrainerConfig, model: nn.Module) -> bool:
@@ -124,37 +129,40 @@ def build_optimizer(model: nn.Module, config: TrainerConfig) -> Optimizer:
 
 
 def decay_fraction(progress: float, schedule: str) -> float:
-    if schedule == "cosine":
-        return 0.5 * (1.0 + math.cos(math.pi * progress))
-    if schedule == "linear":
-        return 1.0 - progress
-    raise ValueError(f"unknown lr_schedule {schedule!r}; expected one of {list(LR_SCHEDULES)}")
+    """Fraction of the decayable range left after `progress` (0..1) of the decay phase."""
+    shapes = {"cosine": lambda t: (1.0 + math.cos(math.pi * t)) / 2.0, "linear": lambda t: 1.0 - t}
+    if schedule not in shapes:
+        raise ValueError(f"lr_schedule {schedule!r} is not one of {list(LR_SCHEDULES)}")
+    return shapes[schedule](progress)
 
 
 def unfreeze_ramp(step: int, config: TrainerConfig) -> float:
-    if config.freeze_backbone_steps <= 0 or config.unfreeze_warmup_steps <= 0:
-        return 1.0
-    offset = step - config.freeze_backbone_steps
-    if offset < 0 or offset >= config.unfreeze_warmup_steps:
-        return 1.0
-    return (offset + 1) / config.unfreeze_warmup_steps
+    """Linear ramp of the learning rate over `unfreeze_warmup_steps` after the backbone unfreezes."""
+    ramp = config.unfreeze_warmup_steps
+    since = step - config.freeze_backbone_steps
+    if config.freeze_backbone_steps > 0 and ramp > 0 and 0 <= since < ramp:
+        return (since + 1) / ramp
+    return 1.0
 
 
 def lr_multiplier(step: int, config: TrainerConfig) -> float:
-    if config.warmup_steps > 0 and step < config.warmup_steps:
-        return (step + 1) / config.warmup_steps
-    span = max(1, config.max_steps - config.warmup_steps)
-    progress = min(1.0, max(0.0, (step - config.warmup_steps) / span))
-    value = config.min_lr_ratio + (1.0 - config.min_lr_ratio) * decay_fraction(progress, config.lr_schedule)
-    return value * unfreeze_ramp(step, config)
+    """Learning rate at `step` as a fraction of the configured peak."""
+    warm = config.warmup_steps
+    if warm > 0 and step < warm:
+        return (step + 1) / warm
+    t = (step - warm) / max(1, config.max_steps - warm)
+    floor = config.min_lr_ratio
+    shaped = floor + (1.0 - floor) * decay_fraction(min(max(t, 0.0), 1.0), config.lr_schedule)
+    return shaped * unfreeze_ramp(step, config)
 
 
 def weight_decay_at(step: int, config: TrainerConfig) -> float:
-    if config.final_weight_decay is None:
-        return config.weight_decay
-    progress = min(1.0, max(0.0, step / max(1, config.max_steps)))
-    span = config.final_weight_decay - config.weight_decay
-    return config.weight_decay + span * (1.0 - math.cos(math.pi * progress)) / 2
+    """Weight decay at `step`: constant, or a cosine from `weight_decay` to `final_weight_decay`."""
+    start, end = config.weight_decay, config.final_weight_decay
+    if end is None:
+        return start
+    t = min(max(step / max(1, config.max_steps), 0.0), 1.0)
+    return end + (start - end) * decay_fraction(t, "cosine")
 
 
 class WarmupDecaySchedule(LambdaLR):

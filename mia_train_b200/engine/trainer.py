@@ -14,6 +14,8 @@ Additions:
   AdamW kernel; nothing in a step waits on the host.
 * `nan_guard` stops the run when a logged loss is non-finite; `watchdog_seconds` dumps all thread
   stacks when one step takes longer than that.
+* At every logging step (already a device synchronisation) the native kernels' error word is read:
+  a bounded wait that ran out raises `DeviceWaitError` instead of training on partial results.
 """
 
 from __future__ import annotations
@@ -36,6 +38,7 @@ from torch.utils.data import DataLoader, DistributedSampler
 
 from ..algorithms.base import BaseAlgorithm
 from ..data.base import BaseDataset
+from ..ops._native import raise_on_device_errors
 from ..parallel.parallel_dims import ParallelDims
 from ..parallel.parallelize import parallelize_algorithm
 from ..utils.device import move_to_device
@@ -284,6 +287,10 @@ class Trainer:
                     frozen = False
                 if step % self.config.log_every == 0:
                     logged = reduce_metrics(metrics)
+                    # reduce_metrics synchronised the device: read the kernels' error word here, so a
+                    # wait that timed out (a lost peer, a stuck pipeline) stops the run instead of
+                    # letting AdamW apply partial gradients.
+                    raise_on_device_errors(self.device)
                     if self.config.nan_guard and not math.isfinite(logged.get("loss", 0.0)):
                         raise NonFiniteLossError(f"loss became {logged['loss']} at step {step}")
                     logged["lr"] = float(self.scheduler.get_last_lr()[0])
@@ -313,6 +320,7 @@ class Trainer:
         if self.graph_step is not None:
             self.graph_step.release()
             self.graph_step = None
+        raise_on_device_errors(self.device)
         self.logger.close()
         return step
 

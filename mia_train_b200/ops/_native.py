@@ -84,3 +84,55 @@ def use_native(*tensors: torch.Tensor) -> bool:
         return False
     native()  # raises if missing: CUDA inputs never fall back silently
     return True
+
+
+# Codes a kernel writes to the per-device error word when a bounded wait runs out (common.cuh).
+ERROR_CODES = {
+    101: "GEMM TMA producer wait",
+    102: "GEMM MMA issuer wait",
+    103: "GEMM epilogue wait",
+    201: "attention barrier wait",
+    301: "collective flag wait",
+    401: "sharded-optimizer reduce-scatter barrier",
+    402: "sharded-optimizer gradient-norm exchange",
+    403: "sharded-optimizer all-gather barrier",
+    501: "symmetric-memory barrier",
+    502: "tensor-parallel chunk flag wait",
+    503: "tensor-parallel slot reuse wait",
+}
+
+
+class DeviceWaitError(RuntimeError):
+    """A kernel gave up a bounded wait (a peer or a pipeline stage never arrived)."""
+
+    def __init__(self, code: int, device: int) -> None:
+        self.code = code
+        self.device = device
+        what = ERROR_CODES.get(code, "unknown wait")
+        super().__init__(
+            f"device {device}: a kernel abandoned a bounded wait ({what}, code {code}); the step's results "
+            "are not trustworthy (a peer rank may be gone)"
+        )
+
+
+def device_error_code(device: int) -> int:
+    """Read and clear the error word of `device` (synchronises with that device)."""
+    return int(native().check_errors(int(device)))
+
+
+def raise_on_device_errors(device: torch.device | int) -> None:
+    """Raise `DeviceWaitError` if any kernel on `device` recorded a wait timeout since the last check.
+
+    A no-op for CPU devices and when the extension is not loadable (no native kernel ran then).
+    """
+    if isinstance(device, torch.device):
+        if device.type != "cuda":
+            return
+        index = device.index if device.index is not None else torch.cuda.current_device()
+    else:
+        index = int(device)
+    if not native_available():
+        return
+    code = device_error_code(index)
+    if code != 0:
+        raise DeviceWaitError(code, index)

@@ -31,12 +31,14 @@ class ParallelDims:
     param_dtype: str = "bf16"
 
     def __post_init__(self) -> None:
-        if self.dp_replicate < 1 or self.dp_shard < 1 or self.tp < 1:
-            raise ValueError(f"dp_replicate, dp_shard, and tp must all be >= 1, got {self}")
+        sizes = {"dp_replicate": self.dp_replicate, "dp_shard": self.dp_shard, "tp": self.tp}
+        bad = [f"{k} = {v}" for k, v in sizes.items() if v < 1]
+        if bad:
+            raise ValueError(f"[parallelism]: every mesh dimension is a positive size ({', '.join(bad)})")
         if self.fsdp_unit not in FSDP_UNITS:
-            raise ValueError(f"fsdp_unit must be one of {FSDP_UNITS}, got {self.fsdp_unit!r}")
+            raise ValueError(f"[parallelism]: fsdp_unit {self.fsdp_unit!r} is not one of {', '.join(FSDP_UNITS)}")
         if self.param_dtype not in PARAM_DTYPES:
-            raise ValueError(f"param_dtype must be one of {PARAM_DTYPES}, got {self.param_dtype!r}")
+            raise ValueError(f"[parallelism]: param_dtype {self.param_dtype!r} is not one of {', '.join(PARAM_DTYPES)}")
 
     @property
     def world_size(self) -> int:
@@ -67,8 +69,8 @@ class ParallelDims:
         actual = dist.get_world_size()
         if actual != self.world_size:
             raise ValueError(
-                f"process group world_size={actual} does not match dp_replicate({self.dp_replicate}) "
-                f"* dp_shard({self.dp_shard}) * tp({self.tp}) = {self.world_size}"
+                f"[parallelism] describes a mesh of {self.world_size} ranks ({self.dp_replicate} replicas x "
+                f"{self.dp_shard} shards x tp {self.tp}), but {actual} processes were launched"
             )
         return init_device_mesh(
             device_type,

@@ -1,10 +1,17 @@
-"""TOML run configuration -> frozen dataclasses (reference `src/utils/config.py:15-154`).
+"""Run configuration: one TOML file, parsed into frozen dataclasses.
 
-`[model]`, `[algorithm]`, `[data]` and `[val_data]` are registry names plus constructor kwargs;
-`[trainer]`, `[parallelism]`, `[init]`, `[augment]` and `[lora]` are strict dataclasses that name any
-unknown key. `[lora]` and `[trainer].freeze_backbone_steps` are mutually exclusive: LoRA freezes the
-base weights before the optimizer is built, and the unfreeze boundary would then enable gradients
-for tensors that no param group holds.
+The section and key names are the reference's contract (`src/utils/config.py:15-154`), so a config
+written for it loads here unchanged:
+
+* component sections `[model]`, `[algorithm]`, `[data]` (required) and `[val_data]` (optional):
+  `name` picks a registered implementation, every other key goes to its constructor;
+* settings sections `[trainer]` (required), `[parallelism]`, `[init]`, `[augment]`, `[lora]`: keys
+  must be fields of the section's dataclass, and an unknown key is an error naming the valid ones;
+* a top-level `experiment_name`.
+
+The parser is driven by the `_SECTIONS` table below. One rule spans sections: `[lora]` and
+`[trainer].freeze_backbone_steps` exclude each other (LoRA leaves the base weights out of the
+optimizer before it is built; the unfreeze step would then create gradients nobody applies).
 """
 
 from __future__ import annotations
@@ -18,11 +25,11 @@ from typing import Any
 from ..engine.config import AugmentConfig, InitConfig, LoRAConfig, TrainerConfig
 from ..parallel.parallel_dims import ParallelDims
 
-COMPONENT_SECTIONS = ("model", "algorithm", "data")
-
 
 @dataclass(frozen=True)
 class ComponentConfig:
+    """A registry name and the constructor keyword arguments that go with it."""
+
     name: str
     kwargs: dict[str, Any] = field(default_factory=dict)
 
@@ -43,73 +50,87 @@ class RunConfig:
     def __post_init__(self) -> None:
         if self.lora.enabled() and self.trainer.freeze_backbone_steps > 0:
             raise ValueError(
-                "[lora] and [trainer].freeze_backbone_steps cannot both be set: LoRA keeps the base "
-                "weights out of the optimizer, so the unfreeze boundary would allocate gradients "
-                "that are never applied. Drop freeze_backbone_steps; a zero-initialised adapter "
-                "already starts the encoder at its pretrained function."
+                "a [lora] adapter cannot be combined with [trainer].freeze_backbone_steps: the base "
+                "weights are outside the optimizer, so unfreezing them would only add unused gradients "
+                "(a zero-initialised adapter already starts from the pretrained encoder; remove "
+                "freeze_backbone_steps)"
             )
 
 
-def _component(raw: dict[str, Any], section: str) -> ComponentConfig:
-    body = dict(raw[section])
-    if "name" not in body:
-        raise ValueError(f"[{section}] must set 'name' to select a registered implementation")
-    return ComponentConfig(name=body.pop("name"), kwargs=body)
+# section -> (dataclass, or None for a component section; required)
+_SECTIONS: dict[str, tuple[type | None, bool]] = {
+    "model": (None, True),
+    "algorithm": (None, True),
+    "data": (None, True),
+    "val_data": (None, False),
+    "trainer": (TrainerConfig, True),
+    "parallelism": (ParallelDims, False),
+    "init": (InitConfig, False),
+    "augment": (AugmentConfig, False),
+    "lora": (LoRAConfig, False),
+}
 
 
-def dataclass_from_section(cls: Any, body: dict[str, Any], section: str) -> Any:
-    valid = {f.name for f in dataclasses.fields(cls)}
-    unknown = sorted(set(body) - valid)
-    if unknown:
-        raise ValueError(f"[{section}] has unknown key(s) {unknown}; valid keys are {sorted(valid)}")
-    return cls(**body)
+def _component(section: str, table: dict[str, Any]) -> ComponentConfig:
+    kwargs = {k: v for k, v in table.items() if k != "name"}
+    if "name" not in table:
+        raise ValueError(f"[{section}] needs a 'name' key selecting one of the registered implementations")
+    return ComponentConfig(str(table["name"]), kwargs)
+
+
+def _settings(section: str, cls: type, table: dict[str, Any]) -> Any:
+    allowed = [f.name for f in dataclasses.fields(cls)]
+    stray = sorted(k for k in table if k not in allowed)
+    if stray:
+        raise ValueError(f"[{section}]: unknown key(s) {', '.join(stray)} (accepted keys: {', '.join(sorted(allowed))})")
+    return cls(**table)
 
 
 def parse_run_config(raw: dict[str, Any]) -> RunConfig:
+    """Build a `RunConfig` from an already-parsed TOML document."""
     if "experiment_name" not in raw:
-        raise ValueError("config must set a top-level 'experiment_name'")
-    missing = [s for s in (*COMPONENT_SECTIONS, "trainer") if s not in raw]
-    if missing:
-        raise ValueError(f"config is missing required section(s): {missing}")
-    return RunConfig(
-        experiment_name=raw["experiment_name"],
-        model=_component(raw, "model"),
-        algorithm=_component(raw, "algorithm"),
-        data=_component(raw, "data"),
-        trainer=dataclass_from_section(TrainerConfig, dict(raw["trainer"]), "trainer"),
-        parallelism=dataclass_from_section(ParallelDims, dict(raw.get("parallelism", {})), "parallelism"),
-        val_data=_component(raw, "val_data") if "val_data" in raw else None,
-        init=dataclass_from_section(InitConfig, dict(raw.get("init", {})), "init"),
-        augment=dataclass_from_section(AugmentConfig, dict(raw.get("augment", {})), "augment"),
-        lora=dataclass_from_section(LoRAConfig, dict(raw.get("lora", {})), "lora"),
-    )
+        raise ValueError("the config has no top-level experiment_name")
+    absent = [name for name, (_, required) in _SECTIONS.items() if required and name not in raw]
+    if absent:
+        raise ValueError(f"the config is missing the required section(s) {', '.join(absent)}")
+    parsed: dict[str, Any] = {}
+    for name, (cls, _) in _SECTIONS.items():
+        if name not in raw:
+            continue
+        table = dict(raw[name])
+        parsed[name] = _component(name, table) if cls is None else _settings(name, cls, table)
+    return RunConfig(experiment_name=raw["experiment_name"], **parsed)
 
 
 def load_run_config(path: Path) -> RunConfig:
-    with Path(path).open("rb") as handle:
-        return parse_run_config(tomllib.load(handle))
+    return parse_run_config(tomllib.loads(Path(path).read_text(encoding="utf-8")))
 
 
 def as_plain_dict(config: RunConfig) -> dict[str, Any]:
+    """Every resolved setting as nested plain containers (what `resolved_config.json` stores)."""
     return dataclasses.asdict(config)
 
 
 def flatten_resolved(config: dict[str, Any], prefix: str = "") -> dict[str, Any]:
-    """Nested settings as dotted paths. Tuples become lists so a JSON round trip compares equal."""
-    flat: dict[str, Any] = {}
-    for key, value in config.items():
-        path = f"{prefix}{key}"
-        if isinstance(value, dict):
-            flat.update(flatten_resolved(value, path + "."))
-        else:
-            flat[path] = list(value) if isinstance(value, tuple) else value
-    return flat
+    """{"a": {"b": 1}} -> {"a.b": 1}; tuples become lists so values survive a JSON round trip."""
+    out: dict[str, Any] = {}
+    stack: list[tuple[str, Any]] = [(prefix, config)]
+    while stack:
+        path, node = stack.pop()
+        for key, value in node.items():
+            dotted = f"{path}{key}"
+            if isinstance(value, dict):
+                stack.append((dotted + ".", value))
+            else:
+                out[dotted] = list(value) if isinstance(value, tuple) else value
+    return out
 
 
 def diff_resolved(old: dict[str, Any], new: dict[str, Any]) -> dict[str, tuple[Any, Any]]:
-    before, after = flatten_resolved(old), flatten_resolved(new)
-    return {
-        p: (before.get(p), after.get(p))
-        for p in sorted(set(before) | set(after))
-        if before.get(p) != after.get(p)
-    }
+    """Dotted paths whose values differ between two resolved configs -> (old value, new value)."""
+    a, b = flatten_resolved(old), flatten_resolved(new)
+    changed: dict[str, tuple[Any, Any]] = {}
+    for key in sorted(a.keys() | b.keys()):
+        if a.get(key) != b.get(key):
+            changed[key] = (a.get(key), b.get(key))
+    return changed

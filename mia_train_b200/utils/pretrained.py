@@ -1,19 +1,25 @@
-"""`[init]`: start a run from weights trained elsewhere (reference `src/utils/pretrained.py:38-395`).
+"""`[init]`: start a run from weights trained elsewhere.
 
-Reads a `.pth`/`.pt` state dict or a DCP directory (converted through `dcp_to_torch_save`),
-unwraps it from `model` / `state_dict` / `teacher` / `student` nesting, keeps only keys under
-`prefix` (stripped), optionally folds LoRA adapters into their weights, then copies every tensor
-whose name and shape match, inflating 4-D conv kernels to 5-D (in-plane kernel replicated over
-depth and divided by it; input channels averaged to one or spread from one) when asked. Strict mode
-refuses shape mismatches, loads that matched nothing, and unused checkpoint tensors, each with a
-hint naming the likely configuration difference.
+Interface of reference `src/utils/pretrained.py:38-395` (the `[init]` keys and what they mean);
+the implementation is this framework's own. Loading is a short pipeline over a flat
+name -> tensor mapping:
+
+1. `read_state_dict` -- a `.pth` / `.pt` file, or a DCP checkpoint directory converted through
+   `dcp_to_torch_save`; a wrapper dict (`model`, `state_dict`, `teacher`, `student`) is opened.
+2. prefix selection -- keep the keys under `prefix`, with the prefix removed.
+3. LoRA folding (`merge_lora`) -- W <- W + s * B @ A for every adapter in the checkpoint.
+4. matching -- each model tensor takes the checkpoint tensor of the same name: copied when shapes
+   agree, inflated from a 2-D kernel to a 3-D one when `inflate` is set, otherwise a mismatch.
+5. verdict -- in strict mode a mismatch, a load that matched nothing, or checkpoint tensors nobody
+   took (unless `allow_unused`) raise, with a hint about the configuration difference that usually
+   causes them.
 """
 
 from __future__ import annotations
 
 import logging
 import tempfile
-from collections.abc import Sequence
+from collections.abc import Iterable, Sequence
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Any
@@ -23,11 +29,15 @@ import torch.distributed as dist
 import torch.nn as nn
 
 logger = logging.getLogger(__name__)
+
+# Wrapper keys that checkpoints from other trainers put around the weights, in lookup order.
 NESTING_KEYS = ("model", "state_dict", "teacher", "student")
 
 
 @dataclass
 class LoadReport:
+    """What happened to every tensor of the model and of the checkpoint."""
+
     copied: list[str] = field(default_factory=list)
     inflated: list[str] = field(default_factory=list)
     merged: list[str] = field(default_factory=list)
@@ -37,89 +47,121 @@ class LoadReport:
     mismatched: list[tuple[str, tuple[int, ...], tuple[int, ...]]] = field(default_factory=list)
     filtered_by_prefix: list[str] = field(default_factory=list)
 
+    def counts(self) -> dict[str, int]:
+        return {
+            "copied": len(self.copied),
+            "inflated 2D->3D": len(self.inflated),
+            "LoRA adapters merged": len(self.merged),
+            "skipped": len(self.skipped),
+            "kept at initial value": len(self.kept_initial),
+            "unused from checkpoint": len(self.unused),
+            "shape mismatches": len(self.mismatched),
+            "filtered out by prefix": len(self.filtered_by_prefix),
+        }
+
     def summary(self) -> str:
-        parts = [
-            f"{len(self.copied)} copied",
-            f"{len(self.inflated)} inflated 2D->3D",
-            f"{len(self.merged)} LoRA adapters merged",
-            f"{len(self.skipped)} skipped",
-            f"{len(self.kept_initial)} kept at initial value",
-            f"{len(self.unused)} unused from checkpoint",
-        ]
-        if self.mismatched:
-            parts.append(f"{len(self.mismatched)} shape mismatches")
-        if self.filtered_by_prefix:
-            parts.append(f"{len(self.filtered_by_prefix)} filtered out by prefix")
-        return ", ".join(parts)
+        always = {"copied", "inflated 2D->3D", "LoRA adapters merged", "skipped", "kept at initial value",
+                  "unused from checkpoint"}
+        return ", ".join(f"{n} {label}" for label, n in self.counts().items() if n or label in always)
 
 
-def _unwrap(state: Any) -> dict[str, torch.Tensor]:
-    if not isinstance(state, dict):
-        raise ValueError(f"checkpoint is a {type(state).__name__}, not a state dict")
-    for key in NESTING_KEYS:
-        inner = state.get(key)
-        if isinstance(inner, dict) and any(isinstance(v, torch.Tensor) for v in inner.values()):
-            return {k: v for k, v in inner.items() if isinstance(v, torch.Tensor)}
-    tensors = {k: v for k, v in state.items() if isinstance(v, torch.Tensor)}
-    if not tensors:
-        raise ValueError(f"checkpoint holds no tensors at the top level or under any of {list(NESTING_KEYS)}")
-    return tensors
+# ---------------------------------------------------------------------------------------- reading
+def _tensors_of(mapping: dict[str, Any]) -> dict[str, torch.Tensor]:
+    return {k: v for k, v in mapping.items() if isinstance(v, torch.Tensor)}
+
+
+def _open_wrapper(obj: Any) -> dict[str, torch.Tensor]:
+    if not isinstance(obj, dict):
+        raise ValueError(f"expected a state dict, but the checkpoint holds a {type(obj).__name__}")
+    nested = (obj.get(k) for k in NESTING_KEYS)
+    for inner in nested:
+        if isinstance(inner, dict) and _tensors_of(inner):
+            return _tensors_of(inner)
+    own = _tensors_of(obj)
+    if own:
+        return own
+    raise ValueError(f"the checkpoint has no tensors, neither at its top level nor under {', '.join(NESTING_KEYS)}")
 
 
 def read_state_dict(path: str | Path) -> dict[str, torch.Tensor]:
-    path = Path(path)
-    if not path.exists():
-        raise FileNotFoundError(f"no checkpoint at {path}")
-    if path.is_dir():
+    """Name -> tensor (on the CPU) from a torch save file or a DCP directory."""
+    where = Path(path)
+    if where.is_dir():
         from torch.distributed.checkpoint.format_utils import dcp_to_torch_save
 
-        with tempfile.TemporaryDirectory() as scratch:
-            flat = Path(scratch) / "converted.pt"
-            dcp_to_torch_save(str(path), str(flat))
-            return _unwrap(torch.load(flat, map_location="cpu", weights_only=False))
-    return _unwrap(torch.load(path, map_location="cpu", weights_only=False))
+        with tempfile.TemporaryDirectory() as tmp:
+            single = Path(tmp) / "single_file.pt"
+            dcp_to_torch_save(str(where), str(single))
+            return _open_wrapper(torch.load(single, map_location="cpu", weights_only=False))
+    if not where.is_file():
+        raise FileNotFoundError(f"[init] path {where} does not exist")
+    return _open_wrapper(torch.load(where, map_location="cpu", weights_only=False))
 
 
+# ------------------------------------------------------------------------------------ transforms
 def inflate_2d_to_3d(weight: torch.Tensor, target: torch.Size) -> torch.Tensor:
-    if weight.ndim != 4 or len(target) != 5:
-        raise ValueError(f"inflation maps a 4D kernel to a 5D one, got {tuple(weight.shape)} -> {tuple(target)}")
-    out_c, in_c, h, w = weight.shape
-    t_out, t_in, depth, t_h, t_w = target
-    if (out_c, h, w) != (t_out, t_h, t_w):
-        raise ValueError(
-            f"cannot inflate a {tuple(weight.shape)} kernel into {tuple(target)}: output channels and the "
-            "in-plane kernel must already match"
-        )
-    if in_c != t_in:
-        if t_in == 1:
-            weight = weight.mean(dim=1, keepdim=True)
-        elif in_c == 1:
-            weight = weight.expand(-1, t_in, -1, -1) / t_in
+    """A (O, I, h, w) kernel as a (O, I', d, h, w) one whose response to a volume that is constant
+    along depth equals the 2-D kernel's response to one slice: every depth tap gets weight / d.
+    Input channels are averaged down to one, or spread evenly from one."""
+    if weight.dim() != 4 or len(target) != 5:
+        raise ValueError(f"inflation takes a 4-D kernel to a 5-D one; got {tuple(weight.shape)} and {tuple(target)}")
+    o, i, h, w = weight.shape
+    to, ti, d, th, tw = target
+    if (o, h, w) != (to, th, tw):
+        raise ValueError(f"kernel {tuple(weight.shape)} cannot become {tuple(target)}: the output channels and "
+                         "the in-plane size have to agree already")
+    if i != ti:
+        if ti == 1:
+            weight = weight.mean(1, keepdim=True)
+        elif i == 1:
+            weight = weight.repeat(1, ti, 1, 1) / ti
         else:
-            raise ValueError(f"cannot map {in_c} checkpoint input channels onto {t_in}")
-    return (weight.unsqueeze(2).expand(-1, -1, depth, -1, -1) / depth).contiguous()
+            raise ValueError(f"no rule maps {i} input channels onto {ti}")
+    return (weight[:, :, None] / d).repeat(1, 1, d, 1, 1).contiguous()
 
 
 def merge_lora_tensors(checkpoint: dict[str, torch.Tensor]) -> tuple[dict[str, torch.Tensor], list[str]]:
+    """Fold every `<layer>.lora_a/.lora_b/.lora_scaling` triple into `<layer>.weight`."""
+    layers = sorted(k[: -len(".lora_a")] for k in checkpoint if k.endswith(".lora_a"))
     out = dict(checkpoint)
-    folded = []
-    for key in sorted(checkpoint):
-        if not key.endswith(".lora_a"):
-            continue
-        layer = key[: -len(".lora_a")]
-        needed = [f"{layer}.{s}" for s in ("lora_a", "lora_b", "lora_scaling", "weight")]
-        missing = [n for n in needed if n not in out]
-        if missing:
-            raise ValueError(f"cannot merge the LoRA adapter at {layer!r}: the checkpoint is missing {missing}")
-        a = out.pop(f"{layer}.lora_a")
-        b = out.pop(f"{layer}.lora_b")
-        s = out.pop(f"{layer}.lora_scaling")
-        base = out[f"{layer}.weight"]
-        out[f"{layer}.weight"] = base + s.to(base.dtype) * (b.to(base.dtype) @ a.to(base.dtype))
-        folded.append(layer)
-    return out, folded
+    for layer in layers:
+        parts = {s: f"{layer}.{s}" for s in ("lora_a", "lora_b", "lora_scaling", "weight")}
+        absent = [name for name in parts.values() if name not in out]
+        if absent:
+            raise ValueError(f"adapter {layer!r} cannot be folded: {', '.join(absent)} not in the checkpoint")
+        w = out[parts["weight"]]
+        a, b, s = (out.pop(parts[key]).to(w.dtype) for key in ("lora_a", "lora_b", "lora_scaling"))
+        out[parts["weight"]] = torch.addmm(w, b, a, alpha=float(s)) if s.numel() == 1 else w + s * (b @ a)
+    return out, layers
 
 
+# ----------------------------------------------------------------------------------------- hints
+_UNUSED_HINTS = (
+    (("ls1.gamma", "ls2.gamma"), "layerscale_init (the released DINOv3 ViTs use 1.0e-05)"),
+    (("bias_mask",), "mask_k_bias = true"),
+    (("storage_tokens",), "n_storage_tokens (the released DINOv3 ViTs use 4)"),
+)
+
+
+def _hint_for_unused(names: Iterable[str]) -> str:
+    names = list(names)
+    wanted = [fix for needles, fix in _UNUSED_HINTS if any(n in key for key in names for n in needles)]
+    if wanted:
+        return "The checkpoint has parts this model was configured without; consider " + "; ".join(wanted) + "."
+    return "If the extra tensors are expected, set allow_unused = true (or select a sub-tree with prefix)."
+
+
+def _hint_for_mismatch(names: Iterable[str]) -> str:
+    names = list(names)
+    if any("rope_embed" in n for n in names):
+        return ("RoPE period buffers depend on the model's own settings (and on 2-D vs 3-D); "
+                'leave them at their initial values with skip = ["rope_embed."].')
+    if any(n.startswith("patch_embed.") for n in names):
+        return "A 2-D patch embedding needs inflate_2d_to_3d = true and the checkpoint's patch size."
+    return "Compare embed_dim, depth, num_heads and patch_size with the checkpoint's."
+
+
+# ---------------------------------------------------------------------------------------- loading
 def load_pretrained(
     model: nn.Module,
     path: str | Path,
@@ -131,94 +173,67 @@ def load_pretrained(
     allow_unused: bool = False,
     merge_lora: bool = False,
 ) -> LoadReport:
-    checkpoint = read_state_dict(path)
-    filtered: list[str] = []
+    """Copy matching tensors of the checkpoint at `path` into `model` (see the module docstring)."""
+    source = read_state_dict(path)
+    report = LoadReport()
     if prefix:
-        filtered = sorted(k for k in checkpoint if not k.startswith(prefix))
-        checkpoint = {k[len(prefix):]: v for k, v in checkpoint.items() if k.startswith(prefix)}
-    merged: list[str] = []
+        report.filtered_by_prefix = sorted(k for k in source if not k.startswith(prefix))
+        source = {k.removeprefix(prefix): v for k, v in source.items() if k.startswith(prefix)}
     if merge_lora:
-        checkpoint, merged = merge_lora_tensors(checkpoint)
-        if not merged:
-            raise ValueError(f"merge_lora is set but {path} holds no LoRA adapter, so nothing would be merged")
-    targets: dict[str, torch.Tensor] = dict(model.named_parameters())
-    targets.update(model.named_buffers())
-    report = LoadReport(merged=merged, filtered_by_prefix=filtered)
+        source, report.merged = merge_lora_tensors(source)
+        if not report.merged:
+            raise ValueError(f"merge_lora = true, but {path} contains no LoRA adapter to fold")
+
+    def skipped(name: str) -> bool:
+        return any(name.startswith(s) for s in skip)
+
+    destinations = {**dict(model.named_parameters()), **dict(model.named_buffers())}
+    remaining = dict(source)
     with torch.no_grad():
-        for name, dest in targets.items():
-            src = checkpoint.pop(name, None)
-            if any(name.startswith(s) for s in skip):
+        for name, dest in destinations.items():
+            src = remaining.pop(name, None)
+            if skipped(name):
                 report.skipped.append(name)
-                continue
-            if src is None:
+            elif src is None:
                 report.kept_initial.append(name)
             elif src.shape == dest.shape:
                 dest.copy_(src)
                 report.copied.append(name)
-            elif inflate and src.ndim == 4 and dest.ndim == 5:
-                dest.copy_(inflate_2d_to_3d(src, dest.shape).to(dest.dtype))
+            elif inflate and src.dim() == 4 and dest.dim() == 5:
+                dest.copy_(inflate_2d_to_3d(src, dest.shape))
                 report.inflated.append(name)
             else:
                 report.mismatched.append((name, tuple(src.shape), tuple(dest.shape)))
-    report.unused = sorted(k for k in checkpoint if not any(k.startswith(s) for s in skip))
-    logger.info("loaded pretrained weights from %s: %s", path, report.summary())
-    if not strict:
-        return report
-    if report.mismatched:
-        details = "\n".join(f"  {n}: checkpoint {s} vs model {d}" for n, s, d in report.mismatched)
-        raise ValueError(f"{len(report.mismatched)} tensor(s) in {path} do not fit this model:\n{details}\n{_mismatch_hint(report)}")
-    if not report.copied and not report.inflated:
-        raise ValueError(
-            f"nothing in {path} matched this model's parameters; the checkpoint offers keys like "
-            f"{sorted(checkpoint)[:5]}, the model wants {sorted(targets)[:5]}. Set `prefix` if the "
-            "checkpoint stores the encoder under one."
-        )
-    if report.unused and not allow_unused:
-        more = " ..." if len(report.unused) > 6 else ""
-        raise ValueError(
-            f"{len(report.unused)} tensor(s) in {path} have no home in this model: {report.unused[:6]}{more}\n"
-            f"{_unused_hint(report)}"
-        )
-    _log_load(model, Path(path), report)
+    report.unused = sorted(k for k in remaining if not skipped(k))
+    logger.info("[init] %s <- %s: %s", type(model).__name__, path, report.summary())
+    if strict:
+        _enforce(report, path, remaining, destinations, allow_unused)
+    _announce(model, Path(path), report)
     return report
 
 
-def _log_load(model: nn.Module, path: Path, report: LoadReport) -> None:
+def _enforce(report: LoadReport, path: Any, remaining: dict, destinations: dict, allow_unused: bool) -> None:
+    if report.mismatched:
+        rows = "\n".join(f"  {name}: checkpoint {src} vs model {dst}" for name, src, dst in report.mismatched)
+        raise ValueError(f"[init] shapes differ for {len(report.mismatched)} tensor(s) of {path}:\n{rows}\n"
+                         + _hint_for_mismatch(n for n, _, _ in report.mismatched))
+    if not (report.copied or report.inflated):
+        raise ValueError(
+            f"[init] no tensor of {path} fits this model: the checkpoint has e.g. {sorted(remaining)[:5]}, the model "
+            f"e.g. {sorted(destinations)[:5]} (if the weights sit under a sub-tree, set prefix)"
+        )
+    if report.unused and not allow_unused:
+        shown = ", ".join(report.unused[:6]) + (", ..." if len(report.unused) > 6 else "")
+        raise ValueError(f"[init] {len(report.unused)} tensor(s) of {path} found no home in this model ({shown}). "
+                         + _hint_for_unused(report.unused))
+
+
+def _announce(model: nn.Module, path: Path, report: LoadReport) -> None:
     if dist.is_initialized() and dist.get_rank() != 0:
         return
-    print(f"[init] {type(model).__name__} <- {path}", flush=True)
-    print(f"[init]   {report.summary()}", flush=True)
-    for label, names in (
-        ("filtered out by prefix", report.filtered_by_prefix),
-        ("skipped", report.skipped),
-        ("kept at initial value", report.kept_initial),
-        ("unused from checkpoint", report.unused),
-    ):
+    lines = [f"[init] {type(model).__name__} <- {path}", f"[init]   {report.summary()}"]
+    for label, names in (("filtered out by prefix", report.filtered_by_prefix), ("skipped", report.skipped),
+                         ("kept at initial value", report.kept_initial), ("unused from checkpoint", report.unused)):
         if names:
-            more = " ..." if len(names) > 4 else ""
-            print(f"[init]   {len(names)} {label}: {', '.join(names[:4])}{more}", flush=True)
-
-
-def _unused_hint(report: LoadReport) -> str:
-    missing = []
-    if any("ls1.gamma" in k or "ls2.gamma" in k for k in report.unused):
-        missing.append("layerscale_init (the released DINOv3 ViTs use 1.0e-05)")
-    if any("bias_mask" in k for k in report.unused):
-        missing.append("mask_k_bias = true")
-    if any("storage_tokens" in k for k in report.unused):
-        missing.append("n_storage_tokens (the released DINOv3 ViTs use 4)")
-    if missing:
-        return "The model appears to be missing: " + "; ".join(missing) + "."
-    return "Set allow_unused = true if the checkpoint is expected to hold more than this model needs, or `prefix`."
-
-
-def _mismatch_hint(report: LoadReport) -> str:
-    for name, _, _ in report.mismatched:
-        if "rope_embed" in name:
-            return (
-                "rope_embed buffers are derived from the model's own base and differ between 2D and 3D; "
-                'add skip = ["rope_embed."] to [init]'
-            )
-        if name.startswith("patch_embed."):
-            return "Set inflate_2d_to_3d = true and configure the model with the checkpoint's patch size."
-    return "Check that embed_dim, depth, num_heads and patch_size match the checkpoint's."
+            lines.append(f"[init]   {len(names)} {label}: {', '.join(names[:4])}{' ...' if len(names) > 4 else ''}")
+    print("\n".join(lines), flush=True)

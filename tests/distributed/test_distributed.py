@@ -132,3 +132,33 @@ def _prep_failure(rank, world, root):
 def test_prep_failure_reaches_every_rank(run_distributed, tmp_path):
     out = run_distributed(_prep_failure, 2, str(tmp_path), timeout=120)
     assert all("could not prepare" in v for v in out.values())
+
+
+def _device_wait_timeout(rank, world, root, config_path):
+    """Every rank's kernels report an abandoned wait at the first logging step (what the surviving
+    ranks see when a peer is lost): the Trainer must stop with DeviceWaitError, not keep stepping."""
+    import mia_train_b200.engine.trainer as trainer_module
+    from mia_train_b200.engine.run import run
+    from mia_train_b200.ops._native import DeviceWaitError
+
+    calls = []
+
+    def fake_check(device):
+        calls.append(device)
+        raise DeviceWaitError(402, 0)
+
+    trainer_module.raise_on_device_errors = fake_check
+    try:
+        run(Path(config_path), output_root=Path(root), resume=None)
+    except DeviceWaitError as error:
+        return f"raised after {len(calls)} check(s): {error}"
+    return "no error"
+
+
+def test_device_wait_timeout_stops_training(run_distributed, tmp_path):
+    cfg = tmp_path / "dist.toml"
+    cfg.write_text(CONFIG.format(steps=6, parallelism="dp_shard = 2"))
+    out = run_distributed(_device_wait_timeout, 2, str(tmp_path / "runs"), str(cfg), timeout=180)
+    for msg in out.values():
+        assert msg.startswith("raised after 1 check"), msg
+        assert "code 402" in msg

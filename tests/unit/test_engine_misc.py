@@ -109,3 +109,15 @@ def test_profiler_summary_from_synthetic_trace(tmp_path):
     text = summarize(path)
     assert "k1" in text and "forward" in text
     assert union_length([(0, 10), (5, 20), (30, 40)]) == 30
+
+
+def test_raise_on_device_errors_reads_and_reports(monkeypatch):
+    from mia_train_b200.ops import _native
+
+    monkeypatch.setattr(_native, "native_available", lambda: True)
+    codes = iter([0, 402])
+    monkeypatch.setattr(_native, "device_error_code", lambda device: next(codes))
+    _native.raise_on_device_errors(0)  # clean word: nothing raised
+    with pytest.raises(_native.DeviceWaitError, match="gradient-norm exchange"):
+        _native.raise_on_device_errors(0)
+    _native.raise_on_device_errors(torch.device("cpu"))  # CPU: never reads a device word

@@ -14,9 +14,11 @@ from mia_train_b200.evals.semantic_seg import (
 
 def test_tile_starts_cover_and_pull_back():
     assert tile_starts(10, 16, 2) == [0]
-    assert tile_starts(10, 4, 0) == [0, 4, 6]
-    s = tile_starts(100, 32, 8)
-    assert s[0] == 0 and s[-1] == 68 and all(b - a <= 24 for a, b in zip(s, s[1:]))
+    assert tile_starts(10, 4, 0) == [0, 3, 6]  # the fewest tiles, spread evenly
+    for extent, tile, overlap in ((100, 32, 8), (257, 64, 16), (64, 64, 0), (65, 64, 32)):
+        s = tile_starts(extent, tile, overlap)
+        assert s[0] == 0 and s[-1] == max(0, extent - tile)
+        assert all(0 < b - a <= tile - overlap for a, b in zip(s, s[1:]))  # at least `overlap` overlap
 
 
 def test_blend_weight_profile():
