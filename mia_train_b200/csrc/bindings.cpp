@@ -65,6 +65,15 @@ void zero_all_gather(std::vector<int64_t> data_peers, std::vector<int64_t> shado
                      int64_t seg_lo, int64_t shard_len, int64_t bf16_begin, at::Tensor epoch, int64_t rank, int64_t blocks,
                      double timeout_ms, int64_t seq);
 void zero_advance_epoch(at::Tensor epoch);
+void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_full, c10::optional<at::Tensor> bias,
+                c10::optional<at::Tensor> aux, c10::optional<at::Tensor> aux_out, bool b_kmajor, int64_t act,
+                std::vector<int64_t> flag_peers, std::vector<int64_t> send_peers, int64_t send_parity_bytes,
+                int64_t rank, double timeout_ms);
+void tp_gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, c10::optional<at::Tensor> bias,
+                c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> residual,
+                c10::optional<at::Tensor> pre_out, bool b_kmajor, std::vector<int64_t> flag_peers,
+                std::vector<int64_t> recv_peers, int64_t recv_parity_bytes, int64_t rank, double timeout_ms);
+int64_t tp_flag_bytes();
 at::Tensor axial_angles_fwd(at::Tensor coords, std::vector<at::Tensor> freqs);
 void axial_angles_bwd(at::Tensor dangles, at::Tensor coords, std::vector<at::Tensor> freqs,
                       std::vector<at::Tensor> dfreqs);
@@ -106,6 +115,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("zero_norm_exchange", &mia::zero_norm_exchange, "cross-rank grad norm -> clip scale");
   m.def("zero_all_gather", &mia::zero_all_gather, "peer-memory parameter all-gather + local refresh");
   m.def("zero_advance_epoch", &mia::zero_advance_epoch);
+  m.def("tp_ag_gemm", &mia::tp_ag_gemm, "fused all-gather (peer memory) -> tcgen05 GEMM, sequence-parallel input");
+  m.def("tp_gemm_rs", &mia::tp_gemm_rs, "fused tcgen05 GEMM -> reduce-scatter (peer stores) + bias/LayerScale/residual");
+  m.def("tp_flag_bytes", &mia::tp_flag_bytes, "bytes of one rank's flag area for the fused TP kernels");
   m.def("set_tc_attention_mode", &mia::set_tc_attention_mode, "1: tcgen05 attention where it applies (head dim 32 / 64); 0: warp-level kernels");
   m.def("tc_attention_mode", &mia::tc_attention_mode);
   m.def("tc_attention_launches", &mia::tc_attention_launches);

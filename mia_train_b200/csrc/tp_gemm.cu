@@ -1,0 +1,1050 @@
+// Fused tensor-parallel collective GEMMs over NVLink peer memory (sequence-parallel Megatron layout).
+//
+// Under sequence parallelism the residual stream stays sharded by token: rank r of W holds rows
+// [r S, (r + 1) S) of the (M, C) activations, S = M / W. A column-parallel layer (qkv, fc1, and the
+// dX GEMMs of the row-parallel layers in backward) needs every row of its input; a row-parallel
+// layer (proj, fc2, and the dX GEMMs of column-parallel layers) produces partial sums over this
+// rank's share of the features, which are summed over ranks and scattered back by token. Each of
+// the two kernels below does the math and the transfer in one launch:
+//
+//   tp_ag_gemm   D[M, N] = epi( gather_q(A_q)[M, K] . B[N, K]^T ),  A_r = this rank's (S, K) rows.
+//   tp_gemm_rs   O_r[S, N] = epi( sum_q (A_q[M, K] . B_q^T)[rows of rank r] ).
+//
+// Both are persistent tcgen05 GEMMs (one CTA per SM, warp 0 issues TMA, warp 1 issues
+// tcgen05.mma into double-buffered TMEM accumulators, eight epilogue warps drain TMEM). What is
+// added:
+//
+// all-gather -> GEMM. CTA b owns the 128-row blocks b, b + G, ... of the gathered M (G = grid), so
+// every row block is fetched exactly once per GPU and no CTA waits on another CTA of its GPU. Four
+// copy warps per CTA first copy the CTA's local rows (A_r) into this rank's symmetric send buffer
+// and into the gathered output, and publish each block to every peer with a system-scope release
+// flag; then they pull the remote rows of their blocks from the peers' send buffers with 16-byte
+// loads over NVLink (12 in flight per thread) into the gathered output, 128 columns at a time,
+// advancing a shared-memory progress counter. The TMA producer waits on that counter before it
+// loads a K slice of a block's first N tile; the other N tiles of the block re-read the rows from
+// local memory. Blocks whose rows are all local are computed first, so the tensor cores start
+// while the remote rows are still in flight. The gathered A is an output: the backward pass uses
+// it for the weight gradient.
+//
+// GEMM -> reduce-scatter. Tiles are visited starting with the rows owned by the next rank. The
+// epilogue rounds each accumulator row to bf16 and stores it straight into the owner's receive
+// slot (peer stores over NVLink, or local stores for this rank's own rows); when all N tiles of a
+// row block are stored (a per-block counter), the last CTA publishes the block to its owner(s).
+// After its last tile every CTA reduces some of this rank's row blocks: it waits for the block's
+// flags from every rank, sums the W slots in fp32 and applies bias, LayerScale and the residual add
+// before the single bf16 store.
+//
+// Buffers and ordering. Send and receive buffers are double-buffered by the parity of a per-kind
+// epoch counter kept on the device (advanced by the last CTA of every launch, so a captured CUDA
+// graph replays correctly). A rank writes buffer e % 2 in launch e; every peer last read it in
+// launch e - 2, and this rank has proof that every peer finished launch e - 2: in launch e - 1 it
+// waited for data that each peer published at the start of its launch e - 1. Flags hold the epoch
+// of the launch that published, so they only grow. Every rank must issue the same sequence of
+// these launches (every TP layer's forward and backward does, on every rank).
+//
+// Co-residency. CTAs wait on flags that CTAs of other GPUs publish, which in turn may wait on this
+// GPU: the kernels are launched cooperatively, so all CTAs of a launch are resident together.
+// Every wait is bounded (%globaltimer); on expiry the kernel records an error code in the device
+// error word and unwinds (drains its copies and MMAs, frees tensor memory) instead of hanging.
+// No load here uses cluster multicast; peers are read and written with plain 16-byte accesses
+// only, and TMA reads local memory only.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "common.cuh"
+#include "errors.h"
+#include "gemm_common.cuh"
+
+namespace mia {
+namespace tp {
+
+constexpr int kMaxWorld = 8;
+constexpr int kMaxMBlocks = 2048;  // 128-row blocks of the gathered M: M <= 262144
+constexpr int kMaxOwned = 64;      // row blocks per CTA in the all-gather kernel
+constexpr int kEpi = 8;            // epilogue warps
+constexpr int kCopyWarps = 4;
+constexpr int kCopyThreads = 32 * kCopyWarps;
+constexpr int kAgThreads = 64 + 32 * kEpi + kCopyThreads;  // 448
+constexpr int kRsThreads = 64 + 32 * kEpi;                 // 320
+constexpr int kCopyCols = 128;   // columns per copy group (two 64-wide K slices)
+constexpr int kCopyInFlight = 12;
+
+// Flag area of one rank (int32):
+//   ag_ready[src][block]  written by src: its rows of gathered block `block` are in its send buffer
+//   rs_ready[src][block]  written by src: its partial rows of block `block` are in our receive slot
+//   block_count[block]    local: N tiles of a block stored (reduce-scatter)
+//   ctl[]                 local: epochs and exit counters
+constexpr int kAgReady = 0;
+constexpr int kRsReady = kAgReady + kMaxWorld * kMaxMBlocks;
+constexpr int kBlockCount = kRsReady + kMaxWorld * kMaxMBlocks;
+constexpr int kCtl = kBlockCount + kMaxMBlocks;
+constexpr int kCtlAgEpoch = 0, kCtlAgExit = 1, kCtlRsEpoch = 2, kCtlRsExit = 3;
+constexpr int kFlagInts = kCtl + 16;
+
+struct Peers {
+  int64_t p[kMaxWorld];
+};
+
+__device__ __forceinline__ int64_t pick(const Peers& p, int i) {
+  int64_t r = p.p[0];
+#pragma unroll
+  for (int j = 1; j < kMaxWorld; ++j) r = (i == j) ? p.p[j] : r;
+  return r;
+}
+
+__device__ __forceinline__ void st_release_sys(int* addr, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_cta_shared(int* addr, int v) {
+  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(addr)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta_shared(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(addr)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Bounded wait until *flag >= target (system scope). False on timeout (error recorded).
+__device__ __forceinline__ bool wait_flag(const int* flag, int target, uint64_t timeout_ns, volatile int* abort_flag,
+                                          int* err, int code) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t start = globaltimer_ns();
+  while (ld_acquire_sys(flag) < target) {
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (globaltimer_ns() - start > timeout_ns) {
+      record_error(err, code);
+      if (abort_flag != nullptr) *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+struct TpShape {
+  int M, N, K;      // gathered rows, output columns, reduction length
+  int S;            // rows per rank (M = S * world)
+  int rank, world;
+  int num_blocks;   // ceil(M / 128)
+};
+
+__device__ __forceinline__ int block_src_lo(const TpShape& s, int mb) { return (mb * 128) / s.S; }
+__device__ __forceinline__ int block_src_hi(const TpShape& s, int mb) {
+  return (min(mb * 128 + 128, s.M) - 1) / s.S;
+}
+
+// ------------------------------------------------------------------------------- all-gather GEMM
+struct AgParams {
+  GemmParams g;                 // M = gathered rows; D, bias, aux, aux_out, act, err
+  TpShape s;
+  const __nv_bfloat16* a_local; // (S, K)
+  __nv_bfloat16* a_full;        // (M, K) gathered output
+  Peers send;                   // every rank's send area (parity 0; parity 1 at + send_parity_elems)
+  int64_t send_parity_elems;
+  Peers flags;
+  uint64_t timeout_ns;
+};
+
+// Copies rows [0, nrows) x columns [c0, c0 + ncols) (ncols % 8 == 0) from src to dst (row strides in
+// elements), kCopyInFlight 16-byte loads in flight per thread. `ct` is the thread's index among the
+// copy threads. `dst2` (optional) receives the same data with stride ld2.
+template <bool kPeer>
+__device__ __forceinline__ void copy_rows(__nv_bfloat16* dst, int64_t ld_dst, __nv_bfloat16* dst2, int64_t ld2,
+                                          const __nv_bfloat16* src, int64_t ld_src, int nrows, int c0, int ncols,
+                                          int ct) {
+  const int vpr = ncols / 8;
+  const int total = nrows * vpr;
+  for (int base = 0; base < total; base += kCopyThreads * kCopyInFlight) {
+    uint4 buf[kCopyInFlight];
+#pragma unroll
+    for (int u = 0; u < kCopyInFlight; ++u) {
+      const int v = base + u * kCopyThreads + ct;
+      if (v < total) {
+        const int row = v / vpr, col = c0 + (v - row * vpr) * 8;
+        const uint4* sp = reinterpret_cast<const uint4*>(src + (int64_t)row * ld_src + col);
+        buf[u] = kPeer ? __ldcg(sp) : __ldg(sp);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kCopyInFlight; ++u) {
+      const int v = base + u * kCopyThreads + ct;
+      if (v < total) {
+        const int row = v / vpr, col = c0 + (v - row * vpr) * 8;
+        *reinterpret_cast<uint4*>(dst + (int64_t)row * ld_dst + col) = buf[u];
+        if (dst2 != nullptr) *reinterpret_cast<uint4*>(dst2 + (int64_t)row * ld2 + col) = buf[u];
+      }
+    }
+  }
+}
+
+template <int BN, int STAGES>
+struct AgSmem {
+  static constexpr int kBTileBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kBytes = STAGES * kStageBytes + 1024 + 512 + kMaxOwned * 4;
+};
+
+template <int BN, bool B_MN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kAgThreads, 1)
+    tp_ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const AgParams P) {
+  using L = AgSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * kATileBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* progress = reinterpret_cast<int*>(tmem_slot + 2);  // K slices ready, in sequence order
+  int* nseq_slot = reinterpret_cast<int*>(tmem_slot + 3);
+  volatile int* copy_stop = reinterpret_cast<volatile int*>(tmem_slot + 4);
+  int* seq = reinterpret_cast<int*>(smem + STAGES * L::kStageBytes + 512);  // owned blocks, compute order
+
+  const GemmParams& p = P.g;
+  const TpShape& s = P.s;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  const int num_k = (p.K + kBK - 1) / kBK;
+  const int* ctl = reinterpret_cast<const int*>(pick(P.flags, s.rank)) + kCtl;
+  const int epoch = *reinterpret_cast<const volatile int*>(ctl + kCtlAgEpoch) + 1;
+  const int64_t par_off = (epoch & 1) ? P.send_parity_elems : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 32 * kEpi);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *progress = 0;
+    // Compute order: blocks whose rows are all local first, then the rest.
+    int n = 0;
+    for (int pass = 0; pass < 2; ++pass)
+      for (int mb = blockIdx.x; mb < s.num_blocks; mb += gridDim.x) {
+        const bool local = block_src_lo(s, mb) == s.rank && block_src_hi(s, mb) == s.rank;
+        if ((pass == 0) == local && n < kMaxOwned) seq[n++] = mb;
+      }
+    *nseq_slot = n;
+    fence_barrier_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nseq = *nseq_slot;
+  const int num_n = (p.N + BN - 1) / BN;
+  constexpr int kCopyWarp0 = 2 + kEpi;
+
+  if (warp >= kCopyWarp0) {
+    // ---------------- copy warps
+    const int ct = threadIdx.x - 32 * kCopyWarp0;
+    __nv_bfloat16* my_send = reinterpret_cast<__nv_bfloat16*>(pick(P.send, s.rank)) + par_off;
+    const int row_lo = s.rank * s.S, row_hi = row_lo + s.S;
+    // Phase 1: this rank's rows of every owned block -> send buffer and gathered output.
+    int nlocal = 0;
+    for (int i = 0; i < nseq; ++i) {
+      const int mb = seq[i];
+      const int r0 = max(mb * 128, row_lo), r1 = min(min(mb * 128 + 128, s.M), row_hi);
+      if (r0 < r1)
+        copy_rows<false>(P.a_full + (int64_t)r0 * p.K, p.K, my_send + (int64_t)(r0 - row_lo) * p.K, p.K,
+                         P.a_local + (int64_t)(r0 - row_lo) * p.K, p.K, r1 - r0, 0, p.K, ct);
+      if (block_src_lo(s, mb) == s.rank && block_src_hi(s, mb) == s.rank) ++nlocal;
+    }
+    __threadfence_system();
+    fence_proxy_async_global();
+    named_barrier(1, kCopyThreads);
+    if (ct == 0) {
+      st_release_cta_shared(progress, nlocal * num_k);
+      for (int i = 0; i < nseq; ++i) {
+        const int mb = seq[i];
+        if (block_src_lo(s, mb) > s.rank || block_src_hi(s, mb) < s.rank) continue;
+        for (int q = 0; q < s.world; ++q)
+          if (q != s.rank)
+            st_release_sys(reinterpret_cast<int*>(pick(P.flags, q)) + kAgReady + s.rank * kMaxMBlocks + mb, epoch);
+      }
+    }
+    // Phase 2: remote rows of the remaining blocks, in compute order.
+    int done = nlocal * num_k;
+    bool ok = true;
+    const int* my_flags = reinterpret_cast<const int*>(pick(P.flags, s.rank));
+    for (int i = nlocal; i < nseq && ok; ++i) {
+      const int mb = seq[i];
+      const int lo = block_src_lo(s, mb), hi = block_src_hi(s, mb);
+      if (ct < s.world) {
+        const int q = ct;
+        if (q != s.rank && q >= lo && q <= hi &&
+            !wait_flag(my_flags + kAgReady + q * kMaxMBlocks + mb, epoch, P.timeout_ns, abort_flag, p.err,
+                       kErrTpChunkWait))
+          *abort_flag = 1;
+      }
+      // One thread decides for all copy threads (the abort flag may change under their feet).
+      named_barrier(1, kCopyThreads);
+      if (ct == 0) *copy_stop = *abort_flag;
+      named_barrier(1, kCopyThreads);
+      if (*copy_stop) {
+        ok = false;
+        break;
+      }
+      for (int c0 = 0; c0 < p.K; c0 += kCopyCols) {
+        const int ncols = min(kCopyCols, p.K - c0);
+        for (int q = lo; q <= hi; ++q) {
+          if (q == s.rank) continue;
+          const int r0 = max(mb * 128, q * s.S), r1 = min(min(mb * 128 + 128, s.M), (q + 1) * s.S);
+          const __nv_bfloat16* src =
+              reinterpret_cast<const __nv_bfloat16*>(pick(P.send, q)) + par_off + (int64_t)(r0 - q * s.S) * p.K;
+          copy_rows<true>(P.a_full + (int64_t)r0 * p.K, p.K, nullptr, 0, src, p.K, r1 - r0, c0, ncols, ct);
+        }
+        __threadfence();
+        fence_proxy_async_global();
+        named_barrier(1, kCopyThreads);
+        done += (ncols + kBK - 1) / kBK;
+        if (ct == 0) st_release_cta_shared(progress, done);
+      }
+    }
+  } else if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
+      for (int i = 0; i < nseq && ok; ++i) {
+        const int m0 = seq[i] * 128;
+        for (int nt = 0; nt < num_n && ok; ++nt) {
+          const int n0 = nt * BN;
+          for (int kb = 0; kb < num_k; ++kb) {
+            if (nt == 0) {
+              const int need = i * num_k + kb + 1;
+              if (ld_acquire_cta_shared(progress) < need) {
+                const uint64_t t0 = globaltimer_ns();
+                while (ld_acquire_cta_shared(progress) < need) {
+                  if (*abort_flag) {
+                    ok = false;
+                    break;
+                  }
+                  if (globaltimer_ns() - t0 > P.timeout_ns + MIA_WAIT_LIMIT_NS) {
+                    record_error(p.err, kErrTpChunkWait);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                  }
+                }
+                if (!ok) break;
+              }
+              fence_proxy_async_global();
+            }
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
+              ok = false;
+              break;
+            }
+            const int k0 = kb * kBK;
+            mbar_arrive_expect_tx(&full_bar[stage], kTx);
+            uint8_t* a_dst = smA + stage * kATileBytes;
+            uint8_t* b_dst = smB + stage * L::kBTileBytes;
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
+            if (!B_MN) {
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+            }
+            ++issued;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      if (!ok) {
+        int st = stage, ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--st < 0) {
+            st = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(&full_bar[st], ph, nullptr, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, false, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, any = false;
+      for (int i = 0; i < nseq && ok; ++i) {
+        for (int nt = 0; nt < num_n && ok; ++nt) {
+          if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * BN;
+          for (int kb = 0; kb < num_k; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrGemmMmaWait)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(smA + stage * kATileBytes);
+            const uint32_t b_base = smem_u32(smB + stage * L::kBTileBytes);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t a_desc = make_sdesc_sw128(a_base + k * 32, 16, 1024);
+              const uint64_t b_desc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
+                                           : make_sdesc_sw128(b_base + k * 32, 16, 1024);
+              tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              any = true;
+            }
+            tc_commit(&empty_bar[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (!ok) break;
+          tc_commit(&tfull_bar[acc]);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1;
+        }
+      }
+      if (!ok && any) {
+        tc_commit(drain_bar);
+        mbar_wait(drain_bar, 0, nullptr, nullptr, 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..9
+    const int lane_group = warp % 4;
+    const int col_part = (warp - 2) / 4;  // two column halves
+    constexpr int kPartCols = BN / 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int i = 0; i < nseq && ok; ++i) {
+      const int m = seq[i] * 128 + lane_group * 32 + lane;
+      for (int nt = 0; nt < num_n; ++nt) {
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrGemmEpilogueWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int n0 = nt * BN + col_part * kPartCols;
+        const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_part * kPartCols;
+#pragma unroll 1
+        for (int c = 0; c < kPartCols / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait_regs(r);
+          epilogue_chunk<EPI>(p, m, n0 + c * 32, r);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    int* wctl = reinterpret_cast<int*>(pick(P.flags, s.rank)) + kCtl;
+    __threadfence();
+    if (atomicAdd(wctl + kCtlAgExit, 1) == (int)gridDim.x - 1) {
+      wctl[kCtlAgExit] = 0;
+      __threadfence();
+      wctl[kCtlAgEpoch] = epoch;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------- GEMM reduce-scatter
+struct RsParams {
+  TpShape s;
+  int* err;
+  Peers recv;        // every rank's receive area: [parity][src][S][N] bf16
+  int64_t recv_parity_elems;
+  Peers flags;
+  // reduce epilogue: out = residual + gamma * (sum + bias); `pre_out` keeps sum + bias
+  __nv_bfloat16* out;
+  const float* bias;
+  const float* gamma;
+  const __nv_bfloat16* residual;
+  __nv_bfloat16* pre_out;
+  uint64_t timeout_ns;
+  int num_n_tiles, num_tiles, first_block;
+};
+
+template <int BN, int STAGES>
+struct RsSmem {
+  static constexpr int kBTileBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kBytes = STAGES * kStageBytes + 1024 + 512;
+};
+
+__device__ __forceinline__ void rs_tile(const RsParams& P, int tile, int& mb, int& nt) {
+  const int t = tile % P.s.num_blocks;
+  nt = tile / P.s.num_blocks;
+  mb = t + P.first_block;
+  if (mb >= P.s.num_blocks) mb -= P.s.num_blocks;
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+__global__ void __launch_bounds__(kRsThreads, 1)
+    tp_gemm_rs_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const RsParams P) {
+  using L = RsSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * kATileBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* tile_arrivals = reinterpret_cast<int*>(tmem_slot + 2);  // [2], per accumulator
+
+  const TpShape& s = P.s;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  const int num_k = (s.K + kBK - 1) / kBK;
+  int* my_flags = reinterpret_cast<int*>(pick(P.flags, s.rank));
+  const int epoch = *reinterpret_cast<const volatile int*>(my_flags + kCtl + kCtlRsEpoch) + 1;
+  const int64_t par_off = (epoch & 1) ? P.recv_parity_elems : 0;
+  const int64_t slot_elems = (int64_t)s.S * s.N;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 32 * kEpi);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    tile_arrivals[0] = tile_arrivals[1] = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
+      for (int tile = blockIdx.x; tile < P.num_tiles && ok; tile += gridDim.x) {
+        int mb, nt;
+        rs_tile(P, tile, mb, nt);
+        const int m0 = mb * 128, n0 = nt * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, P.err, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          const int k0 = kb * kBK;
+          mbar_arrive_expect_tx(&full_bar[stage], kTx);
+          uint8_t* a_dst = smA + stage * kATileBytes;
+          uint8_t* b_dst = smB + stage * L::kBTileBytes;
+          if (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        int st = stage, ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--st < 0) {
+            st = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(&full_bar[st], ph, nullptr, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, any = false;
+      for (int tile = blockIdx.x; tile < P.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, P.err, kErrGemmMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, P.err, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smA + stage * kATileBytes);
+          const uint32_t b_base = smem_u32(smB + stage * L::kBTileBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t a_desc = A_MN ? make_sdesc_sw128(a_base + k * 2048, 8192, 1024)
+                                         : make_sdesc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t b_desc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
+                                         : make_sdesc_sw128(b_base + k * 32, 16, 1024);
+            tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            any = true;
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (!ok && any) {
+        tc_commit(drain_bar);
+        mbar_wait(drain_bar, 0, nullptr, nullptr, 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps: partial rows -> owner's receive slot
+    const int lane_group = warp % 4;
+    const int col_part = (warp - 2) / 4;
+    constexpr int kPartCols = BN / 2;
+    const int et = threadIdx.x - 64;  // 0 .. 32 * kEpi - 1
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < P.num_tiles; tile += gridDim.x) {
+      int mb, nt;
+      rs_tile(P, tile, mb, nt);
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, P.err, kErrGemmEpilogueWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int m = mb * 128 + lane_group * 32 + lane;
+      const int n0 = nt * BN + col_part * kPartCols;
+      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_part * kPartCols;
+      __nv_bfloat16* dst_row = nullptr;
+      if (m < s.M) {
+        const int owner = m / s.S;
+        dst_row = reinterpret_cast<__nv_bfloat16*>(pick(P.recv, owner)) + par_off + (int64_t)s.rank * slot_elems +
+                  (int64_t)(m - owner * s.S) * s.N;
+      }
+#pragma unroll 1
+      for (int c = 0; c < kPartCols / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait_regs(r);
+        const int n = n0 + c * 32;
+        if (dst_row != nullptr && n < s.N) {
+          if (n + 32 <= s.N) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst_row + n);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              d4[q] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1])),
+                                 pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
+                                 pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
+                                 pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n + j < s.N) dst_row[n + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        }
+      }
+      // Publish the block once all its N tiles are stored (by any CTA of this GPU). The last epilogue
+      // warp of this CTA to finish the tile counts it; a warp arrives before it releases the
+      // accumulator, so the counter of one accumulator never mixes two tiles.
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0 && atomicAdd(&tile_arrivals[acc], 1) == kEpi - 1) {
+        tile_arrivals[acc] = 0;
+        __threadfence_system();
+        int* count = my_flags + kBlockCount + mb;
+        if (atomicAdd(count, 1) == P.num_n_tiles - 1) {
+          *count = 0;
+          const int lo = block_src_lo(s, mb), hi = block_src_hi(s, mb);
+          for (int q = lo; q <= hi; ++q)
+            st_release_sys(reinterpret_cast<int*>(pick(P.flags, q)) + kRsReady + s.rank * kMaxMBlocks + mb, epoch);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    // ---------------- reduce this rank's row blocks (sum of W slots + epilogue)
+    if (ok && !*abort_flag) {
+      const int row_lo = s.rank * s.S, row_hi = row_lo + s.S;
+      const int mb_lo = row_lo / 128, mb_hi = (row_hi - 1) / 128;
+      const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(pick(P.recv, s.rank)) + par_off;
+      const int vpr = s.N / 8;
+      for (int mb = mb_lo + (int)blockIdx.x; mb <= mb_hi; mb += gridDim.x) {
+        // Every thread waits for the block's W slots itself (no barrier that a failed wait could strand).
+        bool ready = true;
+        for (int q = 0; q < s.world && ready; ++q)
+          ready = wait_flag(my_flags + kRsReady + q * kMaxMBlocks + mb, epoch, P.timeout_ns, abort_flag, P.err,
+                            kErrTpSlotWait);
+        if (!ready) break;
+        const int r0 = max(mb * 128, row_lo) - row_lo, r1 = min(mb * 128 + 128, row_hi) - row_lo;
+        const int total = (r1 - r0) * vpr;
+        for (int v = et; v < total; v += 32 * kEpi) {
+          const int lr = r0 + v / vpr, n = (v % vpr) * 8;
+          float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          for (int q = 0; q < s.world; ++q) {
+            const uint4 u = __ldcg(reinterpret_cast<const uint4*>(recv + q * slot_elems + (int64_t)lr * s.N + n));
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              a[2 * h] += bf16_lo(w[h]);
+              a[2 * h + 1] += bf16_hi(w[h]);
+            }
+          }
+          if (P.bias != nullptr) {
+            const float4 b0 = __ldg(reinterpret_cast<const float4*>(P.bias + n));
+            const float4 b1 = __ldg(reinterpret_cast<const float4*>(P.bias + n + 4));
+            a[0] += b0.x; a[1] += b0.y; a[2] += b0.z; a[3] += b0.w;
+            a[4] += b1.x; a[5] += b1.y; a[6] += b1.z; a[7] += b1.w;
+          }
+          const int64_t o = (int64_t)lr * s.N + n;
+          if (P.pre_out != nullptr)
+            *reinterpret_cast<uint4*>(P.pre_out + o) =
+                make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+          if (P.gamma != nullptr) {
+            const float4 g0 = __ldg(reinterpret_cast<const float4*>(P.gamma + n));
+            const float4 g1 = __ldg(reinterpret_cast<const float4*>(P.gamma + n + 4));
+            a[0] *= g0.x; a[1] *= g0.y; a[2] *= g0.z; a[3] *= g0.w;
+            a[4] *= g1.x; a[5] *= g1.y; a[6] *= g1.z; a[7] *= g1.w;
+          }
+          if (P.residual != nullptr) {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(P.residual + o));
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              a[2 * h] += bf16_lo(w[h]);
+              a[2 * h + 1] += bf16_hi(w[h]);
+            }
+          }
+          *reinterpret_cast<uint4*>(P.out + o) =
+              make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(my_flags + kCtl + kCtlRsExit, 1) == (int)gridDim.x - 1) {
+      my_flags[kCtl + kCtlRsExit] = 0;
+      __threadfence();
+      my_flags[kCtl + kCtlRsEpoch] = epoch;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------- host
+Peers to_peers(const std::vector<int64_t>& v, int world, const char* what) {
+  TORCH_CHECK((int)v.size() == world && world >= 1 && world <= kMaxWorld, what, ": expected ", world,
+              " peer pointers (world 1..", kMaxWorld, ")");
+  Peers p{};
+  for (int i = 0; i < world; ++i) {
+    TORCH_CHECK(v[i] != 0 && (v[i] & 255) == 0, what, ": peer pointers must be non-null and 256-byte aligned");
+    p.p[i] = v[i];
+  }
+  return p;
+}
+
+template <typename Kern, typename Params>
+void coop_launch(Kern kern, int grid, int threads, int smem_bytes, cudaStream_t stream, const CUtensorMap& ta,
+                 const CUtensorMap& tb, const Params& prm) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, prm));
+}
+
+int64_t flag_bytes() { return (int64_t)kFlagInts * 4; }
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <int BN, bool B_MN, int EPI>
+static void launch_ag(const CUtensorMap& ta, const CUtensorMap& tb, const AgParams& prm, int grid, cudaStream_t st,
+                      int device) {
+  constexpr int ST = BN == 256 ? 4 : 6;
+  using L = AgSmem<BN, ST>;
+  auto kern = tp_ag_gemm_kernel<BN, B_MN, ST, EPI>;
+  static bool configured[64] = {false};
+  if (!configured[device]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    configured[device] = true;
+  }
+  coop_launch(kern, grid, kAgThreads, L::kBytes, st, ta, tb, prm);
+}
+
+template <int BN, bool B_MN>
+static void dispatch_ag_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const AgParams& prm, int grid,
+                            cudaStream_t st, int device) {
+  if (epi == kEpiGelu) launch_ag<BN, B_MN, kEpiGelu>(ta, tb, prm, grid, st, device);
+  else if (epi == kEpiDGelu) launch_ag<BN, B_MN, kEpiDGelu>(ta, tb, prm, grid, st, device);
+  else launch_ag<BN, B_MN, kEpiPlain>(ta, tb, prm, grid, st, device);
+}
+
+}  // namespace tp
+
+// D = epi(gather(A) . B^T). a_local (S, K) bf16 this rank's rows; b (N, K) (b_kmajor) or (K, N);
+// out (M, N) bf16; a_full (M, K) bf16 receives the gathered A. `send_peers[q]` is rank q's send area
+// (two parities of `send_parity_bytes` each), `flag_peers[q]` its flag area.
+void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_full, c10::optional<at::Tensor> bias,
+                c10::optional<at::Tensor> aux, c10::optional<at::Tensor> aux_out, bool b_kmajor, int64_t act,
+                std::vector<int64_t> flag_peers, std::vector<int64_t> send_peers, int64_t send_parity_bytes,
+                int64_t rank, double timeout_ms) {
+  using namespace tp;
+  const int world = (int)flag_peers.size();
+  TORCH_CHECK(a_local.is_cuda() && a_local.scalar_type() == at::kBFloat16 && a_local.dim() == 2 &&
+                  a_local.is_contiguous(),
+              "tp_ag_gemm: a_local must be a contiguous bf16 (S, K) CUDA matrix");
+  const int64_t S = a_local.size(0), K = a_local.size(1), M = S * world;
+  TORCH_CHECK(b.scalar_type() == at::kBFloat16 && b.dim() == 2 && b.is_contiguous(), "tp_ag_gemm: bf16 B expected");
+  const int64_t N = b_kmajor ? b.size(0) : b.size(1);
+  TORCH_CHECK((b_kmajor ? b.size(1) : b.size(0)) == K, "tp_ag_gemm: K mismatch");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(0) == M && out.size(1) == N,
+              "tp_ag_gemm: out must be a contiguous bf16 (M, N) matrix");
+  TORCH_CHECK(a_full.scalar_type() == at::kBFloat16 && a_full.is_contiguous() && a_full.size(0) == M &&
+                  a_full.size(1) == K,
+              "tp_ag_gemm: a_full must be a contiguous bf16 (M, K) matrix");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0 && S >= 1, "tp_ag_gemm: K and N must be multiples of 8");
+  TORCH_CHECK((M + 127) / 128 <= kMaxMBlocks, "tp_ag_gemm: at most ", kMaxMBlocks * 128, " gathered rows");
+  TORCH_CHECK(S * K * 2 <= send_parity_bytes, "tp_ag_gemm: send buffer too small (", send_parity_bytes, " bytes for ",
+              S * K * 2, ")");
+  TORCH_CHECK(send_parity_bytes % 256 == 0, "tp_ag_gemm: send parity stride must be a multiple of 256 bytes");
+  TORCH_CHECK(al16(a_local.data_ptr()) && al16(b.data_ptr()) && al16(out.data_ptr()) && al16(a_full.data_ptr()),
+              "tp_ag_gemm: 16-byte aligned operands expected");
+  TORCH_CHECK(rank >= 0 && rank < world, "tp_ag_gemm: rank out of range");
+  TORCH_CHECK(act != kActDGelu || aux.has_value(), "tp_ag_gemm: GELU' needs aux");
+  c10::cuda::CUDAGuard guard(a_local.device());
+  const int device = a_local.get_device();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+
+  AgParams prm{};
+  GemmParams& p = prm.g;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.D = out.data_ptr();
+  p.act = (int)act;
+  p.splits = 1;
+  p.err = error_word(device);
+  auto vec = [&](const c10::optional<at::Tensor>& t) -> const float* {
+    if (!t.has_value()) return nullptr;
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == N,
+                "tp_ag_gemm: bias must be a contiguous fp32 vector of length N");
+    return t->data_ptr<float>();
+  };
+  auto mat = [&](const c10::optional<at::Tensor>& t) -> __nv_bfloat16* {
+    if (!t.has_value()) return nullptr;
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->size(0) == M && t->size(1) == N &&
+                    al16(t->data_ptr()),
+                "tp_ag_gemm: aux tensors must be contiguous bf16 (M, N) matrices");
+    return reinterpret_cast<__nv_bfloat16*>(t->data_ptr());
+  };
+  p.bias = vec(bias);
+  p.aux = mat(aux);
+  p.aux_out = mat(aux_out);
+  prm.s = TpShape{(int)M, (int)N, (int)K, (int)S, (int)rank, world, (int)((M + 127) / 128)};
+  prm.a_local = reinterpret_cast<const __nv_bfloat16*>(a_local.data_ptr());
+  prm.a_full = reinterpret_cast<__nv_bfloat16*>(a_full.data_ptr());
+  prm.send = to_peers(send_peers, world, "tp_ag_gemm send");
+  prm.send_parity_elems = send_parity_bytes / 2;
+  prm.flags = to_peers(flag_peers, world, "tp_ag_gemm flags");
+  prm.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms * 1e6 : 5e9);
+
+  const int grid = (int)std::min<int64_t>(prm.s.num_blocks, sm_count(device));
+  TORCH_CHECK(prm.s.num_blocks <= (int64_t)grid * kMaxOwned, "tp_ag_gemm: too many row blocks per CTA");
+  const int bn = N <= 128 ? 128 : 256;
+  const int epi = act == kActGelu ? kEpiGelu : (act == kActDGelu ? kEpiDGelu : kEpiPlain);
+  CUtensorMap ta = make_bf16_map(a_full.data_ptr(), K, M, K, 64, kBM);
+  CUtensorMap tb = b_kmajor ? make_bf16_map(b.data_ptr(), K, N, K, 64, bn) : make_bf16_map(b.data_ptr(), N, K, N, 64, 64);
+  if (bn == 256) {
+    if (b_kmajor) dispatch_ag_epi<256, false>(epi, ta, tb, prm, grid, stream, device);
+    else dispatch_ag_epi<256, true>(epi, ta, tb, prm, grid, stream, device);
+  } else {
+    if (b_kmajor) dispatch_ag_epi<128, false>(epi, ta, tb, prm, grid, stream, device);
+    else dispatch_ag_epi<128, true>(epi, ta, tb, prm, grid, stream, device);
+  }
+}
+
+namespace tp {
+template <int BN, bool A_MN, bool B_MN>
+static void launch_rs(const CUtensorMap& ta, const CUtensorMap& tb, const RsParams& prm, int grid, cudaStream_t st,
+                      int device) {
+  constexpr int ST = BN == 256 ? 4 : 6;
+  using L = RsSmem<BN, ST>;
+  auto kern = tp_gemm_rs_kernel<BN, A_MN, B_MN, ST>;
+  static bool configured[64] = {false};
+  if (!configured[device]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    configured[device] = true;
+  }
+  coop_launch(kern, grid, kRsThreads, L::kBytes, st, ta, tb, prm);
+}
+}  // namespace tp
+
+// O_r = residual + gamma * (sum_q (A_q . B_q^T)[rows of r] + bias). a (M, K) bf16 (K-major) holds
+// every row of this rank's partial product input; b (N, K) (b_kmajor) or (K, N); out (S, N) bf16
+// with S = M / world. `recv_peers[q]` is rank q's receive area (two parities of
+// `recv_parity_bytes`, each holding world slots of S x N bf16). `pre_out` (S, N) keeps sum + bias.
+void tp_gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, c10::optional<at::Tensor> bias,
+                c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> residual,
+                c10::optional<at::Tensor> pre_out, bool b_kmajor, std::vector<int64_t> flag_peers,
+                std::vector<int64_t> recv_peers, int64_t recv_parity_bytes, int64_t rank, double timeout_ms) {
+  using namespace tp;
+  const int world = (int)flag_peers.size();
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.dim() == 2 && a.is_contiguous(),
+              "tp_gemm_rs: a must be a contiguous bf16 (M, K) CUDA matrix");
+  const int64_t M = a.size(0), K = a.size(1);
+  TORCH_CHECK(M % world == 0, "tp_gemm_rs: M must be divisible by the world size");
+  const int64_t S = M / world;
+  TORCH_CHECK(b.scalar_type() == at::kBFloat16 && b.dim() == 2 && b.is_contiguous(), "tp_gemm_rs: bf16 B expected");
+  const int64_t N = b_kmajor ? b.size(0) : b.size(1);
+  TORCH_CHECK((b_kmajor ? b.size(1) : b.size(0)) == K, "tp_gemm_rs: K mismatch");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(0) == S && out.size(1) == N,
+              "tp_gemm_rs: out must be a contiguous bf16 (M / world, N) matrix");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0, "tp_gemm_rs: K and N must be multiples of 8");
+  TORCH_CHECK((M + 127) / 128 <= kMaxMBlocks, "tp_gemm_rs: at most ", kMaxMBlocks * 128, " rows");
+  TORCH_CHECK((int64_t)world * S * N * 2 <= recv_parity_bytes && recv_parity_bytes % 256 == 0,
+              "tp_gemm_rs: receive buffer too small or misaligned");
+  TORCH_CHECK(al16(a.data_ptr()) && al16(b.data_ptr()) && al16(out.data_ptr()), "tp_gemm_rs: 16-byte aligned operands");
+  TORCH_CHECK(rank >= 0 && rank < world, "tp_gemm_rs: rank out of range");
+  c10::cuda::CUDAGuard guard(a.device());
+  const int device = a.get_device();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+
+  RsParams prm{};
+  prm.s = TpShape{(int)M, (int)N, (int)K, (int)S, (int)rank, world, (int)((M + 127) / 128)};
+  prm.err = error_word(device);
+  prm.recv = to_peers(recv_peers, world, "tp_gemm_rs recv");
+  prm.recv_parity_elems = recv_parity_bytes / 2;
+  prm.flags = to_peers(flag_peers, world, "tp_gemm_rs flags");
+  prm.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  auto vec = [&](const c10::optional<at::Tensor>& t) -> const float* {
+    if (!t.has_value()) return nullptr;
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == N,
+                "tp_gemm_rs: bias / gamma must be contiguous fp32 vectors of length N");
+    return t->data_ptr<float>();
+  };
+  auto mat = [&](const c10::optional<at::Tensor>& t) -> __nv_bfloat16* {
+    if (!t.has_value()) return nullptr;
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->size(0) == S && t->size(1) == N &&
+                    al16(t->data_ptr()),
+                "tp_gemm_rs: residual / pre_out must be contiguous bf16 (M / world, N) matrices");
+    return reinterpret_cast<__nv_bfloat16*>(t->data_ptr());
+  };
+  prm.bias = vec(bias);
+  prm.gamma = vec(gamma);
+  prm.residual = mat(residual);
+  prm.pre_out = mat(pre_out);
+  prm.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms * 1e6 : 5e9);
+  const int bn = N <= 128 ? 128 : 256;
+  prm.num_n_tiles = (int)((N + bn - 1) / bn);
+  prm.num_tiles = prm.s.num_blocks * prm.num_n_tiles;
+  // start with the first row block owned by the next rank
+  prm.first_block = (int)((((rank + 1) % world) * S) / 128);
+  const int grid = std::min(prm.num_tiles, sm_count(device));
+  CUtensorMap ta = make_bf16_map(a.data_ptr(), K, M, K, 64, kBM);
+  CUtensorMap tb = b_kmajor ? make_bf16_map(b.data_ptr(), K, N, K, 64, bn) : make_bf16_map(b.data_ptr(), N, K, N, 64, 64);
+  if (bn == 256) {
+    if (b_kmajor) launch_rs<256, false, false>(ta, tb, prm, grid, stream, device);
+    else launch_rs<256, false, true>(ta, tb, prm, grid, stream, device);
+  } else {
+    if (b_kmajor) launch_rs<128, false, false>(ta, tb, prm, grid, stream, device);
+    else launch_rs<128, false, true>(ta, tb, prm, grid, stream, device);
+  }
+}
+
+int64_t tp_flag_bytes() { return tp::flag_bytes(); }
+
+}  // namespace mia

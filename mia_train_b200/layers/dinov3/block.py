@@ -119,7 +119,33 @@ class SelfAttentionBlock(nn.Module):
             return self._dropped_list(x_list, rope_list)
         return self._fused_list(x_list, rope_list)
 
-    def forward(self, x_or_x_list, rope_or_rope_list=None):
+    def _forward_with_attention(self, x: torch.Tensor, attention: Callable) -> torch.Tensor:
+        """The block on one tensor with a caller-provided attention core `attention(attn, qkv) -> out`."""
+        if self.training and self.sample_drop_ratio > 0:
+            raise NotImplementedError("blocks with a custom attention core do not support drop_path > 0")
+        h = _norm(self.norm1, x)
+        out = attention(self.attn, self.attn._qkv(h))
+        from ..common.lora import apply_linear
+
+        x_attn = apply_linear(self.attn.proj, out, residual=x, gamma=self._gamma(self.ls1))
+        return self.mlp.forward(_norm(self.norm2, x_attn), residual=x_attn, gamma=self._gamma(self.ls2))
+
+    def forward(self, x_or_x_list, rope_or_rope_list=None, *, attention: Callable | None = None, sp=None,
+                tokens: tuple[int, int] | None = None):
+        """`attention(attn, qkv) -> out` replaces the global attention core (windowed blocks); with `sp`
+        (a `parallel.sequence_parallel.SequenceParallel`) the input is this rank's token rows of a
+        (B, T) token matrix, `tokens = (B, T)`, and the block runs sequence-parallel."""
+        if sp is not None:
+            from ...parallel.sequence_parallel import block_forward
+
+            if self.training and self.sample_drop_ratio > 0:
+                raise NotImplementedError("sequence-parallel blocks do not support drop_path > 0")
+            rope = rope_or_rope_list
+            core = attention or (lambda attn, qkv: attn.compute_attention(qkv, rope=rope))
+            b, t = tokens
+            return block_forward(self, x_or_x_list, sp, lambda qkv: core(self.attn, qkv), b, t)
+        if attention is not None:
+            return self._forward_with_attention(x_or_x_list, attention)
         if isinstance(x_or_x_list, torch.Tensor):
             return self._forward_list([x_or_x_list], rope_list=[rope_or_rope_list])[0]
         if isinstance(x_or_x_list, list):

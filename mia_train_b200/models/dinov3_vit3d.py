@@ -222,6 +222,9 @@ class DinoVisionTransformer3D(BaseModel):
     def _run_blocks(self, tokens_list: list[torch.Tensor], grids: list[tuple[int, int, int]],
                     take: set[int] | None = None) -> tuple[list[torch.Tensor], list[list[torch.Tensor]]]:
         shared = None if self._rope_augmented() else [self._rope(g) for g in grids]
+        sp = getattr(self, "_sequence_parallel", None)
+        if sp is not None:
+            return self._run_blocks_sequence_parallel(sp, tokens_list, grids, shared, take)
         taken: list[list[torch.Tensor]] = []
         for i, blk in enumerate(self.blocks):
             ropes = shared if shared is not None else [self._rope(g) for g in grids]
@@ -234,6 +237,34 @@ class DinoVisionTransformer3D(BaseModel):
             if take is not None and i in take:
                 taken.append(list(tokens_list))
         return tokens_list, taken
+
+    def _run_blocks_sequence_parallel(self, sp, tokens_list, grids, shared, take):
+        """Blocks on this rank's token rows (crop by crop); tokens are gathered again after the last block."""
+        from .windowed import windowed_core
+
+        outs: list[torch.Tensor] = []
+        taken: list[list[torch.Tensor]] = [[] for _ in self.blocks] if take is not None else []
+        for c, (tok, grid) in enumerate(zip(tokens_list, grids, strict=True)):
+            b, t, _ = tok.shape
+            x_r, _ = sp.split(tok)
+            for i, blk in enumerate(self.blocks):
+                rope = shared[c] if shared is not None else self._rope(grid)
+                core = windowed_core(grid, rope, self.n_prefix, self.window_size) if self.is_windowed(i) else None
+                x_r = blk(x_r, rope, attention=core, sp=sp, tokens=(b, t))
+                if take is not None and i in take:
+                    taken[i].append(sp.gather(x_r, b, t))
+            outs.append(sp.gather(x_r, b, t))
+        if take is not None:
+            taken = [t for i, t in enumerate(taken) if i in take]
+        return outs, taken
+
+    def enable_sequence_parallel(self, sp) -> None:
+        """Run the blocks sequence-parallel (`parallel.sequence_parallel.SequenceParallel`); call after
+        the blocks were sharded by `apply_tensor_parallel`."""
+        from ..parallel.sequence_parallel import mark_partial_params
+
+        self._sequence_parallel = sp
+        mark_partial_params(list(self.blocks), sp.group)
 
     def _windowed_block(self, blk: SelfAttentionBlock, x: torch.Tensor, grid, rope) -> torch.Tensor:
         """One block with window attention for patch tokens and global attention for the prefix."""

@@ -12,11 +12,12 @@ Cost per block: `N (w^3 + P)` key interactions instead of `N^2` -- for a 32^3 gr
 
 from __future__ import annotations
 
+import functools
+
 import torch
 import torch.nn.functional as F
 
-from ..layers.common.lora import apply_linear
-from ..layers.dinov3.block import SelfAttentionBlock, _norm
+from ..layers.dinov3.block import SelfAttentionBlock
 from ..layers.dinov3.rope import RopeTables
 from ..ops.attention import attention, rope_attention, rotate_pairs
 from ..parallel.tensor_parallel import rope_to_tp
@@ -38,24 +39,22 @@ def window_merge(x: torch.Tensor, b: int, grid: tuple[int, int, int], w: int) ->
     return x.reshape(b, d * h * ww, c)
 
 
-def windowed_block_forward(
-    blk: SelfAttentionBlock,
-    x: torch.Tensor,
+def windowed_attention(
+    attn,
+    qkv: torch.Tensor,
     grid: tuple[int, int, int],
     rope: RopeTables | None,
     n_prefix: int,
     w: int,
 ) -> torch.Tensor:
-    if blk.training and blk.sample_drop_ratio > 0:
-        raise NotImplementedError("windowed blocks do not support drop_path > 0")
+    """(B, P + N, 3 C) projections -> (B, P + N, C): patch queries attend within their window plus the
+    prefix tokens, prefix queries attend to every token. C is this rank's share of the width under
+    tensor parallelism."""
     if any(g % w for g in grid):
         raise ValueError(f"patch grid {grid} is not divisible by window_size {w}")
-    attn = blk.attn
-    b, n_tok, _ = x.shape
+    b, n_tok, _ = qkv.shape
     heads, hd = attn.num_heads, attn.head_dim
-    c = heads * hd  # this rank's share of the width under tensor parallelism
-    h = _norm(blk.norm1, x)
-    qkv = attn._qkv(h)  # (B, P + N, 3C)
+    c = heads * hd
     pre, pat = qkv[:, :n_prefix], qkv[:, n_prefix:]
     nwin = (grid[0] // w) * (grid[1] // w) * (grid[2] // w)
     win = window_partition(pat, grid, w)  # (B*nw, w^3, 3C)
@@ -67,7 +66,7 @@ def windowed_block_forward(
         ang_w = window_partition(ang.unsqueeze(0), grid, w)  # (nw, w^3, D/2)
         ang_w = F.pad(ang_w, (0, 0, n_prefix, 0))
         angles_win = ang_w.repeat(b, 1, 1)
-        pairs = attn._pairs_on(x.device)
+        pairs = attn._pairs_on(qkv.device)
     out_win = rope_attention(packed, angles_win, pairs, attn.scale)[:, n_prefix:]  # (B*nw, w^3, H, hd)
     out_pat = window_merge(out_win.reshape(b * nwin, w**3, c), b, grid, w)
     # prefix queries attend to every token (keys of patches rotated by their angles)
@@ -78,7 +77,25 @@ def windowed_block_forward(
         full = F.pad(rope_to_tp(rope.angles.float(), attn), (0, 0, n_prefix, 0)).unsqueeze(0)
         k_all = rotate_pairs(k_all, full, pairs)
     out_pre = attention(q_pre.contiguous(), k_all.contiguous(), v_all.contiguous(), attn.scale).reshape(b, n_prefix, c)
-    out = torch.cat([out_pre, out_pat.to(out_pre.dtype)], dim=1)
-    gamma1 = blk._gamma(blk.ls1)
-    x_attn = apply_linear(attn.proj, out, residual=x, gamma=gamma1)
-    return blk.mlp.forward(_norm(blk.norm2, x_attn), residual=x_attn, gamma=blk._gamma(blk.ls2))
+    return torch.cat([out_pre, out_pat.to(out_pre.dtype)], dim=1)
+
+
+def windowed_core(grid: tuple[int, int, int], rope: RopeTables | None, n_prefix: int, w: int):
+    """The attention core of a windowed block, for `SelfAttentionBlock.forward(..., attention=...)`."""
+    return functools.partial(_windowed_core, grid=grid, rope=rope, n_prefix=n_prefix, w=w)
+
+
+def _windowed_core(attn, qkv, *, grid, rope, n_prefix, w):
+    return windowed_attention(attn, qkv, grid, rope, n_prefix, w)
+
+
+def windowed_block_forward(
+    blk: SelfAttentionBlock,
+    x: torch.Tensor,
+    grid: tuple[int, int, int],
+    rope: RopeTables | None,
+    n_prefix: int,
+    w: int,
+) -> torch.Tensor:
+    """One block (or its activation-checkpoint wrapper) with windowed attention."""
+    return blk(x, rope, attention=windowed_core(grid, rope, n_prefix, w))

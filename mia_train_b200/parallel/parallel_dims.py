@@ -9,6 +9,10 @@ New keys (defaults keep reference configs valid):
   resharding per block); `"model"` reproduces the reference's two coarse units.
 * `param_dtype` -- dtype FSDP2 all-gathers parameters in (`"bf16"` halves the traffic of the
   reference's fp32 gather; `"fp32"` reproduces it). Gradients are always reduced in fp32.
+* `tp_comm` -- how tensor-parallel blocks communicate: `"fused"` (sequence-parallel, the
+  all-gather -> GEMM and GEMM -> reduce-scatter kernels over NVLink peer memory; on CPU the same
+  layout on collectives), `"collective"` (sequence-parallel on NCCL / Gloo collectives) or
+  `"allreduce"` (replicated activations, one all-reduce per row-parallel layer).
 """
 
 from __future__ import annotations
@@ -20,6 +24,7 @@ from torch.distributed.device_mesh import DeviceMesh, init_device_mesh
 
 FSDP_UNITS = ("block", "model")
 PARAM_DTYPES = ("bf16", "fp32")
+TP_COMMS = ("fused", "collective", "allreduce")
 
 
 @dataclass(frozen=True)
@@ -29,6 +34,7 @@ class ParallelDims:
     tp: int = 1
     fsdp_unit: str = "block"
     param_dtype: str = "bf16"
+    tp_comm: str = "fused"
 
     def __post_init__(self) -> None:
         sizes = {"dp_replicate": self.dp_replicate, "dp_shard": self.dp_shard, "tp": self.tp}
@@ -39,6 +45,8 @@ class ParallelDims:
             raise ValueError(f"[parallelism]: fsdp_unit {self.fsdp_unit!r} is not one of {', '.join(FSDP_UNITS)}")
         if self.param_dtype not in PARAM_DTYPES:
             raise ValueError(f"[parallelism]: param_dtype {self.param_dtype!r} is not one of {', '.join(PARAM_DTYPES)}")
+        if self.tp_comm not in TP_COMMS:
+            raise ValueError(f"[parallelism]: tp_comm {self.tp_comm!r} is not one of {', '.join(TP_COMMS)}")
 
     @property
     def world_size(self) -> int:

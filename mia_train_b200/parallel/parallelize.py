@@ -44,7 +44,14 @@ def _apply_tensor_parallel(model: nn.Module, mesh: DeviceMesh, dims: ParallelDim
             f"{type(model).__name__} does not define a tensor_parallel_plan(), but tp={dims.tp} was requested"
         )
     if isinstance(plan, BlockTensorParallelPlan):
-        apply_tensor_parallel(plan, mesh["tp"].get_group())
+        group = mesh["tp"].get_group()
+        apply_tensor_parallel(plan, group)
+        enable = getattr(model, "enable_sequence_parallel", None)
+        if dims.tp_comm != "allreduce" and enable is not None:
+            from ..ops.tp import TpComm
+            from .sequence_parallel import SequenceParallel
+
+            enable(SequenceParallel(TpComm(group, dims.tp_comm)))
         return
     parallelize_module(model, mesh["tp"], plan)
     prepare = getattr(model, "after_tensor_parallel", None)

@@ -1,4 +1,6 @@
-"""Tensor parallelism on 2 GPUs with the native kernels (NCCL collectives) against the dense model."""
+"""Tensor parallelism on 2 GPUs with the native kernels against the dense model: replicated
+activations with NCCL all-reduces, and sequence parallelism on NCCL collectives or on the fused
+all-gather -> GEMM / GEMM -> reduce-scatter kernels over NVLink peer memory."""
 
 from __future__ import annotations
 
@@ -17,15 +19,18 @@ WORKER = Path(__file__).with_name("tp_worker.py")
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp_dinov3_matches_dense():
+@pytest.mark.parametrize("mode,port", [("allreduce", 29533), ("collective", 29534), ("fused", 29535)])
+def test_tp_dinov3_matches_dense(mode, port):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29533", str(WORKER)]
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(port), str(WORKER), mode]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert out.returncode == 0, out.stderr[-4000:]
     res = json.loads([x for x in out.stdout.splitlines() if x.startswith("{")][-1])
     assert res["errors"] == 0
-    assert res["sharded_layers"] == 2 * 5  # qkv, proj, SwiGLU w1 / w2 / w3 per block
+    assert res["mode"] == mode
+    # qkv, proj and SwiGLU w1 / w2 / w3, or the GELU MLP's fc1 / fc2, per block
+    assert res["sharded_layers"] == 2 * (5 if mode == "allreduce" else 4)
     assert abs(res["loss"] - res["ref"]) < 2e-2 * max(1.0, abs(res["ref"]))
     assert res["grad_rel"] < 0.05, res  # relative L2 error of every replicated parameter's gradient
     assert res["shard_rel"] < 0.05, res
