@@ -65,6 +65,11 @@ def parse() -> argparse.Namespace:
                     help="data-parallel gradient path for N > 1 (sharded optimizer over peer memory by default)")
     ap.add_argument("--profile-kernels", type=int, default=0, metavar="STEPS",
                     help="also profile STEPS eager steps and print the per-kernel device-time table")
+    ap.add_argument("--config", choices=("vit_l_mae", "windowed_tp"), default="vit_l_mae",
+                    help="vit_l_mae: ViT-L 3D MAE at 128^3 (the default headline workload); windowed_tp: windowed "
+                         "dinov3_vit3d ViT-L SimMIM at 256^3 / patch 8 under sequence-parallel TP (TP = min(4, N))")
+    ap.add_argument("--tp-comm", choices=("fused", "collective"), default="fused",
+                    help="windowed_tp: fused collective-GEMM kernels over NVLink, or NCCL collectives")
     return ap.parse_args()
 
 
@@ -453,9 +458,77 @@ def reference_arm(args: argparse.Namespace, rank: int, world: int, local: int) -
     return {"ms": ms, "flops": step_flops, "loss": float(loss.item()), "clocks": clocks.summary(), "e2e": e2e}
 
 
+def timed_loop(fn, steps: int, sampler_index: int | None, world: int) -> tuple[float, float, dict | None]:
+    """(ms per step, max over ranks; last loss; clock summary): CUDA events around exactly `steps`
+    calls of fn(i), bracketed by a barrier and a synchronize on both sides."""
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(sampler_index) if sampler_index is not None else None
+    if sampler is not None:
+        sampler.__enter__()
+    start.record()
+    loss = None
+    for i in range(steps):
+        loss = fn(i)
+    end.record()
+    torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.__exit__(None, None, None)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end) / steps, world)
+    return ms, float(loss.item()) if loss is not None else float("nan"), sampler.summary() if sampler else None
+
+
+def windowed_tp_main(args: argparse.Namespace, rank: int, world: int, local: int) -> None:
+    from mia_train_b200.benchmarks import windowed_tp as wtp
+
+    def timed(fn, steps, sampler):
+        return timed_loop(fn, steps, local if sampler is not None else None, world)
+
+    if args.impl == "reference":
+        res = wtp.reference_arm(args, rank, world, local, ClockSampler, timed, REPO)
+    else:
+        res = wtp.native_arm(args, rank, world, local, ClockSampler, timed, kernel_table)
+    if rank == 0:
+        if "unavailable" in res:
+            print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
+            return
+        gb = res["global_batch"]
+        value = gb * 1000.0 / res["ms"]
+        line = {
+            "metric": "samples/sec (windowed dinov3_vit3d ViT-L SimMIM, 256^3, patch 8, bf16), whole box, "
+                      "device-timed max over ranks",
+            "value": round(value, 3), "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uint8 blurred-noise + ellipsoid 256^3 volumes, z-scored on device; random-init weights)",
+            "config": {**wtp.describe(world), "global_batch": gb, "seq_len": 32769,
+                       "parallelism": res["parallelism"], "l2": "activations far larger than L2 (no flush)"},
+            "mfu": round(res["flops"] / (res["ms"] / 1000.0) / PEAK_BF16, 4),
+            "tflops_per_gpu": round(res["flops"] / (res["ms"] / 1000.0) / 1e12, 1),
+            "loss": round(res["loss"], 5), "clocks": res["clocks"],
+        }
+        if res.get("e2e"):
+            e = res["e2e"]
+            line["e2e"] = {"value": round(gb * 1000.0 / e["ms_per_step"], 3), "unit": "samples/s", **e}
+        if args.impl == "reference":
+            line["impl"] = "reference"
+        else:
+            line["kernel_errors"] = res["errors"]
+            line["native_library"] = res["lib"]
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     args = parse()
     rank, world, local = dist_setup()
+    if args.config == "windowed_tp":
+        windowed_tp_main(args, rank, world, local)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         res = reference_arm(args, rank, world, local)
     else:

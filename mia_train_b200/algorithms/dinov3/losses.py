@@ -13,6 +13,10 @@
   global masked-patch count is all-reduced.
 * `KoLeoLoss`: -mean log distance to the nearest neighbour of L2-normalised features, outside
   autocast.
+
+On CUDA the DINO and iBOT cross-entropies run on one native soft-target cross-entropy kernel pair
+(log-sum-exp and the teacher dot products in one pass over each student row; `ops/dino.py`) and
+KoLeo on a one-CTA kernel pair; the PyTorch formulas above remain the CPU path and the oracles.
 """
 
 from __future__ import annotations
@@ -100,6 +104,10 @@ class DINOLoss(nn.Module):
         return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations)
 
     def forward(self, student_logits: torch.Tensor, teacher_probs: torch.Tensor, ignore_diagonal: bool = False):
+        from ...ops._native import use_native
+
+        if use_native(student_logits):
+            return self._forward_native(student_logits, teacher_probs, ignore_diagonal)
         log_probs = F.log_softmax(student_logits.float() / self.student_temp, dim=-1)
         n_s, b, _ = log_probs.shape
         n_t = teacher_probs.shape[0]
@@ -109,6 +117,27 @@ class DINOLoss(nn.Module):
         diag = min(n_s, n_t)
         pairwise = torch.diagonal_scatter(pairwise, torch.zeros(diag, device=pairwise.device, dtype=pairwise.dtype))
         return pairwise.sum() / (b * n_s * n_t - b * diag)
+
+
+    def _forward_native(self, student_logits, teacher_probs, ignore_diagonal):
+        """Student row (s, b) pairs with teacher rows (t, b); same-view pairs get weight 0 when ignored."""
+        from ...ops.dino import soft_cross_entropy
+
+        n_s, b, k = student_logits.shape
+        n_t = teacher_probs.shape[0]
+        dev = student_logits.device
+        s_idx = torch.arange(n_s, device=dev).view(n_s, 1, 1)
+        b_idx = torch.arange(b, device=dev).view(1, b, 1)
+        t_idx = torch.arange(n_t, device=dev).view(1, 1, n_t)
+        pairs = (t_idx * b + b_idx).expand(n_s, b, n_t).reshape(n_s * b, n_t)
+        weights = torch.ones(n_s, b, n_t, device=dev)
+        diag = min(n_s, n_t)
+        norm = float(b * n_s * n_t)
+        if ignore_diagonal:
+            weights = weights * (s_idx != t_idx).float()
+            norm = float(b * n_s * n_t - b * diag)
+        return soft_cross_entropy(student_logits.reshape(n_s * b, k), teacher_probs.reshape(n_t * b, k), pairs,
+                                  weights.reshape(n_s * b, n_t), self.student_temp, norm)
 
 
 class IBOTPatchLoss(nn.Module):
@@ -126,11 +155,25 @@ class IBOTPatchLoss(nn.Module):
 
     def forward_masked(self, student_logits, teacher_probs, student_masks_flat, n_masked_patches=None,
                        masks_weight=None):
-        loss = torch.sum(teacher_probs * F.log_softmax(student_logits.float() / self.student_temp, dim=-1), dim=-1)
+        from ...ops._native import use_native
+
         if masks_weight is None:
             masks_weight = (
                 (1 / student_masks_flat.sum(-1).clamp(min=1.0)).unsqueeze(-1).expand_as(student_masks_flat)[student_masks_flat]
             )
+        if use_native(student_logits) and student_logits.dim() == 2:
+            from ...ops.dino import soft_cross_entropy
+
+            rows = student_logits.shape[0]
+            w = masks_weight.float().reshape(-1)[:rows]
+            if w.shape[0] < rows:  # rows past the masked patches (padding) carry no loss
+                w = torch.cat([w, w.new_zeros(rows - w.shape[0])])
+            if n_masked_patches is not None:
+                w = torch.where(torch.arange(rows, device=w.device) < n_masked_patches, w, torch.zeros_like(w))
+            pairs = torch.arange(rows, device=student_logits.device, dtype=torch.int32).view(rows, 1)
+            return soft_cross_entropy(student_logits, teacher_probs, pairs, w.view(rows, 1), self.student_temp,
+                                      float(student_masks_flat.shape[0]))
+        loss = torch.sum(teacher_probs * F.log_softmax(student_logits.float() / self.student_temp, dim=-1), dim=-1)
         if n_masked_patches is not None:
             loss = loss[:n_masked_patches]
         return -(loss * masks_weight).sum() / student_masks_flat.shape[0]
@@ -149,6 +192,13 @@ class KoLeoLoss(nn.Module):
         return torch.argmax(dots, dim=1)
 
     def forward(self, student_output: torch.Tensor) -> torch.Tensor:
+        from ...ops._native import use_native
+
+        if use_native(student_output):
+            from ...ops.dino import koleo
+
+            with torch.autocast("cuda", enabled=False):
+                return koleo(student_output, self.eps)
         with torch.autocast("cuda", enabled=False), torch.autocast("cpu", enabled=False):
             x = F.normalize(student_output.float(), eps=self.eps, p=2, dim=-1)
             nearest = self._pairwise_nearest(x)

@@ -65,6 +65,9 @@ void zero_all_gather(std::vector<int64_t> data_peers, std::vector<int64_t> shado
                      int64_t seg_lo, int64_t shard_len, int64_t bf16_begin, at::Tensor epoch, int64_t rank, int64_t blocks,
                      double timeout_ms, int64_t seq);
 void zero_advance_epoch(at::Tensor epoch);
+void zero_reduce_scatter_bf16(std::vector<int64_t> grad_peers, std::vector<int64_t> grad16_peers,
+                              std::vector<int64_t> flag_peers, int64_t seg_lo, int64_t shard_len, at::Tensor partial,
+                              at::Tensor epoch, int64_t rank, double timeout_ms, int64_t seq, int64_t threads);
 void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_full, c10::optional<at::Tensor> bias,
                 c10::optional<at::Tensor> aux, c10::optional<at::Tensor> aux_out, bool b_kmajor, int64_t act,
                 std::vector<int64_t> flag_peers, std::vector<int64_t> send_peers, int64_t send_parity_bytes,
@@ -74,6 +77,12 @@ void tp_gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, c10::optional<at::Te
                 c10::optional<at::Tensor> pre_out, bool b_kmajor, std::vector<int64_t> flag_peers,
                 std::vector<int64_t> recv_peers, int64_t recv_parity_bytes, int64_t rank, double timeout_ms);
 int64_t tp_flag_bytes();
+void soft_ce_fwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse, at::Tensor loss);
+void soft_ce_bwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse,
+                 at::Tensor grad_scale, at::Tensor dS);
+void koleo_fwd(at::Tensor x, double eps, at::Tensor xn, at::Tensor nn, at::Tensor dist, at::Tensor loss);
+void koleo_bwd(at::Tensor x, at::Tensor xn, at::Tensor nn, at::Tensor dist, double eps, at::Tensor grad,
+               at::Tensor dxn, at::Tensor dx);
 at::Tensor axial_angles_fwd(at::Tensor coords, std::vector<at::Tensor> freqs);
 void axial_angles_bwd(at::Tensor dangles, at::Tensor coords, std::vector<at::Tensor> freqs,
                       std::vector<at::Tensor> dfreqs);
@@ -115,9 +124,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("zero_norm_exchange", &mia::zero_norm_exchange, "cross-rank grad norm -> clip scale");
   m.def("zero_all_gather", &mia::zero_all_gather, "peer-memory parameter all-gather + local refresh");
   m.def("zero_advance_epoch", &mia::zero_advance_epoch);
+  m.def("zero_reduce_scatter_bf16", &mia::zero_reduce_scatter_bf16,
+        "peer-memory gradient reduce-scatter with bf16 on the wire (fp32 sum) + sum of squares");
   m.def("tp_ag_gemm", &mia::tp_ag_gemm, "fused all-gather (peer memory) -> tcgen05 GEMM, sequence-parallel input");
   m.def("tp_gemm_rs", &mia::tp_gemm_rs, "fused tcgen05 GEMM -> reduce-scatter (peer stores) + bias/LayerScale/residual");
   m.def("tp_flag_bytes", &mia::tp_flag_bytes, "bytes of one rank's flag area for the fused TP kernels");
+  m.def("soft_ce_fwd", &mia::soft_ce_fwd, "soft-target cross-entropy over prototypes (DINO / iBOT): lse + per-row loss");
+  m.def("soft_ce_bwd", &mia::soft_ce_bwd, "gradient of soft_ce_fwd with respect to the student logits");
+  m.def("koleo_fwd", &mia::koleo_fwd, "KoLeo: normalise, nearest neighbour, -mean log distance");
+  m.def("koleo_bwd", &mia::koleo_bwd, "gradient of koleo_fwd");
   m.def("set_tc_attention_mode", &mia::set_tc_attention_mode, "1: tcgen05 attention where it applies (head dim 32 / 64); 0: warp-level kernels");
   m.def("tc_attention_mode", &mia::tc_attention_mode);
   m.def("tc_attention_launches", &mia::tc_attention_launches);

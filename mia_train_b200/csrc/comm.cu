@@ -150,6 +150,75 @@ __global__ void zero_reduce_scatter_kernel(PeerPtrs grads, PeerPtrs flags, int64
   }
 }
 
+// The same reduce-scatter with bf16 on the wire. CTA b owns groups [g0, g1) of 8 elements of every
+// shard of the segment: it first rounds this rank's fp32 gradient of that part of every shard to
+// bf16 (this rank's IPC bf16 buffer), passes the per-block barrier (block b of every peer has
+// rounded the same part of every shard, in particular of this rank's), then sums its part of this
+// rank's shard from every rank's bf16 copy in fp32 into the local fp32 gradient and accumulates the
+// sum of squares. Half the NVLink bytes of the fp32 kernel; the sum itself stays fp32.
+__global__ void zero_reduce_scatter_bf16_kernel(PeerPtrs grads, PeerPtrs grads16, PeerPtrs flags, int64_t seg_lo,
+                                                int64_t shard_len, float* __restrict__ partial,
+                                                const int* __restrict__ epoch_ptr, int rank, int world, int seq,
+                                                uint64_t timeout_ns, int* err) {
+  const int epoch = *epoch_ptr * kSeqPerStep + seq + 1;
+  const int64_t groups = shard_len / 8;
+  const int64_t per = (groups + gridDim.x - 1) / gridDim.x;
+  const int64_t g0 = blockIdx.x * per, g1 = min(groups, g0 + per);
+  const float* my32 = reinterpret_cast<const float*>(pick(grads, rank));
+  __nv_bfloat16* my16 = reinterpret_cast<__nv_bfloat16*>(pick(grads16, rank));
+  for (int sh = 0; sh < world; ++sh) {
+    const int64_t base = seg_lo + (int64_t)sh * shard_len;
+    for (int64_t g = g0 + threadIdx.x; g < g1; g += blockDim.x) {
+      const float4 a = *reinterpret_cast<const float4*>(my32 + base + g * 8);
+      const float4 b = *reinterpret_cast<const float4*>(my32 + base + g * 8 + 4);
+      *reinterpret_cast<uint4*>(my16 + base + g * 8) =
+          make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+    }
+  }
+  __threadfence_system();
+  float s = 0.f;
+  if (block_barrier(flags, 0, rank, world, epoch, timeout_ns, err, kErrZeroReduceScatterWait)) {
+    const int64_t own = seg_lo + (int64_t)rank * shard_len;
+    float* out = reinterpret_cast<float*>(pick(grads, rank)) + own;
+    for (int64_t g = g0 + threadIdx.x; g < g1; g += blockDim.x) {
+      uint4 v[kMaxWorld];
+#pragma unroll
+      for (int q = 0; q < kMaxWorld; ++q) {
+        int src = rank + q;
+        if (src >= world) src -= world;  // rotated start spreads the reads over the sources
+        if (q < world) v[q] = __ldcg(reinterpret_cast<const uint4*>(
+                                  reinterpret_cast<const __nv_bfloat16*>(pick(grads16, src)) + own) + g);
+      }
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < kMaxWorld; ++q) {
+        if (q < world) {
+          const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            acc[2 * h] += bf16_lo(w[h]);
+            acc[2 * h + 1] += bf16_hi(w[h]);
+          }
+        }
+      }
+      *reinterpret_cast<float4*>(out + g * 8) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(out + g * 8 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += acc[j] * acc[j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+    partial[blockIdx.x] = tot;
+  }
+}
+
 // values: float[kMaxWorld] area of every rank (inside the flag allocation, after the flags).
 __global__ void zero_norm_exchange_kernel(PeerPtrs flags, const float* __restrict__ partial, int nparts,
                                           const int* __restrict__ epoch_ptr, int rank, int world, float max_norm,
@@ -354,6 +423,28 @@ void zero_reduce_scatter(std::vector<int64_t> grad_peers, std::vector<int64_t> f
                                                        shard_len, partial.data_ptr<float>(), epoch.data_ptr<int>(),
                                                        (int)rank, world, (int)seq, timeout_from_ms(timeout_ms),
                                                        error_word(partial.get_device()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void zero_reduce_scatter_bf16(std::vector<int64_t> grad_peers, std::vector<int64_t> grad16_peers,
+                              std::vector<int64_t> flag_peers, int64_t seg_lo, int64_t shard_len, at::Tensor partial,
+                              at::Tensor epoch, int64_t rank, double timeout_ms, int64_t seq, int64_t threads) {
+  TORCH_CHECK(threads >= 64 && threads <= 1024 && threads % 32 == 0,
+              "zero_reduce_scatter_bf16: 64..1024 threads, whole warps");
+  TORCH_CHECK(seq >= 0 && seq < kSeqPerStep, "zero_reduce_scatter_bf16: launch sequence number out of range");
+  const int world = (int)grad_peers.size();
+  TORCH_CHECK(seg_lo % 64 == 0 && shard_len % 64 == 0, "zero_reduce_scatter_bf16: 64-element aligned segments");
+  TORCH_CHECK(partial.scalar_type() == at::kFloat && partial.is_cuda() && partial.numel() >= 1 &&
+                  partial.numel() <= kMaxBlocks,
+              "zero_reduce_scatter_bf16: partial sums buffer of 1..", kMaxBlocks, " floats expected");
+  TORCH_CHECK(epoch.scalar_type() == at::kInt && epoch.is_cuda(), "zero_reduce_scatter_bf16: int32 device epoch");
+  c10::cuda::CUDAGuard guard(partial.device());
+  const int grid = (int)partial.numel();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  zero_reduce_scatter_bf16_kernel<<<grid, (int)threads, 0, stream>>>(
+      to_peers(grad_peers, world), to_peers(grad16_peers, world), to_peers(flag_peers, world), seg_lo, shard_len,
+      partial.data_ptr<float>(), epoch.data_ptr<int>(), (int)rank, world, (int)seq, timeout_from_ms(timeout_ms),
+      error_word(partial.get_device()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

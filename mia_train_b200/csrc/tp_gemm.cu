@@ -26,10 +26,12 @@
 // while the remote rows are still in flight. The gathered A is an output: the backward pass uses
 // it for the weight gradient.
 //
-// GEMM -> reduce-scatter. Tiles are visited starting with the rows owned by the next rank. The
+// GEMM -> reduce-scatter. CTA b owns row blocks b, b + G, ... and computes all N tiles of a block
+// in a row, visiting the blocks owned by the next rank first and this rank's own last. The
 // epilogue rounds each accumulator row to bf16 and stores it straight into the owner's receive
-// slot (peer stores over NVLink, or local stores for this rank's own rows); when all N tiles of a
-// row block are stored (a per-block counter), the last CTA publishes the block to its owner(s).
+// slot (peer stores over NVLink, or local stores for this rank's own rows), releases the
+// accumulator to the MMA warp, and once the block's last N tile is stored publishes the block to
+// its owner(s) with one system fence per warp.
 // After its last tile every CTA reduces some of this rank's row blocks: it waits for the block's
 // flags from every rank, sums the W slots in fp32 and applies bias, LayerScale and the residual add
 // before the single bf16 store.
@@ -75,7 +77,7 @@ constexpr int kCopyInFlight = 12;
 // Flag area of one rank (int32):
 //   ag_ready[src][block]  written by src: its rows of gathered block `block` are in its send buffer
 //   rs_ready[src][block]  written by src: its partial rows of block `block` are in our receive slot
-//   block_count[block]    local: N tiles of a block stored (reduce-scatter)
+//   (spare)               kMaxMBlocks ints, unused
 //   ctl[]                 local: epochs and exit counters
 constexpr int kAgReady = 0;
 constexpr int kRsReady = kAgReady + kMaxWorld * kMaxMBlocks;
@@ -199,8 +201,8 @@ struct AgSmem {
 
 template <int BN, bool B_MN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kAgThreads, 1)
-    tp_ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const AgParams P) {
+    tp_ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmL,
+                      const __grid_constant__ CUtensorMap tmB, const AgParams P) {
   using L = AgSmem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -213,9 +215,10 @@ __global__ void __launch_bounds__(kAgThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* progress = reinterpret_cast<int*>(tmem_slot + 2);  // K slices ready, in sequence order
+  int* progress = reinterpret_cast<int*>(tmem_slot + 2);  // K slices of non-local blocks ready, in order
   int* nseq_slot = reinterpret_cast<int*>(tmem_slot + 3);
   volatile int* copy_stop = reinterpret_cast<volatile int*>(tmem_slot + 4);
+  int* nlocal_slot = reinterpret_cast<int*>(tmem_slot + 5);
   int* seq = reinterpret_cast<int*>(smem + STAGES * L::kStageBytes + 512);  // owned blocks, compute order
 
   const GemmParams& p = P.g;
@@ -239,16 +242,21 @@ __global__ void __launch_bounds__(kAgThreads, 1)
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     *progress = 0;
-    // Compute order: blocks whose rows are all local first, then the rest.
-    int n = 0;
+    // Compute order: blocks whose rows are all local first (read straight from A_r), then the rest.
+    int n = 0, nl = 0;
     for (int pass = 0; pass < 2; ++pass)
       for (int mb = blockIdx.x; mb < s.num_blocks; mb += gridDim.x) {
         const bool local = block_src_lo(s, mb) == s.rank && block_src_hi(s, mb) == s.rank;
-        if ((pass == 0) == local && n < kMaxOwned) seq[n++] = mb;
+        if ((pass == 0) == local && n < kMaxOwned) {
+          seq[n++] = mb;
+          nl += local ? 1 : 0;
+        }
       }
     *nseq_slot = n;
+    *nlocal_slot = nl;
     fence_barrier_init();
     prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmL);
     prefetch_tensormap(&tmB);
   }
   if (warp == 1) {
@@ -260,6 +268,7 @@ __global__ void __launch_bounds__(kAgThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nseq = *nseq_slot;
+  const int nlocal = *nlocal_slot;
   const int num_n = (p.N + BN - 1) / BN;
   constexpr int kCopyWarp0 = 2 + kEpi;
 
@@ -268,21 +277,20 @@ __global__ void __launch_bounds__(kAgThreads, 1)
     const int ct = threadIdx.x - 32 * kCopyWarp0;
     __nv_bfloat16* my_send = reinterpret_cast<__nv_bfloat16*>(pick(P.send, s.rank)) + par_off;
     const int row_lo = s.rank * s.S, row_hi = row_lo + s.S;
-    // Phase 1: this rank's rows of every owned block -> send buffer and gathered output.
-    int nlocal = 0;
+    // Phase 1: this rank's rows of every owned block -> send buffer (for the peers) and gathered
+    // output. The tensor cores read local-only blocks straight from A_r, so nothing waits on this.
     for (int i = 0; i < nseq; ++i) {
       const int mb = seq[i];
       const int r0 = max(mb * 128, row_lo), r1 = min(min(mb * 128 + 128, s.M), row_hi);
       if (r0 < r1)
-        copy_rows<false>(P.a_full + (int64_t)r0 * p.K, p.K, my_send + (int64_t)(r0 - row_lo) * p.K, p.K,
+        copy_rows<false>(P.a_full + (int64_t)r0 * p.K, p.K,
+                         s.world > 1 ? my_send + (int64_t)(r0 - row_lo) * p.K : nullptr, p.K,
                          P.a_local + (int64_t)(r0 - row_lo) * p.K, p.K, r1 - r0, 0, p.K, ct);
-      if (block_src_lo(s, mb) == s.rank && block_src_hi(s, mb) == s.rank) ++nlocal;
     }
     __threadfence_system();
     fence_proxy_async_global();
     named_barrier(1, kCopyThreads);
     if (ct == 0) {
-      st_release_cta_shared(progress, nlocal * num_k);
       for (int i = 0; i < nseq; ++i) {
         const int mb = seq[i];
         if (block_src_lo(s, mb) > s.rank || block_src_hi(s, mb) < s.rank) continue;
@@ -292,7 +300,7 @@ __global__ void __launch_bounds__(kAgThreads, 1)
       }
     }
     // Phase 2: remote rows of the remaining blocks, in compute order.
-    int done = nlocal * num_k;
+    int done = 0;
     bool ok = true;
     const int* my_flags = reinterpret_cast<const int*>(pick(P.flags, s.rank));
     for (int i = nlocal; i < nseq && ok; ++i) {
@@ -339,11 +347,12 @@ __global__ void __launch_bounds__(kAgThreads, 1)
       constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
       for (int i = 0; i < nseq && ok; ++i) {
         const int m0 = seq[i] * 128;
+        const bool local = i < nlocal;
         for (int nt = 0; nt < num_n && ok; ++nt) {
           const int n0 = nt * BN;
           for (int kb = 0; kb < num_k; ++kb) {
-            if (nt == 0) {
-              const int need = i * num_k + kb + 1;
+            if (nt == 0 && !local) {
+              const int need = (i - nlocal) * num_k + kb + 1;
               if (ld_acquire_cta_shared(progress) < need) {
                 const uint64_t t0 = globaltimer_ns();
                 while (ld_acquire_cta_shared(progress) < need) {
@@ -370,7 +379,8 @@ __global__ void __launch_bounds__(kAgThreads, 1)
             mbar_arrive_expect_tx(&full_bar[stage], kTx);
             uint8_t* a_dst = smA + stage * kATileBytes;
             uint8_t* b_dst = smB + stage * L::kBTileBytes;
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
+            if (local) tma_load_2d(a_dst, &tmL, &full_bar[stage], k0, m0 - s.rank * s.S);
+            else tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
             if (!B_MN) {
               tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
             } else {
@@ -509,23 +519,18 @@ struct RsParams {
   const __nv_bfloat16* residual;
   __nv_bfloat16* pre_out;
   uint64_t timeout_ns;
-  int num_n_tiles, num_tiles, first_block;
 };
 
 template <int BN, int STAGES>
 struct RsSmem {
   static constexpr int kBTileBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
-  static constexpr int kBytes = STAGES * kStageBytes + 1024 + 512;
+  static constexpr int kBytes = STAGES * kStageBytes + 1024 + 512 + kMaxOwned * 4;
 };
 
-__device__ __forceinline__ void rs_tile(const RsParams& P, int tile, int& mb, int& nt) {
-  const int t = tile % P.s.num_blocks;
-  nt = tile / P.s.num_blocks;
-  mb = t + P.first_block;
-  if (mb >= P.s.num_blocks) mb -= P.s.num_blocks;
-}
-
+// CTA b owns the 128-row blocks b, b + G, ... and computes every N tile of a block before the next
+// block, so it alone decides when a block's partial rows are complete and publishes them. Blocks
+// are visited by owner distance: rows of the next rank first, this rank's own rows last.
 template <int BN, bool A_MN, bool B_MN, int STAGES>
 __global__ void __launch_bounds__(kRsThreads, 1)
     tp_gemm_rs_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -542,12 +547,15 @@ __global__ void __launch_bounds__(kRsThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* tile_arrivals = reinterpret_cast<int*>(tmem_slot + 2);  // [2], per accumulator
+  int* block_arrivals = reinterpret_cast<int*>(tmem_slot + 2);  // [4], by block sequence index mod 4
+  int* nseq_slot = reinterpret_cast<int*>(tmem_slot + 6);
+  int* seq = reinterpret_cast<int*>(smem + STAGES * L::kStageBytes + 512);
 
   const TpShape& s = P.s;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   constexpr uint32_t kTmemCols = 2 * BN;
   const int num_k = (s.K + kBK - 1) / kBK;
+  const int num_n = (s.N + BN - 1) / BN;
   int* my_flags = reinterpret_cast<int*>(pick(P.flags, s.rank));
   const int epoch = *reinterpret_cast<const volatile int*>(my_flags + kCtl + kCtlRsEpoch) + 1;
   const int64_t par_off = (epoch & 1) ? P.recv_parity_elems : 0;
@@ -564,7 +572,14 @@ __global__ void __launch_bounds__(kRsThreads, 1)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
-    tile_arrivals[0] = tile_arrivals[1] = 0;
+    for (int j = 0; j < 4; ++j) block_arrivals[j] = 0;
+    int n = 0;
+    for (int d = 1; d <= s.world; ++d) {
+      const int owner = (s.rank + d) % s.world;
+      for (int mb = blockIdx.x; mb < s.num_blocks; mb += gridDim.x)
+        if (block_src_lo(s, mb) == owner && n < kMaxOwned) seq[n++] = mb;
+    }
+    *nseq_slot = n;
     fence_barrier_init();
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
@@ -577,6 +592,7 @@ __global__ void __launch_bounds__(kRsThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int nseq = *nseq_slot;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -585,35 +601,36 @@ __global__ void __launch_bounds__(kRsThreads, 1)
       int issued = 0;
       bool ok = true;
       constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
-      for (int tile = blockIdx.x; tile < P.num_tiles && ok; tile += gridDim.x) {
-        int mb, nt;
-        rs_tile(P, tile, mb, nt);
-        const int m0 = mb * 128, n0 = nt * BN;
-        for (int kb = 0; kb < num_k; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, P.err, kErrGemmProducerWait)) {
-            ok = false;
-            break;
-          }
-          const int k0 = kb * kBK;
-          mbar_arrive_expect_tx(&full_bar[stage], kTx);
-          uint8_t* a_dst = smA + stage * kATileBytes;
-          uint8_t* b_dst = smB + stage * L::kBTileBytes;
-          if (!A_MN) {
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
-          } else {
+      for (int i = 0; i < nseq && ok; ++i) {
+        const int m0 = seq[i] * 128;
+        for (int nt = 0; nt < num_n && ok; ++nt) {
+          const int n0 = nt * BN;
+          for (int kb = 0; kb < num_k; ++kb) {
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, P.err, kErrGemmProducerWait)) {
+              ok = false;
+              break;
+            }
+            const int k0 = kb * kBK;
+            mbar_arrive_expect_tx(&full_bar[stage], kTx);
+            uint8_t* a_dst = smA + stage * kATileBytes;
+            uint8_t* b_dst = smB + stage * L::kBTileBytes;
+            if (!A_MN) {
+              tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 2; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
-          }
-          if (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
-          } else {
+              for (int j = 0; j < 2; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+            }
+            if (!B_MN) {
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
-          }
-          ++issued;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+            }
+            ++issued;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
         }
       }
@@ -636,40 +653,42 @@ __global__ void __launch_bounds__(kRsThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true, any = false;
-      for (int tile = blockIdx.x; tile < P.num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, P.err, kErrGemmMmaWait)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_k; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, P.err, kErrGemmMmaWait)) {
+      for (int i = 0; i < nseq && ok; ++i) {
+        for (int nt = 0; nt < num_n && ok; ++nt) {
+          if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, P.err, kErrGemmMmaWait)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smA + stage * kATileBytes);
-          const uint32_t b_base = smem_u32(smB + stage * L::kBTileBytes);
+          const uint32_t d_tmem = tmem_base + acc * BN;
+          for (int kb = 0; kb < num_k; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag, P.err, kErrGemmMmaWait)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(smA + stage * kATileBytes);
+            const uint32_t b_base = smem_u32(smB + stage * L::kBTileBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t a_desc = A_MN ? make_sdesc_sw128(a_base + k * 2048, 8192, 1024)
-                                         : make_sdesc_sw128(a_base + k * 32, 16, 1024);
-            const uint64_t b_desc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
-                                         : make_sdesc_sw128(b_base + k * 32, 16, 1024);
-            tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            any = true;
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t a_desc = A_MN ? make_sdesc_sw128(a_base + k * 2048, 8192, 1024)
+                                           : make_sdesc_sw128(a_base + k * 32, 16, 1024);
+              const uint64_t b_desc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
+                                           : make_sdesc_sw128(b_base + k * 32, 16, 1024);
+              tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              any = true;
+            }
+            tc_commit(&empty_bar[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
-          tc_commit(&empty_bar[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+          if (!ok) break;
+          tc_commit(&tfull_bar[acc]);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1;
         }
-        if (!ok) break;
-        tc_commit(&tfull_bar[acc]);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1;
       }
       if (!ok && any) {
         tc_commit(drain_bar);
@@ -685,68 +704,66 @@ __global__ void __launch_bounds__(kRsThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < P.num_tiles; tile += gridDim.x) {
-      int mb, nt;
-      rs_tile(P, tile, mb, nt);
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, P.err, kErrGemmEpilogueWait)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+    for (int i = 0; i < nseq && ok; ++i) {
+      const int mb = seq[i];
       const int m = mb * 128 + lane_group * 32 + lane;
-      const int n0 = nt * BN + col_part * kPartCols;
-      const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_part * kPartCols;
       __nv_bfloat16* dst_row = nullptr;
       if (m < s.M) {
         const int owner = m / s.S;
         dst_row = reinterpret_cast<__nv_bfloat16*>(pick(P.recv, owner)) + par_off + (int64_t)s.rank * slot_elems +
                   (int64_t)(m - owner * s.S) * s.N;
       }
+      for (int nt = 0; nt < num_n; ++nt) {
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, P.err, kErrGemmEpilogueWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int n0 = nt * BN + col_part * kPartCols;
+        const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_part * kPartCols;
 #pragma unroll 1
-      for (int c = 0; c < kPartCols / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait_regs(r);
-        const int n = n0 + c * 32;
-        if (dst_row != nullptr && n < s.N) {
-          if (n + 32 <= s.N) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst_row + n);
+        for (int c = 0; c < kPartCols / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait_regs(r);
+          const int n = n0 + c * 32;
+          if (dst_row != nullptr && n < s.N) {
+            if (n + 32 <= s.N) {
+              uint4* d4 = reinterpret_cast<uint4*>(dst_row + n);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              d4[q] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1])),
-                                 pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
-                                 pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
-                                 pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
-          } else {
+              for (int q = 0; q < 4; ++q)
+                d4[q] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1])),
+                                   pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
+                                   pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
+                                   pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n + j < s.N) dst_row[n + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+              for (int j = 0; j < 32; ++j)
+                if (n + j < s.N) dst_row[n + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+            }
           }
         }
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);  // the MMA may refill this accumulator while we publish
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
       }
-      // Publish the block once all its N tiles are stored (by any CTA of this GPU). The last epilogue
-      // warp of this CTA to finish the tile counts it; a warp arrives before it releases the
-      // accumulator, so the counter of one accumulator never mixes two tiles.
+      if (!ok) break;
+      // The block's partial rows are stored: make them visible system-wide, then the last warp of this
+      // CTA publishes the block to its owner(s). A warp is at most two blocks ahead of the slowest
+      // one (it needs every warp's release of the accumulator it reuses), so four counters suffice.
       __threadfence_system();
       __syncwarp();
-      if (lane == 0 && atomicAdd(&tile_arrivals[acc], 1) == kEpi - 1) {
-        tile_arrivals[acc] = 0;
+      if (lane == 0 && atomicAdd(&block_arrivals[i & 3], 1) == kEpi - 1) {
+        block_arrivals[i & 3] = 0;
         __threadfence_system();
-        int* count = my_flags + kBlockCount + mb;
-        if (atomicAdd(count, 1) == P.num_n_tiles - 1) {
-          *count = 0;
-          const int lo = block_src_lo(s, mb), hi = block_src_hi(s, mb);
-          for (int q = lo; q <= hi; ++q)
-            st_release_sys(reinterpret_cast<int*>(pick(P.flags, q)) + kRsReady + s.rank * kMaxMBlocks + mb, epoch);
-        }
+        const int lo = block_src_lo(s, mb), hi = block_src_hi(s, mb);
+        for (int q = lo; q <= hi; ++q)
+          st_release_sys(reinterpret_cast<int*>(pick(P.flags, q)) + kRsReady + s.rank * kMaxMBlocks + mb, epoch);
       }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1;
     }
     // ---------------- reduce this rank's row blocks (sum of W slots + epilogue)
-    if (ok && !*abort_flag) {
+    if (ok) {
       const int row_lo = s.rank * s.S, row_hi = row_lo + s.S;
       const int mb_lo = row_lo / 128, mb_hi = (row_hi - 1) / 128;
       const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(pick(P.recv, s.rank)) + par_off;
@@ -831,9 +848,8 @@ Peers to_peers(const std::vector<int64_t>& v, int world, const char* what) {
   return p;
 }
 
-template <typename Kern, typename Params>
-void coop_launch(Kern kern, int grid, int threads, int smem_bytes, cudaStream_t stream, const CUtensorMap& ta,
-                 const CUtensorMap& tb, const Params& prm) {
+template <typename Kern, typename... Args>
+void coop_launch(Kern kern, int grid, int threads, int smem_bytes, cudaStream_t stream, const Args&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(threads, 1, 1);
@@ -844,7 +860,7 @@ void coop_launch(Kern kern, int grid, int threads, int smem_bytes, cudaStream_t 
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, prm));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, args...));
 }
 
 int64_t flag_bytes() { return (int64_t)kFlagInts * 4; }
@@ -852,8 +868,8 @@ int64_t flag_bytes() { return (int64_t)kFlagInts * 4; }
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <int BN, bool B_MN, int EPI>
-static void launch_ag(const CUtensorMap& ta, const CUtensorMap& tb, const AgParams& prm, int grid, cudaStream_t st,
-                      int device) {
+static void launch_ag(const CUtensorMap& ta, const CUtensorMap& tl, const CUtensorMap& tb, const AgParams& prm,
+                      int grid, cudaStream_t st, int device) {
   constexpr int ST = BN == 256 ? 4 : 6;
   using L = AgSmem<BN, ST>;
   auto kern = tp_ag_gemm_kernel<BN, B_MN, ST, EPI>;
@@ -862,15 +878,15 @@ static void launch_ag(const CUtensorMap& ta, const CUtensorMap& tb, const AgPara
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     configured[device] = true;
   }
-  coop_launch(kern, grid, kAgThreads, L::kBytes, st, ta, tb, prm);
+  coop_launch(kern, grid, kAgThreads, L::kBytes, st, ta, tl, tb, prm);
 }
 
 template <int BN, bool B_MN>
-static void dispatch_ag_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const AgParams& prm, int grid,
-                            cudaStream_t st, int device) {
-  if (epi == kEpiGelu) launch_ag<BN, B_MN, kEpiGelu>(ta, tb, prm, grid, st, device);
-  else if (epi == kEpiDGelu) launch_ag<BN, B_MN, kEpiDGelu>(ta, tb, prm, grid, st, device);
-  else launch_ag<BN, B_MN, kEpiPlain>(ta, tb, prm, grid, st, device);
+static void dispatch_ag_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tl, const CUtensorMap& tb,
+                            const AgParams& prm, int grid, cudaStream_t st, int device) {
+  if (epi == kEpiGelu) launch_ag<BN, B_MN, kEpiGelu>(ta, tl, tb, prm, grid, st, device);
+  else if (epi == kEpiDGelu) launch_ag<BN, B_MN, kEpiDGelu>(ta, tl, tb, prm, grid, st, device);
+  else launch_ag<BN, B_MN, kEpiPlain>(ta, tl, tb, prm, grid, st, device);
 }
 
 }  // namespace tp
@@ -947,13 +963,14 @@ void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_f
   const int bn = N <= 128 ? 128 : 256;
   const int epi = act == kActGelu ? kEpiGelu : (act == kActDGelu ? kEpiDGelu : kEpiPlain);
   CUtensorMap ta = make_bf16_map(a_full.data_ptr(), K, M, K, 64, kBM);
+  CUtensorMap tl = make_bf16_map(a_local.data_ptr(), K, S, K, 64, kBM);
   CUtensorMap tb = b_kmajor ? make_bf16_map(b.data_ptr(), K, N, K, 64, bn) : make_bf16_map(b.data_ptr(), N, K, N, 64, 64);
   if (bn == 256) {
-    if (b_kmajor) dispatch_ag_epi<256, false>(epi, ta, tb, prm, grid, stream, device);
-    else dispatch_ag_epi<256, true>(epi, ta, tb, prm, grid, stream, device);
+    if (b_kmajor) dispatch_ag_epi<256, false>(epi, ta, tl, tb, prm, grid, stream, device);
+    else dispatch_ag_epi<256, true>(epi, ta, tl, tb, prm, grid, stream, device);
   } else {
-    if (b_kmajor) dispatch_ag_epi<128, false>(epi, ta, tb, prm, grid, stream, device);
-    else dispatch_ag_epi<128, true>(epi, ta, tb, prm, grid, stream, device);
+    if (b_kmajor) dispatch_ag_epi<128, false>(epi, ta, tl, tb, prm, grid, stream, device);
+    else dispatch_ag_epi<128, true>(epi, ta, tl, tb, prm, grid, stream, device);
   }
 }
 
@@ -1029,11 +1046,8 @@ void tp_gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, c10::optional<at::Te
   prm.pre_out = mat(pre_out);
   prm.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms * 1e6 : 5e9);
   const int bn = N <= 128 ? 128 : 256;
-  prm.num_n_tiles = (int)((N + bn - 1) / bn);
-  prm.num_tiles = prm.s.num_blocks * prm.num_n_tiles;
-  // start with the first row block owned by the next rank
-  prm.first_block = (int)((((rank + 1) % world) * S) / 128);
-  const int grid = std::min(prm.num_tiles, sm_count(device));
+  const int grid = (int)std::min<int64_t>(prm.s.num_blocks, sm_count(device));
+  TORCH_CHECK(prm.s.num_blocks <= (int64_t)grid * kMaxOwned, "tp_gemm_rs: too many row blocks per CTA");
   CUtensorMap ta = make_bf16_map(a.data_ptr(), K, M, K, 64, kBM);
   CUtensorMap tb = b_kmajor ? make_bf16_map(b.data_ptr(), K, N, K, 64, bn) : make_bf16_map(b.data_ptr(), N, K, N, 64, 64);
   if (bn == 256) {

@@ -4,7 +4,9 @@ Every rank keeps the whole model (a ViT-L is 1.3 GB of fp32 parameters against 1
 forward and backward need no parameter collectives at all. After backward, rank r owns the r-th
 contiguous slice of the flat parameter buffer:
 
-1. reduce-scatter: rank r sums slice r of every rank's flat gradient,
+1. reduce-scatter: rank r sums slice r of every rank's flat gradient (with the p2p implementation
+   the gradients travel in bf16 by default -- each rank rounds its fp32 gradient into a peer-mapped
+   bf16 buffer and the owner sums the copies in fp32; `wire_dtype="fp32"` reads the fp32 values),
 2. the global gradient norm is exchanged and turned into the clip coefficient (times 1/world),
 3. AdamW updates slice r only (exp_avg / exp_avg_sq exist only for the owned slice, so optimizer
    memory is 1/world of the unsharded optimizer),
@@ -61,6 +63,7 @@ class ShardedStep:
         ipc: IpcBuffers | None = None,
         timeout_ms: float = 10_000.0,
         overlap_blocks: int = 64,
+        wire_dtype: str = "bf16",
     ) -> None:
         if impl not in IMPLS:
             raise ValueError(f"sharded step impl must be one of {IMPLS}, got {impl!r}")
@@ -128,6 +131,12 @@ class ShardedStep:
             self.partial = torch.zeros(sum(grids), dtype=torch.float32, device=dev)
             self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
             _, self.flag_peers = ipc.allocate(int(native().comm_flag_bytes()) // 4, torch.int32)
+            if wire_dtype not in ("bf16", "fp32"):
+                raise ValueError(f"wire_dtype must be 'bf16' or 'fp32', got {wire_dtype!r}")
+            self.wire_dtype = wire_dtype
+            # bf16 wire format: each rank rounds its fp32 gradients into this peer-mapped buffer and
+            # the owners sum the bf16 copies in fp32 (half the NVLink bytes of reading fp32)
+            self.grad16_peers = ipc.allocate(flat.total, torch.bfloat16)[1] if wire_dtype == "bf16" else None
 
     # -- reduce-scatter -------------------------------------------------------------------------
     def begin(self) -> None:
@@ -147,8 +156,12 @@ class ShardedStep:
             # Segments reduced during backward use small CTAs (128 threads, no shared memory) so they
             # fit on an SM beside a GEMM CTA instead of displacing it.
             threads = 512 if i == 0 else 128
-            native().zero_reduce_scatter(self.flat.peers["grad"], self.flag_peers, lo + self.rank * sl, sl, part,
-                                         self.epoch, self.rank, self.timeout_ms, self._seq, threads)
+            if self.grad16_peers is not None:
+                native().zero_reduce_scatter_bf16(self.flat.peers["grad"], self.grad16_peers, self.flag_peers, lo, sl,
+                                                  part, self.epoch, self.rank, self.timeout_ms, self._seq, threads)
+            else:
+                native().zero_reduce_scatter(self.flat.peers["grad"], self.flag_peers, lo + self.rank * sl, sl, part,
+                                             self.epoch, self.rank, self.timeout_ms, self._seq, threads)
         else:
             dist.reduce_scatter_tensor(self._own_grads[i], self.flat.grad[lo:lo + self.world * sl], group=self.group)
         self._seq += 1
