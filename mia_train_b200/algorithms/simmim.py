@@ -3,7 +3,9 @@
 The encoder (a DINOv3 model with `forward_features(x, masks)`) replaces hidden patches by its
 `mask_token` and runs the full grid; a linear `head` predicts each patch's voxels; the loss is the
 L1 error on masked patches (optionally against per-patch normalised targets), with the visible
-patches' L1 logged. The mask is drawn in units of `mask_granularity` patches per axis.
+patches' L1 logged. The mask is drawn in units of `mask_granularity` patches per axis. On CUDA the
+loss is one native kernel (`ops.mae.masked_l1`) that reads each target patch straight from the
+volume and writes the prediction's gradient in the same pass (no patchified target copy).
 """
 
 from __future__ import annotations
@@ -105,6 +107,11 @@ class SimMIM(BaseAlgorithm):
                            device=volumes.device)
         out = self.encoder.forward_features(volumes, mask)
         prediction = apply_linear(self.head, out["x_norm_patchtokens"])
+        if prediction.is_cuda and len(self.patch_size) == 3:
+            from ..ops.mae import masked_l1
+
+            loss, visible = masked_l1(prediction, volumes, mask, self.patch_size, self.norm_pix_loss)
+            return {"loss": loss, "masked_fraction": mask.float().mean(), "visible_l1": visible}
         target = patchify(volumes, self.patch_size)
         if self.norm_pix_loss:
             mean = target.mean(dim=-1, keepdim=True)

@@ -73,6 +73,20 @@ __device__ __forceinline__ float fast_exp2f(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, used for a quarter of the softmax exponentials so the multi-function unit
+// (16 results per clock per SM, the limiter of these kernels) and the FMA pipe share the work.
+// Range reduction x = n + f with n = floor(x), f in [0, 1); 2^f by a cubic fitted here to minimise
+// the relative error on [0, 1) (iteratively reweighted least squares over 20001 points): maximum
+// relative error 7.6e-5, far below the bf16 rounding (3.9e-3) that P is stored with; 2^n is added to
+// the exponent field. Arguments below -125 return 0 (the softmax exponents here are <= 0).
+__device__ __forceinline__ float poly_exp2f(float x) {
+  const float fl = floorf(x);
+  const float f = x - fl;
+  const float p = fmaf(fmaf(fmaf(0.07802251590f, f, 0.2260656115f), f, 0.6958365058f), f, 0.9999246655f);
+  const float y = __int_as_float(__float_as_int(p) + ((int)fl << 23));
+  return x < -125.f ? 0.f : y;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kTcThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -279,8 +293,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const int key = kbase + c * 32 + 2 * e;
             const float p0 =
                 (kFull || key < Nk) ? fast_exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, -m_new)) : 0.f;
-            const float p1 =
-                (kFull || key + 1 < Nk) ? fast_exp2f(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, -m_new)) : 0.f;
+            const float x1 = fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, -m_new);
+            const float p1 = (kFull || key + 1 < Nk) ? ((e & 1) ? fast_exp2f(x1) : poly_exp2f(x1)) : 0.f;
             rs += p0 + p1;
             pk[e] = pack_bf16x2(p0, p1);
           }
@@ -615,7 +629,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int e2 = 0; e2 < 2; ++e2) {
             const int e = e4 * 2 + e2;
             const float p0 = fast_exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, -ls[2 * e2]));
-            const float p1 = fast_exp2f(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, -ls[2 * e2 + 1]));
+            const float x1 = fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, -ls[2 * e2 + 1]);
+            const float p1 = e2 ? fast_exp2f(x1) : poly_exp2f(x1);
             const float d0 = p0 * (__uint_as_float(dpv[2 * e]) - ds[2 * e2]);
             const float d1 = p1 * (__uint_as_float(dpv[2 * e + 1]) - ds[2 * e2 + 1]);
             pk[e] = pack_bf16x2(p0, p1);

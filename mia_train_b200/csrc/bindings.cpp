@@ -80,6 +80,8 @@ int64_t tp_flag_bytes();
 void soft_ce_fwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse, at::Tensor loss);
 void soft_ce_bwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse,
                  at::Tensor grad_scale, at::Tensor dS);
+void masked_l1(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, torch::Tensor sums, torch::Tensor grad,
+               int64_t pd, int64_t ph, int64_t pw, bool norm_pix);
 void koleo_fwd(at::Tensor x, double eps, at::Tensor xn, at::Tensor nn, at::Tensor dist, at::Tensor loss);
 void koleo_bwd(at::Tensor x, at::Tensor xn, at::Tensor nn, at::Tensor dist, double eps, at::Tensor grad,
                at::Tensor dxn, at::Tensor dx);
@@ -131,6 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_flag_bytes", &mia::tp_flag_bytes, "bytes of one rank's flag area for the fused TP kernels");
   m.def("soft_ce_fwd", &mia::soft_ce_fwd, "soft-target cross-entropy over prototypes (DINO / iBOT): lse + per-row loss");
   m.def("soft_ce_bwd", &mia::soft_ce_bwd, "gradient of soft_ce_fwd with respect to the student logits");
+  m.def("masked_l1", &mia::masked_l1, "SimMIM masked L1 (targets read from the volume) + gradient");
   m.def("koleo_fwd", &mia::koleo_fwd, "KoLeo: normalise, nearest neighbour, -mean log distance");
   m.def("koleo_bwd", &mia::koleo_bwd, "gradient of koleo_fwd");
   m.def("set_tc_attention_mode", &mia::set_tc_attention_mode, "1: tcgen05 attention where it applies (head dim 32 / 64); 0: warp-level kernels");

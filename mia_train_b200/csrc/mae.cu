@@ -288,6 +288,125 @@ __global__ void norm_pix_mse_kernel(const TP* __restrict__ pred, const TV* __res
   if (threadIdx.x == 0) atomicAdd(loss, tot * mk / (float)P / cnt);
 }
 
+// SimMIM's loss (reference `src/algorithms/simmim.py:197-207`): per patch the mean absolute error
+// between the prediction and the target patch (read straight from the volume, optionally normalised
+// by its own mean and unbiased variance + 1e-6), averaged over the masked patches; the visible
+// patches' mean is accumulated as a metric. One CTA per patch; the gradient sign(p - t) / P / count
+// is written for masked patches (zero for visible ones) in the same pass. sums[0] += masked error,
+// sums[1] += visible error (both already divided by their patch counts).
+template <typename TP, typename TV>
+__global__ void masked_l1_kernel(const TP* __restrict__ pred, const TV* __restrict__ vol, const float* __restrict__ mask,
+                                 const float* __restrict__ counts, float* __restrict__ sums, TP* __restrict__ grad, int C,
+                                 int D, int H, int W, int pd, int ph, int pw, int N, int norm_pix) {
+  const int row = blockIdx.x;
+  const int b = row / N, n = row % N;
+  const int vp = pd * ph * pw;
+  const int P = C * vp;
+  const int runs = P / 8;
+  const TP* pr = pred + (size_t)row * P;
+  TP* gr = grad + (size_t)row * P;
+  const float mk = mask[row];
+  const int gh = H / ph, gw = W / pw;
+  const int zd = n / (gh * gw), zh = (n / gw) % gh, zw = n % gw;
+  auto run_ptr = [&](int u) -> const TV* {
+    const int e = u * 8;
+    const int c = e / vp;
+    int r = e % vp;
+    const int a = r / (ph * pw);
+    r %= ph * pw;
+    const int j = r / pw, l = r % pw;
+    return vol + ((((size_t)b * C + c) * D + (zd * pd + a)) * H + (zh * ph + j)) * W + (zw * pw + l);
+  };
+  __shared__ float red[32];
+  __shared__ float shift_s;
+  auto block_sum = [&](float v) -> float {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < (int)blockDim.x / 32; ++w) tot += red[w];
+    return tot;
+  };
+  float mean = 0.f, inv = 1.f;
+  if (norm_pix) {
+    if (threadIdx.x == 0) shift_s = to_f<TV>(*run_ptr(0));
+    __syncthreads();
+    const float shift = shift_s;
+    float s = 0.f, ss = 0.f;
+    for (int u = threadIdx.x; u < runs; u += blockDim.x) {
+      float x[8];
+      load8<TV>(run_ptr(u), x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = x[j] - shift;
+        s += d;
+        ss += d * d;
+      }
+    }
+    const float tot_s = block_sum(s);
+    const float tot_ss = block_sum(ss);
+    const float m_shifted = tot_s / P;
+    mean = shift + m_shifted;
+    const float var = fmaxf(tot_ss - tot_s * m_shifted, 0.f) / (float)(P > 1 ? P - 1 : 1);
+    inv = rsqrtf(var + 1e-6f);
+  }
+  const float n_masked = counts[0], n_visible = counts[1];
+  const float gscale = mk != 0.f ? 1.f / (float)P / n_masked : 0.f;
+  float ae = 0.f;
+  for (int u = threadIdx.x; u < runs; u += blockDim.x) {
+    float x[8], p[8], g[8];
+    load8<TV>(run_ptr(u), x);
+    load8<TP>(pr + u * 8, p);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float diff = p[j] - (x[j] - mean) * inv;
+      ae += fabsf(diff);
+      g[j] = diff > 0.f ? gscale : (diff < 0.f ? -gscale : 0.f);
+    }
+    store8<TP>(gr + u * 8, g);
+  }
+  const float tot = block_sum(ae) / (float)P;
+  if (threadIdx.x == 0) {
+    if (mk != 0.f) atomicAdd(&sums[0], tot / n_masked);
+    else atomicAdd(&sums[1], tot / n_visible);
+  }
+}
+
+void masked_l1(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, torch::Tensor sums, torch::Tensor grad,
+               int64_t pd, int64_t ph, int64_t pw, bool norm_pix) {
+  TORCH_CHECK(pred.is_cuda() && pred.is_contiguous() && vol.is_contiguous() && mask.is_contiguous(),
+              "masked_l1: contiguous CUDA inputs");
+  TORCH_CHECK(mask.scalar_type() == at::kFloat && sums.scalar_type() == at::kFloat && sums.numel() == 2,
+              "masked_l1: fp32 mask and a 2-element fp32 sums buffer");
+  const int B = (int)vol.size(0), C = (int)vol.size(1), D = (int)vol.size(2), H = (int)vol.size(3), W = (int)vol.size(4);
+  const int N = (int)pred.size(1);
+  const int P = (int)pred.size(2);
+  TORCH_CHECK(P == C * pd * ph * pw, "masked_l1: patch width mismatch");
+  TORCH_CHECK(pw % 8 == 0 && W % 8 == 0, "masked_l1: the W extent of a patch must be a multiple of 8");
+  TORCH_CHECK(mask.numel() == (int64_t)B * N, "masked_l1: one mask value per patch");
+  c10::cuda::CUDAGuard guard(pred.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  auto masked = mask.sum();
+  auto counts = torch::stack({masked.clamp_min(1.0), (masked.neg() + (double)mask.numel()).clamp_min(1.0)});
+  C10_CUDA_CHECK(cudaMemsetAsync(sums.data_ptr(), 0, 2 * sizeof(float), stream));
+  auto launch = [&](auto p_tag, auto v_tag) {
+    using TP = decltype(p_tag);
+    using TV = decltype(v_tag);
+    masked_l1_kernel<TP, TV><<<B * N, 256, 0, stream>>>(
+        reinterpret_cast<const TP*>(pred.data_ptr()), reinterpret_cast<const TV*>(vol.data_ptr()), mask.data_ptr<float>(),
+        counts.data_ptr<float>(), sums.data_ptr<float>(), reinterpret_cast<TP*>(grad.data_ptr()), C, D, H, W, (int)pd,
+        (int)ph, (int)pw, N, norm_pix ? 1 : 0);
+  };
+  const bool pf = pred.scalar_type() == at::kFloat, vf = vol.scalar_type() == at::kFloat;
+  if (pf && vf) launch(float{}, float{});
+  else if (pf && !vf) launch(float{}, bf16{});
+  else if (!pf && vf) launch(bf16{}, float{});
+  else launch(bf16{}, bf16{});
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void norm_pix_mse(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, torch::Tensor loss, torch::Tensor grad,
                   int64_t pd, int64_t ph, int64_t pw, bool norm_pix) {
   TORCH_CHECK(pred.is_contiguous() && vol.is_contiguous() && mask.is_contiguous(), "norm_pix_mse: contiguous inputs");

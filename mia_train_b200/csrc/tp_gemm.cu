@@ -777,45 +777,75 @@ __global__ void __launch_bounds__(kRsThreads, 1)
         if (!ready) break;
         const int r0 = max(mb * 128, row_lo) - row_lo, r1 = min(mb * 128 + 128, row_hi) - row_lo;
         const int total = (r1 - r0) * vpr;
-        for (int v = et; v < total; v += 32 * kEpi) {
-          const int lr = r0 + v / vpr, n = (v % vpr) * 8;
-          float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        // Four 8-element vectors per thread per pass, their W slot loads issued together.
+        constexpr int kU = 4;
+        constexpr int kStride = 32 * kEpi;
+        for (int base = 0; base < total; base += kStride * kU) {
+          float a[kU][8];
+          int64_t off[kU];
+          bool live[kU];
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const int v = base + u * kStride + et;
+            live[u] = v < total;
+            const int vv = live[u] ? v : 0;
+            off[u] = (int64_t)(r0 + vv / vpr) * s.N + (vv % vpr) * 8;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[u][j] = 0.f;
+          }
           for (int q = 0; q < s.world; ++q) {
-            const uint4 u = __ldcg(reinterpret_cast<const uint4*>(recv + q * slot_elems + (int64_t)lr * s.N + n));
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+            uint4 x[kU];
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              a[2 * h] += bf16_lo(w[h]);
-              a[2 * h + 1] += bf16_hi(w[h]);
+            for (int u = 0; u < kU; ++u)
+              if (live[u]) x[u] = __ldcg(reinterpret_cast<const uint4*>(recv + q * slot_elems + off[u]));
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+              if (!live[u]) continue;
+              const uint32_t w[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                a[u][2 * h] += bf16_lo(w[h]);
+                a[u][2 * h + 1] += bf16_hi(w[h]);
+              }
             }
           }
-          if (P.bias != nullptr) {
-            const float4 b0 = __ldg(reinterpret_cast<const float4*>(P.bias + n));
-            const float4 b1 = __ldg(reinterpret_cast<const float4*>(P.bias + n + 4));
-            a[0] += b0.x; a[1] += b0.y; a[2] += b0.z; a[3] += b0.w;
-            a[4] += b1.x; a[5] += b1.y; a[6] += b1.z; a[7] += b1.w;
-          }
-          const int64_t o = (int64_t)lr * s.N + n;
-          if (P.pre_out != nullptr)
-            *reinterpret_cast<uint4*>(P.pre_out + o) =
-                make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
-          if (P.gamma != nullptr) {
-            const float4 g0 = __ldg(reinterpret_cast<const float4*>(P.gamma + n));
-            const float4 g1 = __ldg(reinterpret_cast<const float4*>(P.gamma + n + 4));
-            a[0] *= g0.x; a[1] *= g0.y; a[2] *= g0.z; a[3] *= g0.w;
-            a[4] *= g1.x; a[5] *= g1.y; a[6] *= g1.z; a[7] *= g1.w;
-          }
+          uint4 res[kU];
           if (P.residual != nullptr) {
-            const uint4 u = __ldg(reinterpret_cast<const uint4*>(P.residual + o));
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              a[2 * h] += bf16_lo(w[h]);
-              a[2 * h + 1] += bf16_hi(w[h]);
-            }
+            for (int u = 0; u < kU; ++u)
+              if (live[u]) res[u] = __ldg(reinterpret_cast<const uint4*>(P.residual + off[u]));
           }
-          *reinterpret_cast<uint4*>(P.out + o) =
-              make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            if (!live[u]) continue;
+            const int n = (int)(off[u] % s.N);
+            float* av = a[u];
+            if (P.bias != nullptr) {
+              const float4 b0 = __ldg(reinterpret_cast<const float4*>(P.bias + n));
+              const float4 b1 = __ldg(reinterpret_cast<const float4*>(P.bias + n + 4));
+              av[0] += b0.x; av[1] += b0.y; av[2] += b0.z; av[3] += b0.w;
+              av[4] += b1.x; av[5] += b1.y; av[6] += b1.z; av[7] += b1.w;
+            }
+            if (P.pre_out != nullptr)
+              *reinterpret_cast<uint4*>(P.pre_out + off[u]) = make_uint4(
+                  pack_bf16x2(av[0], av[1]), pack_bf16x2(av[2], av[3]), pack_bf16x2(av[4], av[5]), pack_bf16x2(av[6], av[7]));
+            if (P.gamma != nullptr) {
+              const float4 g0 = __ldg(reinterpret_cast<const float4*>(P.gamma + n));
+              const float4 g1 = __ldg(reinterpret_cast<const float4*>(P.gamma + n + 4));
+              av[0] *= g0.x; av[1] *= g0.y; av[2] *= g0.z; av[3] *= g0.w;
+              av[4] *= g1.x; av[5] *= g1.y; av[6] *= g1.z; av[7] *= g1.w;
+            }
+            if (P.residual != nullptr) {
+              const uint32_t w[4] = {res[u].x, res[u].y, res[u].z, res[u].w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                av[2 * h] += bf16_lo(w[h]);
+                av[2 * h + 1] += bf16_hi(w[h]);
+              }
+            }
+            *reinterpret_cast<uint4*>(P.out + off[u]) = make_uint4(
+                pack_bf16x2(av[0], av[1]), pack_bf16x2(av[2], av[3]), pack_bf16x2(av[4], av[5]), pack_bf16x2(av[6], av[7]));
+          }
         }
       }
     }

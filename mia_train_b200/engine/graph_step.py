@@ -255,6 +255,7 @@ class CapturedStep:
         dp_impl: str = "p2p",
         comm_timeout_ms: float = 10_000.0,
         overlap: bool = False,
+        dp_wire: str = "bf16",
     ) -> None:
         if not hasattr(optimizer, "grad_scale"):
             raise TypeError("CapturedStep needs the fused optimizer (FusedAdamW)")
@@ -290,6 +291,7 @@ class CapturedStep:
             self.zero = ShardedStep(
                 self.flat, optimizer, process_group, "p2p" if self.dp_impl == "p2p" else "nccl",
                 config.grad_clip_norm, self.schedule.current, ipc=ipc, timeout_ms=comm_timeout_ms,
+                wire_dtype=dp_wire,
             )
         # Reduce-scatter each block's weight gradients on a side stream as soon as the block's
         # backward has been issued (its input gradient is the last thing it computes).

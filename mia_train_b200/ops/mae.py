@@ -106,3 +106,63 @@ def norm_pix_mse(
     ):
         return _NativeNormPixMSE.apply(prediction, volumes, mask, tuple(patch), norm_pix)
     return norm_pix_mse_reference(prediction.float(), volumes.float(), mask.float(), patch, norm_pix)
+
+
+def masked_l1_reference(
+    prediction: torch.Tensor,
+    volumes: torch.Tensor,
+    mask: torch.Tensor,
+    patch: tuple[int, ...],
+    norm_pix: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """SimMIM's (masked-patch mean L1, visible-patch mean L1) in PyTorch ops."""
+    target = patchify_reference(volumes, patch)
+    if norm_pix:
+        mean = target.mean(dim=-1, keepdim=True)
+        var = target.var(dim=-1, keepdim=True)
+        target = (target - mean) / torch.sqrt(var + 1e-6)
+    per_patch = (prediction.float() - target.float()).abs().mean(dim=-1)
+    m = mask.float()
+    loss = (per_patch * m).sum() / m.sum().clamp_min(1.0)
+    visible = (per_patch * (1 - m)).sum() / (1 - m).sum().clamp_min(1.0)
+    return loss, visible.detach()
+
+
+class _NativeMaskedL1(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, prediction, volumes, mask, patch, norm_pix):  # type: ignore[override]
+        pred = prediction.contiguous()
+        sums = torch.zeros(2, device=pred.device, dtype=torch.float32)
+        grad = torch.empty_like(pred)
+        native().masked_l1(pred, volumes.contiguous(), mask.float().contiguous(), sums, grad, patch[0], patch[1],
+                           patch[2], bool(norm_pix))
+        ctx.save_for_backward(grad)
+        loss, visible = sums[0].clone(), sums[1].clone()
+        ctx.mark_non_differentiable(visible)
+        return loss, visible
+
+    @staticmethod
+    def backward(ctx, dloss, _dvisible):  # type: ignore[override]
+        (grad,) = ctx.saved_tensors
+        return grad * dloss.to(grad.dtype), None, None, None, None
+
+
+def masked_l1(
+    prediction: torch.Tensor,
+    volumes: torch.Tensor,
+    mask: torch.Tensor,
+    patch: tuple[int, ...],
+    norm_pix: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """(mean L1 over masked patches, mean L1 over visible patches) of (B, N, C * prod(patch)) predictions
+    against the patches of (B, C, D, H, W) volumes; the native kernel reads target patches straight
+    from the volume and writes d(prediction) in the same pass."""
+    if (
+        use_native(prediction)
+        and len(patch) == 3
+        and prediction.dtype in (torch.bfloat16, torch.float32)
+        and volumes.dtype in (torch.float32, torch.bfloat16)
+        and patch[2] % 8 == 0
+    ):
+        return _NativeMaskedL1.apply(prediction, volumes, mask, tuple(patch), norm_pix)
+    return masked_l1_reference(prediction, volumes, mask, patch, norm_pix)

@@ -95,12 +95,18 @@ def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20, tc_mode: in
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
         bwd_us = _time(lambda: ext.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, scale), iters)
         sdpa_us = _time(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=scale), iters)
+        # SDPA backward alone: one forward with autograd, then time the backward of that graph
+        qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+        out_g = torch.nn.functional.scaled_dot_product_attention(qg, kg, vg, scale=scale)
+        go = torch.randn_like(out_g)
+        sdpa_bwd_us = _time(lambda: torch.autograd.grad(out_g, (qg, kg, vg), go, retain_graph=True), iters)
     finally:
         ext.set_tc_attention_mode(previous)
     flops = 4.0 * b * h * n * n * d
     return {"tc_mode": tc_mode, "fwd_us": round(fwd_us, 2), "fwd_tflops": round(flops / fwd_us / 1e6, 1),
             "bwd_us": round(bwd_us, 2), "bwd_tflops": round(2.5 * flops / bwd_us / 1e6, 1),
-            "sdpa_fwd_us": round(sdpa_us, 2)}
+            "sdpa_fwd_us": round(sdpa_us, 2), "sdpa_bwd_us": round(sdpa_bwd_us, 2),
+            "fwd_vs_sdpa": round(sdpa_us / fwd_us, 3), "bwd_vs_sdpa": round(sdpa_bwd_us / bwd_us, 3)}
 
 
 def bench_sinkhorn(b: int, k: int, iters: int = 3, reps: int = 20) -> dict:

@@ -121,3 +121,24 @@ def test_sinkhorn_native_matches_reference(b, k, iters, dtype):
     assert got.shape == ref.shape and got.dtype == torch.float32
     torch.testing.assert_close(got, ref, rtol=1e-3, atol=1e-6 * float(ref.abs().max()))
     torch.testing.assert_close(got.sum(dim=1), ref.sum(dim=1), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs CUDA")
+@pytest.mark.parametrize("norm_pix", [False, True])
+def test_simmim_masked_l1_native(norm_pix):
+    from mia_train_b200.ops.mae import masked_l1, masked_l1_reference
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    vol = torch.randn(2, 1, 32, 32, 32, device=dev, generator=g)
+    mask = torch.rand(2, 64, device=dev, generator=g) < 0.6
+    pred = torch.randn(2, 64, 512, device=dev, generator=g).bfloat16().requires_grad_(True)
+    loss, vis = masked_l1(pred, vol, mask, (8, 8, 8), norm_pix)
+    loss.backward()
+    pr = pred.detach().float().requires_grad_(True)
+    rl, rv = masked_l1_reference(pr, vol, mask, (8, 8, 8), norm_pix)
+    rl.backward()
+    assert abs(float(loss) - float(rl)) < 1e-3 * max(1.0, abs(float(rl)))
+    assert abs(float(vis) - float(rv)) < 1e-3 * max(1.0, abs(float(rv)))
+    # sign gradients: compare where the reference's |diff| is not tiny (bf16 prediction)
+    assert float((pred.grad.float() - pr.grad).abs().max()) <= 2.0 / 512 / float(mask.sum()) + 1e-9

@@ -86,11 +86,11 @@ def main() -> None:
             # compare against the gathered full gradient
             parts = [torch.empty_like(p.grad) for _ in range(world)]
             dist.all_gather(parts, p.grad.contiguous())
-            mode = mod._tp_mode
-            if mode == "qkv":
+            tp_mode = mod._tp_mode
+            if tp_mode == "qkv":
                 per = p.shape[0] // 3
                 full = torch.cat([parts[r][q * per:(q + 1) * per] for q in range(3) for r in range(world)])
-            elif mode == "column" or p.dim() == 1:
+            elif tp_mode == "column" or p.dim() == 1:
                 full = torch.cat(parts, dim=0)
             else:
                 full = torch.cat(parts, dim=1)

@@ -28,6 +28,8 @@ from mia_train_b200.ops import _native  # noqa: E402
 def train(impl: str, rank: int, dev: torch.device, steps: int) -> tuple[list[torch.Tensor], list[float]]:
     overlap = not impl.endswith("_serial")
     impl = impl.removesuffix("_serial")
+    wire = "fp32" if impl.endswith("_fp32") else "bf16"
+    impl = impl.removesuffix("_fp32")
     torch.manual_seed(0)
     model = ViT3D(img_size=(32, 32, 32), patch_size=(8, 8, 8), embed_dim=128, depth=2, num_heads=4)
     alg = MAE(model, input_axes="lcxyz", decoder_embed_dim=64, decoder_depth=1, decoder_num_heads=4).to(dev)
@@ -38,7 +40,7 @@ def train(impl: str, rank: int, dev: torch.device, steps: int) -> tuple[list[tor
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     batches = [torch.randn(2, 1, 1, 32, 32, 32, device=dev, generator=g) for _ in range(steps)]
     step = CapturedStep(alg, opt, cfg, {"img": batches[0]}, eager_steps=2, process_group=dist.group.WORLD,
-                        dp_impl=impl, overlap=overlap)
+                        dp_impl=impl, overlap=overlap, dp_wire=wire)
     losses = []
     for b in batches:
         m = step({"img": b})
@@ -56,10 +58,11 @@ def main() -> None:
     rank = dist.get_rank()
     _native.native()
     steps = 5
-    results = {impl: train(impl, rank, dev, steps) for impl in ("allreduce", "nccl", "p2p", "p2p_serial")}
+    impls = ("allreduce", "nccl", "p2p", "p2p_serial", "p2p_fp32")
+    results = {impl: train(impl, rank, dev, steps) for impl in impls}
     ref, _ = results["allreduce"]
     diffs = {}
-    for impl in ("nccl", "p2p", "p2p_serial"):
+    for impl in impls[1:]:
         params, _ = results[impl]
         diffs[impl] = max(float((a - b).abs().max() / (b.abs().max() + 1e-12)) for a, b in zip(params, ref, strict=True))
     # replicas must agree exactly with each other after the final gather
