@@ -28,6 +28,7 @@
 #include <torch/extension.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -73,8 +74,8 @@ __device__ __forceinline__ float fast_exp2f(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, used for a quarter of the softmax exponentials so the multi-function unit
-// (16 results per clock per SM, the limiter of these kernels) and the FMA pipe share the work.
+// 2^x on the FMA pipe, optionally used for a quarter of the softmax exponentials so the
+// multi-function unit (16 results per clock per SM) and the FMA pipe share the work.
 // Range reduction x = n + f with n = floor(x), f in [0, 1); 2^f by a cubic fitted here to minimise
 // the relative error on [0, 1) (iteratively reweighted least squares over 20001 points): maximum
 // relative error 7.6e-5, far below the bf16 rounding (3.9e-3) that P is stored with; 2^n is added to
@@ -87,7 +88,7 @@ __device__ __forceinline__ float poly_exp2f(float x) {
   return x < -125.f ? 0.f : y;
 }
 
-template <int D>
+template <int D, bool kPoly>
 __global__ void __launch_bounds__(kTcThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ o, float* __restrict__ lse, int H,
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const float p0 =
                 (kFull || key < Nk) ? fast_exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, -m_new)) : 0.f;
             const float x1 = fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, -m_new);
-            const float p1 = (kFull || key + 1 < Nk) ? ((e & 1) ? fast_exp2f(x1) : poly_exp2f(x1)) : 0.f;
+            const float p1 = (kFull || key + 1 < Nk) ? ((!kPoly || (e & 1)) ? fast_exp2f(x1) : poly_exp2f(x1)) : 0.f;
             rs += p0 + p1;
             pk[e] = pack_bf16x2(p0, p1);
           }
@@ -379,7 +380,7 @@ struct TcBwdSmem {
   static constexpr int kBytes = kBar + 160 + 1024;
 };
 
-template <int D>
+template <int D, bool kPoly>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const int e = e4 * 2 + e2;
             const float p0 = fast_exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, -ls[2 * e2]));
             const float x1 = fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, -ls[2 * e2 + 1]);
-            const float p1 = e2 ? fast_exp2f(x1) : poly_exp2f(x1);
+            const float p1 = (!kPoly || e2) ? fast_exp2f(x1) : poly_exp2f(x1);
             const float d0 = p0 * (__uint_as_float(dpv[2 * e]) - ds[2 * e2]);
             const float d1 = p1 * (__uint_as_float(dpv[2 * e + 1]) - ds[2 * e2 + 1]);
             pk[e] = pack_bf16x2(p0, p1);
@@ -723,13 +724,20 @@ bool make_head_map(CUtensorMap* map, const void* base, int B, int H, int N, int 
 }
 
 std::atomic<int> g_tc_attention_mode{1};
+// 1: a quarter of the softmax exponentials on the FMA pipe (poly_exp2f); 0 (default): all on the
+// MUFU unit. Measured on B200 the split is 5-15% slower at every shape tried (512 x 32 to 32768 x 64):
+// the FMA pipe is busy with the scaling, packing and row sums already.
+std::atomic<int> g_attention_poly_exp{[] {
+  const char* v = std::getenv("MIA_ATTN_POLY");
+  return v == nullptr ? 0 : std::atoi(v);
+}()};
 std::atomic<int64_t> g_tc_attention_launches{0};
 
-template <int D>
+template <int D, bool kPoly>
 void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, torch::Tensor& o,
                 torch::Tensor& lse, int B, int H, int Nq, int Nk, float scale_log2, int device, cudaStream_t stream) {
   using L = TcFwdSmem<D>;
-  auto kern = attn_fwd_tc_kernel<D>;
+  auto kern = attn_fwd_tc_kernel<D, kPoly>;
   C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int q_tiles = (Nq + kTcBM - 1) / kTcBM;
   const long grid = (long)q_tiles * B * H;
@@ -739,14 +747,14 @@ void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int D>
+template <int D, bool kPoly>
 void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                 const torch::Tensor& lse, const torch::Tensor& delta, torch::Tensor& dq_acc, Strides3 dqs,
                 torch::Tensor& dk, Strides3 dks, torch::Tensor& dv, Strides3 dvs, int B, int H, int Nq, int Nk,
                 float scale, int device, cudaStream_t stream) {
   using L = TcBwdSmem<D>;
   static_assert(L::kBytes <= 232448, "backward shared memory exceeds 227 KB");
-  auto kern = attn_bwd_tc_kernel<D>;
+  auto kern = attn_bwd_tc_kernel<D, kPoly>;
   C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int k_tiles = (Nk + 127) / 128;
   const long grid = (long)k_tiles * B * H;
@@ -770,8 +778,14 @@ bool attention_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torc
     return false;
   const int device = q.get_device();
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (D == 64) launch_fwd<64>(mq, mk, mv, o, lse, B, H, Nq, Nk, scale_log2, device, stream);
-  else launch_fwd<32>(mq, mk, mv, o, lse, B, H, Nq, Nk, scale_log2, device, stream);
+  const bool poly = g_attention_poly_exp.load() != 0;
+  if (D == 64) {
+    if (poly) launch_fwd<64, true>(mq, mk, mv, o, lse, B, H, Nq, Nk, scale_log2, device, stream);
+    else launch_fwd<64, false>(mq, mk, mv, o, lse, B, H, Nq, Nk, scale_log2, device, stream);
+  } else {
+    if (poly) launch_fwd<32, true>(mq, mk, mv, o, lse, B, H, Nq, Nk, scale_log2, device, stream);
+    else launch_fwd<32, false>(mq, mk, mv, o, lse, B, H, Nq, Nk, scale_log2, device, stream);
+  }
   g_tc_attention_launches.fetch_add(1);
   return true;
 }
@@ -795,10 +809,17 @@ bool attention_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torc
     return false;
   const int device = q.get_device();
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (D == 64)
-    launch_bwd<64>(mq, mk, mv, mdo, lse, delta, dq_acc, dqs, dk, dks, dv, dvs, B, H, Nq, Nk, scale, device, stream);
-  else
-    launch_bwd<32>(mq, mk, mv, mdo, lse, delta, dq_acc, dqs, dk, dks, dv, dvs, B, H, Nq, Nk, scale, device, stream);
+  const bool poly = g_attention_poly_exp.load() != 0;
+#define MIA_BWD(DD, PP) \
+  launch_bwd<DD, PP>(mq, mk, mv, mdo, lse, delta, dq_acc, dqs, dk, dks, dv, dvs, B, H, Nq, Nk, scale, device, stream)
+  if (D == 64) {
+    if (poly) MIA_BWD(64, true);
+    else MIA_BWD(64, false);
+  } else {
+    if (poly) MIA_BWD(32, true);
+    else MIA_BWD(32, false);
+  }
+#undef MIA_BWD
   g_tc_attention_launches.fetch_add(1);
   return true;
 }
@@ -806,5 +827,7 @@ bool attention_bwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torc
 void set_tc_attention_mode(int64_t mode) { g_tc_attention_mode.store((int)mode); }
 int64_t tc_attention_mode() { return g_tc_attention_mode.load(); }
 int64_t tc_attention_launches() { return g_tc_attention_launches.load(); }
+
+int64_t set_attention_poly_exp(int64_t mode) { return g_attention_poly_exp.exchange((int)mode); }
 
 }  // namespace mia

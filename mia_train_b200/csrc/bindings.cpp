@@ -80,6 +80,7 @@ int64_t tp_flag_bytes();
 void soft_ce_fwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse, at::Tensor loss);
 void soft_ce_bwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse,
                  at::Tensor grad_scale, at::Tensor dS);
+int64_t set_attention_poly_exp(int64_t mode);
 void masked_l1(torch::Tensor pred, torch::Tensor vol, torch::Tensor mask, torch::Tensor sums, torch::Tensor grad,
                int64_t pd, int64_t ph, int64_t pw, bool norm_pix);
 void koleo_fwd(at::Tensor x, double eps, at::Tensor xn, at::Tensor nn, at::Tensor dist, at::Tensor loss);
@@ -133,6 +134,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_flag_bytes", &mia::tp_flag_bytes, "bytes of one rank's flag area for the fused TP kernels");
   m.def("soft_ce_fwd", &mia::soft_ce_fwd, "soft-target cross-entropy over prototypes (DINO / iBOT): lse + per-row loss");
   m.def("soft_ce_bwd", &mia::soft_ce_bwd, "gradient of soft_ce_fwd with respect to the student logits");
+  m.def("set_attention_poly_exp", &mia::set_attention_poly_exp,
+        "1: a quarter of the attention softmax exponentials on the FMA pipe; 0: all on MUFU; returns the previous");
   m.def("masked_l1", &mia::masked_l1, "SimMIM masked L1 (targets read from the volume) + gradient");
   m.def("koleo_fwd", &mia::koleo_fwd, "KoLeo: normalise, nearest neighbour, -mean log distance");
   m.def("koleo_bwd", &mia::koleo_bwd, "gradient of koleo_fwd");

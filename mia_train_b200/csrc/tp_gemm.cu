@@ -525,8 +525,25 @@ template <int BN, int STAGES>
 struct RsSmem {
   static constexpr int kBTileBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
-  static constexpr int kBytes = STAGES * kStageBytes + 1024 + 512 + kMaxOwned * 4;
+  static constexpr int kStagingBytes = 128 * BN * 2;  // one bf16 output tile, 16-byte chunks XOR-swizzled by row
+  static constexpr int kBytes = STAGES * kStageBytes + kStagingBytes + 1024 + 512 + kMaxOwned * 4 + 256;
 };
+
+// Bounded wait until *counter >= target (shared memory, written by other warps of this CTA).
+__device__ __forceinline__ bool spin_ge(const volatile int* counter, int target, volatile int* abort_flag, int* err,
+                                        int code) {
+  if (*counter >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (*counter < target) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > MIA_WAIT_LIMIT_NS) {
+      record_error(err, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
 
 // CTA b owns the 128-row blocks b, b + G, ... and computes every N tile of a block before the next
 // block, so it alone decides when a block's partial rows are complete and publishes them. Blocks
@@ -549,7 +566,10 @@ __global__ void __launch_bounds__(kRsThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* block_arrivals = reinterpret_cast<int*>(tmem_slot + 2);  // [4], by block sequence index mod 4
   int* nseq_slot = reinterpret_cast<int*>(tmem_slot + 6);
+  volatile int* staged = reinterpret_cast<volatile int*>(tmem_slot + 7);  // epilogue warps done writing the tile
+  volatile int* drained = reinterpret_cast<volatile int*>(tmem_slot + 8);  // ... done storing it out
   int* seq = reinterpret_cast<int*>(smem + STAGES * L::kStageBytes + 512);
+  uint4* staging = reinterpret_cast<uint4*>(smem + STAGES * L::kStageBytes + 512 + kMaxOwned * 4);
 
   const TpShape& s = P.s;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -573,6 +593,8 @@ __global__ void __launch_bounds__(kRsThreads, 1)
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     for (int j = 0; j < 4; ++j) block_arrivals[j] = 0;
+    *staged = 0;
+    *drained = 0;
     int n = 0;
     for (int d = 1; d <= s.world; ++d) {
       const int owner = (s.rank + d) % s.world;
@@ -697,56 +719,75 @@ __global__ void __launch_bounds__(kRsThreads, 1)
     }
   } else {
     // ---------------- epilogue warps: partial rows -> owner's receive slot
+    // Each warp converts its 32 rows x BN / 2 columns to bf16 into the shared staging tile and
+    // releases the accumulator; once all eight warps have staged the tile, warp w stores rows
+    // [16 w, 16 w + 16) out, two rows of BN * 2 contiguous bytes per instruction, so the NVLink
+    // writes go out as whole row segments rather than 16-byte pieces of 32 different rows.
+    static_assert(BN == 128, "the staged reduce-scatter epilogue is written for 128-column tiles");
     const int lane_group = warp % 4;
     const int col_part = (warp - 2) / 4;
+    const int ew = warp - 2;
     constexpr int kPartCols = BN / 2;
+    constexpr int kChunksPerRow = BN / 8;
     const int et = threadIdx.x - 64;  // 0 .. 32 * kEpi - 1
     int acc = 0;
     uint32_t acc_phase = 0;
+    int tile_seq = 0;
     bool ok = true;
     for (int i = 0; i < nseq && ok; ++i) {
       const int mb = seq[i];
-      const int m = mb * 128 + lane_group * 32 + lane;
-      __nv_bfloat16* dst_row = nullptr;
-      if (m < s.M) {
-        const int owner = m / s.S;
-        dst_row = reinterpret_cast<__nv_bfloat16*>(pick(P.recv, owner)) + par_off + (int64_t)s.rank * slot_elems +
-                  (int64_t)(m - owner * s.S) * s.N;
-      }
       for (int nt = 0; nt < num_n; ++nt) {
-        if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, P.err, kErrGemmEpilogueWait)) {
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, P.err, kErrGemmEpilogueWait) ||
+            !spin_ge(drained, kEpi * tile_seq, abort_flag, P.err, kErrGemmEpilogueWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int n0 = nt * BN + col_part * kPartCols;
+        const int n0 = nt * BN;
+        const int row = lane_group * 32 + lane;
         const uint32_t t_row = tmem_base + ((uint32_t)(lane_group * 32) << 16) + acc * BN + col_part * kPartCols;
 #pragma unroll 1
         for (int c = 0; c < kPartCols / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);
           tmem_ld_wait_regs(r);
-          const int n = n0 + c * 32;
-          if (dst_row != nullptr && n < s.N) {
-            if (n + 32 <= s.N) {
-              uint4* d4 = reinterpret_cast<uint4*>(dst_row + n);
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                d4[q] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1])),
-                                   pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
-                                   pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
-                                   pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n + j < s.N) dst_row[n + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
-            }
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = col_part * (kPartCols / 8) + c * 4 + q;
+            staging[row * kChunksPerRow + (chunk ^ (row & 15))] =
+                make_uint4(pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1])),
+                           pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
+                           pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
+                           pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
           }
         }
         tc_fence_before();
-        mbar_arrive(&tempty_bar[acc]);  // the MMA may refill this accumulator while we publish
+        mbar_arrive(&tempty_bar[acc]);  // the MMA may refill this accumulator while we store
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) atomicAdd(const_cast<int*>(staged), 1);
+        if (!spin_ge(staged, kEpi * (tile_seq + 1), abort_flag, P.err, kErrGemmEpilogueWait)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int tr = 16 * ew + 2 * it + (lane >> 4);
+          const int ch = lane & 15;
+          const int gm = mb * 128 + tr;
+          const int gn = n0 + ch * 8;
+          if (gm < s.M && gn < s.N) {
+            const int owner = gm / s.S;
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(pick(P.recv, owner)) + par_off +
+                                 (int64_t)s.rank * slot_elems + (int64_t)(gm - owner * s.S) * s.N + gn;
+            *reinterpret_cast<uint4*>(dst) = staging[tr * kChunksPerRow + (ch ^ (tr & 15))];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) atomicAdd(const_cast<int*>(drained), 1);
+        ++tile_seq;
       }
       if (!ok) break;
       // The block's partial rows are stored: make them visible system-wide, then the last warp of this
@@ -1008,7 +1049,7 @@ namespace tp {
 template <int BN, bool A_MN, bool B_MN>
 static void launch_rs(const CUtensorMap& ta, const CUtensorMap& tb, const RsParams& prm, int grid, cudaStream_t st,
                       int device) {
-  constexpr int ST = BN == 256 ? 4 : 6;
+  constexpr int ST = 5;
   using L = RsSmem<BN, ST>;
   auto kern = tp_gemm_rs_kernel<BN, A_MN, B_MN, ST>;
   static bool configured[64] = {false};
@@ -1075,18 +1116,13 @@ void tp_gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, c10::optional<at::Te
   prm.residual = mat(residual);
   prm.pre_out = mat(pre_out);
   prm.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms * 1e6 : 5e9);
-  const int bn = N <= 128 ? 128 : 256;
+  const int bn = 128;  // the staged epilogue stores 128-column tiles
   const int grid = (int)std::min<int64_t>(prm.s.num_blocks, sm_count(device));
   TORCH_CHECK(prm.s.num_blocks <= (int64_t)grid * kMaxOwned, "tp_gemm_rs: too many row blocks per CTA");
   CUtensorMap ta = make_bf16_map(a.data_ptr(), K, M, K, 64, kBM);
   CUtensorMap tb = b_kmajor ? make_bf16_map(b.data_ptr(), K, N, K, 64, bn) : make_bf16_map(b.data_ptr(), N, K, N, 64, 64);
-  if (bn == 256) {
-    if (b_kmajor) launch_rs<256, false, false>(ta, tb, prm, grid, stream, device);
-    else launch_rs<256, false, true>(ta, tb, prm, grid, stream, device);
-  } else {
-    if (b_kmajor) launch_rs<128, false, false>(ta, tb, prm, grid, stream, device);
-    else launch_rs<128, false, true>(ta, tb, prm, grid, stream, device);
-  }
+  if (b_kmajor) launch_rs<128, false, false>(ta, tb, prm, grid, stream, device);
+  else launch_rs<128, false, true>(ta, tb, prm, grid, stream, device);
 }
 
 int64_t tp_flag_bytes() { return tp::flag_bytes(); }

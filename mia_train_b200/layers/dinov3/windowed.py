@@ -17,10 +17,10 @@ import functools
 import torch
 import torch.nn.functional as F
 
-from ..layers.dinov3.block import SelfAttentionBlock
-from ..layers.dinov3.rope import RopeTables
-from ..ops.attention import attention, rope_attention, rotate_pairs
-from ..parallel.tensor_parallel import rope_to_tp
+from ...ops.attention import attention, rope_attention
+from ...parallel.tensor_parallel import rope_to_tp
+from .block import SelfAttentionBlock
+from .rope import RopeTables
 
 
 def window_partition(x: torch.Tensor, grid: tuple[int, int, int], w: int) -> torch.Tensor:
@@ -58,7 +58,10 @@ def windowed_attention(
     pre, pat = qkv[:, :n_prefix], qkv[:, n_prefix:]
     nwin = (grid[0] // w) * (grid[1] // w) * (grid[2] // w)
     win = window_partition(pat, grid, w)  # (B*nw, w^3, 3C)
-    pre_rep = pre.repeat_interleave(nwin, dim=0)  # (B*nw, P, 3C)
+    # prefix rows for every window: a broadcast (its backward is a sum over windows; an index-based
+    # repeat would back-propagate through a sorted scatter with 64-fold duplicate indices)
+    pre_rep = pre.unsqueeze(1).expand(b, nwin, n_prefix, pre.shape[-1]).reshape(b * nwin, n_prefix, pre.shape[-1])
+    pre_rep = pre_rep.contiguous()  # with B = 1 the reshape is a stride-0 view, which takes cat's slow path
     packed = torch.cat([pre_rep, win], dim=1).reshape(b * nwin, n_prefix + w**3, 3, heads, hd)
     angles_win = pairs = None
     if rope is not None:
@@ -75,9 +78,20 @@ def windowed_attention(
     v_all = qkv[..., 2 * c :].reshape(b, n_tok, heads, hd)
     if rope is not None:
         full = F.pad(rope_to_tp(rope.angles.float(), attn), (0, 0, n_prefix, 0)).unsqueeze(0)
-        k_all = rotate_pairs(k_all, full, pairs)
+        k_all = rotate_half(k_all, full)
     out_pre = attention(q_pre.contiguous(), k_all.contiguous(), v_all.contiguous(), attn.scale).reshape(b, n_prefix, c)
     return torch.cat([out_pre, out_pat.to(out_pre.dtype)], dim=1)
+
+
+def rotate_half(x: torch.Tensor, angles: torch.Tensor) -> torch.Tensor:
+    """RoPE with channel pairs (i, i + D / 2) on (B, N, H, D) by (1 or B, N, D / 2) angles, written with
+    slices only, so its backward is elementwise (an index-based rotation back-propagates through a
+    sorted scatter)."""
+    half = x.shape[-1] // 2
+    cos = angles.cos().unsqueeze(-2)
+    sin = angles.sin().unsqueeze(-2)
+    x1, x2 = x[..., :half].float(), x[..., half:].float()
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
 
 
 def windowed_core(grid: tuple[int, int, int], rope: RopeTables | None, n_prefix: int, w: int):

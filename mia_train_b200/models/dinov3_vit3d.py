@@ -240,7 +240,7 @@ class DinoVisionTransformer3D(BaseModel):
 
     def _run_blocks_sequence_parallel(self, sp, tokens_list, grids, shared, take):
         """Blocks on this rank's token rows (crop by crop); tokens are gathered again after the last block."""
-        from .windowed import windowed_core
+        from ..layers.dinov3.windowed import windowed_core
 
         outs: list[torch.Tensor] = []
         taken: list[list[torch.Tensor]] = [[] for _ in self.blocks] if take is not None else []
@@ -268,7 +268,7 @@ class DinoVisionTransformer3D(BaseModel):
 
     def _windowed_block(self, blk: SelfAttentionBlock, x: torch.Tensor, grid, rope) -> torch.Tensor:
         """One block with window attention for patch tokens and global attention for the prefix."""
-        from .windowed import windowed_block_forward
+        from ..layers.dinov3.windowed import windowed_block_forward
 
         return windowed_block_forward(blk, x, grid, rope, self.n_prefix, self.window_size)
 

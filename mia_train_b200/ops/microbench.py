@@ -76,7 +76,7 @@ def mae_step_gemms(batch: int = 16) -> list[tuple[str, int, int, int, str, bool]
     return shapes
 
 
-def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20, tc_mode: int = 1) -> dict:
+def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20, tc_mode: int = 1, poly: int = 1) -> dict:
     """Native attention forward / backward on (b, h, n, d) bf16; tc_mode 1 = tcgen05 kernels where
     they apply, 0 = warp-level kernels. FLOPs: 4 b h n^2 d forward, 2.5x that backward."""
     from . import _native
@@ -85,6 +85,7 @@ def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20, tc_mode: in
     ext = _native.native()
     previous = ext.tc_attention_mode()
     ext.set_tc_attention_mode(tc_mode)
+    previous_poly = ext.set_attention_poly_exp(poly)
     try:
         q, k, v = (torch.randn(b, h, n, d, device=dev).bfloat16() for _ in range(3))
         o = torch.empty(b, n, h, d, device=dev, dtype=torch.bfloat16)
@@ -102,8 +103,9 @@ def bench_attention(b: int, h: int, n: int, d: int, iters: int = 20, tc_mode: in
         sdpa_bwd_us = _time(lambda: torch.autograd.grad(out_g, (qg, kg, vg), go, retain_graph=True), iters)
     finally:
         ext.set_tc_attention_mode(previous)
+        ext.set_attention_poly_exp(previous_poly)
     flops = 4.0 * b * h * n * n * d
-    return {"tc_mode": tc_mode, "fwd_us": round(fwd_us, 2), "fwd_tflops": round(flops / fwd_us / 1e6, 1),
+    return {"tc_mode": tc_mode, "poly_exp": poly, "shape": [b, h, n, d], "fwd_us": round(fwd_us, 2), "fwd_tflops": round(flops / fwd_us / 1e6, 1),
             "bwd_us": round(bwd_us, 2), "bwd_tflops": round(2.5 * flops / bwd_us / 1e6, 1),
             "sdpa_fwd_us": round(sdpa_us, 2), "sdpa_bwd_us": round(sdpa_bwd_us, 2),
             "fwd_vs_sdpa": round(sdpa_us / fwd_us, 3), "bwd_vs_sdpa": round(sdpa_bwd_us / bwd_us, 3)}
@@ -198,6 +200,7 @@ def main() -> None:
     for name, default in (("b", 16), ("h", 16), ("n", 512), ("d", 32), ("iters", 20)):
         at.add_argument(f"--{name}", type=int, default=default)
     at.add_argument("--modes", default="1,0", help="attention kernels: 1 = tcgen05, 0 = warp-level mma")
+    at.add_argument("--poly", default="1", help="comma list: 1 = a quarter of the exponentials on the FMA pipe, 0 = none")
     sk = sub.add_parser("sinkhorn")
     sk.add_argument("--b", type=int, default=2048)
     sk.add_argument("--k", type=int, default=65536)
@@ -213,7 +216,8 @@ def main() -> None:
         print(bench_gemm(args.m, args.n, args.k, args.layout, args.iters, args.fp32_out, args.act))
     elif args.cmd == "attention":
         for mode in (int(x) for x in args.modes.split(",")):
-            print(bench_attention(args.b, args.h, args.n, args.d, args.iters, mode))
+            for poly in (int(x) for x in args.poly.split(",")):
+                print(bench_attention(args.b, args.h, args.n, args.d, args.iters, mode, poly))
     else:
         from . import _native
 
