@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           // D contiguous: MN-major, 16 keys = 16 rows per step).
           tc_mma_f16(t_o, make_sdesc_sw<128>(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                      make_sdesc_sw<L::kRowBytes>(v_addr + kk * 16 * L::kRowBytes, L::kKVBytes, kSbo), idesc_o,
-                     kk > 0 ? 1u : 0u);
+                     (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(v_empty);
         tc_commit(o_full);
@@ -236,24 +236,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
   } else {
     // -------------------------------------------------------------------- softmax warps
+    // O accumulates in TMEM over all key blocks (the PV MMAs accumulate), relative to a reference
+    // row maximum m_ref. P_j = exp2(s - m_ref) is used as long as the block's maximum stays within
+    // kRescale (log2 units) of m_ref, so P <= 2^kRescale; past that, the row's O (once the previous
+    // PV MMA has landed) and l are scaled by exp2(m_ref_old - m_ref_new) in TMEM and m_ref moves.
+    // After the first blocks this is rare, so most blocks do no O traffic at all.
+    constexpr float kRescale = 8.f;
     const int lg = warp & 3;  // TMEM lane quarter this warp may access
     const int r = lg * 32 + lane;
     const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
     uint8_t* P = smem + L::kP;
-    float acc[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) acc[d] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-    auto fold = [&](float a) {
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_o + lane_off + c * 32, v);
-        tmem_ld_wait_regs(v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) acc[c * 32 + e] = fmaf(acc[c * 32 + e], a, __uint_as_float(v[e]));
-      }
-    };
+    float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nb; ++j) {
       if (!warp_wait(s_full, j & 1, abort_flag, err)) {
@@ -275,13 +268,26 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           for (int e = 0; e < 32; ++e)
             if (kFull || kbase + c * 32 + e < Nk) mx = fmaxf(mx, __uint_as_float(v[e]));
         }
-        const float m_new = fmaxf(m, mx * scale_log2);
-        const float alpha = (m == -INFINITY) ? 0.f : fast_exp2f(m - m_new);
-        if (j > 0) {
+        const float blk = mx * scale_log2;
+        const bool move = blk > m + kRescale;  // always true for the first block (m = -inf)
+        if (__any_sync(0xffffffffu, move) && j > 0) {
+          // rescale O (all PV MMAs so far have landed once o_full of block j - 1 completes)
           if (!warp_wait(o_full, (j - 1) & 1, abort_flag, err)) return false;
           tc_fence_after();
-          fold(alpha_prev);
+          const float alpha = move ? fast_exp2f(m - blk) : 1.f;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(t_o + lane_off + c * 32, v);
+            tmem_ld_wait_regs(v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st_32x32b_x32(t_o + lane_off + c * 32, v);
+          }
+          tmem_st_wait();
+          l *= alpha;
         }
+        if (move) m = blk;
         float rs = 0.f;
 #pragma unroll
         for (int c = 0; c < kTcBN / 32; ++c) {
@@ -293,8 +299,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           for (int e = 0; e < 16; ++e) {
             const int key = kbase + c * 32 + 2 * e;
             const float p0 =
-                (kFull || key < Nk) ? fast_exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, -m_new)) : 0.f;
-            const float x1 = fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, -m_new);
+                (kFull || key < Nk) ? fast_exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, -m)) : 0.f;
+            const float x1 = fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, -m);
             const float p1 = (kFull || key + 1 < Nk) ? ((!kPoly || (e & 1)) ? fast_exp2f(x1) : poly_exp2f(x1)) : 0.f;
             rs += p0 + p1;
             pk[e] = pack_bf16x2(p0, p1);
@@ -306,9 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             *dst = make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
           }
         }
-        l = l * alpha + rs;
-        m = m_new;
-        alpha_prev = alpha;
+        l += rs;
         return true;
       };
       const bool done = (kbase + kTcBN <= Nk) ? softmax_block(std::true_type{}) : softmax_block(std::false_type{});
@@ -320,25 +324,28 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && nb > 0) {
-      if (warp_wait(o_full, (nb - 1) & 1, abort_flag, err)) {
-        tc_fence_after();
-        fold(alpha_prev);
-      } else {
-        ok = false;
-      }
-    }
+    if (ok && nb > 0 && !warp_wait(o_full, (nb - 1) & 1, abort_flag, err)) ok = false;
     const int qi = q0 + r;
-    if (ok && qi < Nq) {
+    if (ok && nb > 0) {
+      tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      bf16* orow = o + (((size_t)b * Nq + qi) * H + h) * D;
+      bf16* orow = o + (((size_t)b * Nq + (qi < Nq ? qi : 0)) * H + h) * D;
 #pragma unroll
-      for (int d = 0; d < D; d += 8) {
-        *reinterpret_cast<uint4*>(orow + d) =
-            make_uint4(pack_bf16x2(acc[d] * inv, acc[d + 1] * inv), pack_bf16x2(acc[d + 2] * inv, acc[d + 3] * inv),
-                       pack_bf16x2(acc[d + 4] * inv, acc[d + 5] * inv), pack_bf16x2(acc[d + 6] * inv, acc[d + 7] * inv));
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(t_o + lane_off + c * 32, v);  // warp-wide: every lane takes part
+        tmem_ld_wait_regs(v);
+        if (qi < Nq) {
+#pragma unroll
+          for (int d = 0; d < 32; d += 8)
+            *reinterpret_cast<uint4*>(orow + c * 32 + d) = make_uint4(
+                pack_bf16x2(__uint_as_float(v[d]) * inv, __uint_as_float(v[d + 1]) * inv),
+                pack_bf16x2(__uint_as_float(v[d + 2]) * inv, __uint_as_float(v[d + 3]) * inv),
+                pack_bf16x2(__uint_as_float(v[d + 4]) * inv, __uint_as_float(v[d + 5]) * inv),
+                pack_bf16x2(__uint_as_float(v[d + 6]) * inv, __uint_as_float(v[d + 7]) * inv));
+        }
       }
-      lse[(size_t)bh * Nq + qi] = m + log2f(fmaxf(l, 1e-30f));
+      if (qi < Nq) lse[(size_t)bh * Nq + qi] = m + log2f(fmaxf(l, 1e-30f));
     }
   }
   tc_fence_before();

@@ -52,8 +52,10 @@
 // only, and TMA reads local memory only.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <vector>
 
 #include "common.cuh"
@@ -67,12 +69,8 @@ constexpr int kMaxWorld = 8;
 constexpr int kMaxMBlocks = 2048;  // 128-row blocks of the gathered M: M <= 262144
 constexpr int kMaxOwned = 64;      // row blocks per CTA in the all-gather kernel
 constexpr int kEpi = 8;            // epilogue warps
-constexpr int kCopyWarps = 4;
-constexpr int kCopyThreads = 32 * kCopyWarps;
-constexpr int kAgThreads = 64 + 32 * kEpi + kCopyThreads;  // 448
+constexpr int kAgThreads = 64 + 32 * kEpi + 32;  // producer, MMA, epilogue warps, store warp
 constexpr int kRsThreads = 64 + 32 * kEpi;                 // 320
-constexpr int kCopyCols = 128;   // columns per copy group (two 64-wide K slices)
-constexpr int kCopyInFlight = 12;
 
 // Flag area of one rank (int32):
 //   ag_ready[src][block]  written by src: its rows of gathered block `block` are in its send buffer
@@ -149,48 +147,59 @@ __device__ __forceinline__ int block_src_hi(const TpShape& s, int mb) {
 }
 
 // ------------------------------------------------------------------------------- all-gather GEMM
+// Bounded wait until *counter >= target (shared memory, written by other warps of this CTA).
+__device__ __forceinline__ bool spin_ge(const volatile int* counter, int target, volatile int* abort_flag, int* err,
+                                        int code) {
+  if (*counter >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (*counter < target) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > MIA_WAIT_LIMIT_NS) {
+      record_error(err, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
 struct AgParams {
   GemmParams g;                 // M = gathered rows; D, bias, aux, aux_out, act, err
   TpShape s;
-  const __nv_bfloat16* a_local; // (S, K)
-  __nv_bfloat16* a_full;        // (M, K) gathered output
-  Peers send;                   // every rank's send area (parity 0; parity 1 at + send_parity_elems)
-  int64_t send_parity_elems;
   Peers flags;
   uint64_t timeout_ns;
 };
 
-// Copies rows [0, nrows) x columns [c0, c0 + ncols) (ncols % 8 == 0) from src to dst (row strides in
-// elements), kCopyInFlight 16-byte loads in flight per thread. `ct` is the thread's index among the
-// copy threads. `dst2` (optional) receives the same data with stride ld2.
-template <bool kPeer>
-__device__ __forceinline__ void copy_rows(__nv_bfloat16* dst, int64_t ld_dst, __nv_bfloat16* dst2, int64_t ld2,
-                                          const __nv_bfloat16* src, int64_t ld_src, int nrows, int c0, int ncols,
-                                          int ct) {
-  const int vpr = ncols / 8;
-  const int total = nrows * vpr;
-  for (int base = 0; base < total; base += kCopyThreads * kCopyInFlight) {
-    uint4 buf[kCopyInFlight];
-#pragma unroll
-    for (int u = 0; u < kCopyInFlight; ++u) {
-      const int v = base + u * kCopyThreads + ct;
-      if (v < total) {
-        const int row = v / vpr, col = c0 + (v - row * vpr) * 8;
-        const uint4* sp = reinterpret_cast<const uint4*>(src + (int64_t)row * ld_src + col);
-        buf[u] = kPeer ? __ldcg(sp) : __ldg(sp);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kCopyInFlight; ++u) {
-      const int v = base + u * kCopyThreads + ct;
-      if (v < total) {
-        const int row = v / vpr, col = c0 + (v - row * vpr) * 8;
-        *reinterpret_cast<uint4*>(dst + (int64_t)row * ld_dst + col) = buf[u];
-        if (dst2 != nullptr) *reinterpret_cast<uint4*>(dst2 + (int64_t)row * ld2 + col) = buf[u];
-      }
-    }
-  }
+// Tensor maps of the all-gather kernel: the gathered output, this rank's rows, and every rank's send
+// buffer as a 3-D (K, S, parity) array (index `rank` is this rank's own, used for its stores).
+struct AgMaps {
+  CUtensorMap full;   // (K, M) gathered A, local
+  CUtensorMap local;  // (K, S) this rank's rows, local
+  CUtensorMap send[kMaxWorld];
+};
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
 }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 template <int BN, int STAGES>
 struct AgSmem {
@@ -199,10 +208,20 @@ struct AgSmem {
   static constexpr int kBytes = STAGES * kStageBytes + 1024 + 512 + kMaxOwned * 4;
 };
 
+// Warp roles: 0 TMA producer, 1 MMA issuer, 2..9 epilogue, 10 store warp (kAgWarps = 11).
+//
+// CTA b owns the 128-row blocks b, b + G, ... of the gathered M (every block's rows come from one
+// rank: S is a multiple of 128 when there are peers). The producer visits this CTA's local blocks
+// first, then the remote ones. For every block, the first N tile's K slices of A come by TMA from
+// where the rows live -- this rank's own rows, or the owner's send buffer over NVLink -- and the
+// store warp writes each such slice, once it has landed in shared memory, to the gathered output
+// (and, for local rows, to this rank's send buffer) with TMA stores before it releases the stage;
+// the block's other N tiles re-read A from the gathered output. After the last slice of a local
+// block is stored, the store warp waits for its stores to complete and publishes the block to every
+// peer. The producer waits for a remote block's flag before its first load from the owner.
 template <int BN, bool B_MN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kAgThreads, 1)
-    tp_ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmL,
-                      const __grid_constant__ CUtensorMap tmB, const AgParams P) {
+    tp_ag_gemm_kernel(const __grid_constant__ AgMaps maps, const __grid_constant__ CUtensorMap tmB, const AgParams P) {
   using L = AgSmem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,10 +234,8 @@ __global__ void __launch_bounds__(kAgThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* progress = reinterpret_cast<int*>(tmem_slot + 2);  // K slices of non-local blocks ready, in order
-  int* nseq_slot = reinterpret_cast<int*>(tmem_slot + 3);
-  volatile int* copy_stop = reinterpret_cast<volatile int*>(tmem_slot + 4);
-  int* nlocal_slot = reinterpret_cast<int*>(tmem_slot + 5);
+  int* nseq_slot = reinterpret_cast<int*>(tmem_slot + 2);
+  int* nlocal_slot = reinterpret_cast<int*>(tmem_slot + 3);
   int* seq = reinterpret_cast<int*>(smem + STAGES * L::kStageBytes + 512);  // owned blocks, compute order
 
   const GemmParams& p = P.g;
@@ -228,12 +245,12 @@ __global__ void __launch_bounds__(kAgThreads, 1)
   const int num_k = (p.K + kBK - 1) / kBK;
   const int* ctl = reinterpret_cast<const int*>(pick(P.flags, s.rank)) + kCtl;
   const int epoch = *reinterpret_cast<const volatile int*>(ctl + kCtlAgEpoch) + 1;
-  const int64_t par_off = (epoch & 1) ? P.send_parity_elems : 0;
+  const int par = epoch & 1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], 1);
+      mbar_init(&empty_bar[i], 2);  // the MMA warp's commit and the store warp
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
@@ -241,12 +258,11 @@ __global__ void __launch_bounds__(kAgThreads, 1)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
-    *progress = 0;
-    // Compute order: blocks whose rows are all local first (read straight from A_r), then the rest.
+    *reinterpret_cast<volatile int*>(tmem_slot + 4) = 0;
     int n = 0, nl = 0;
     for (int pass = 0; pass < 2; ++pass)
       for (int mb = blockIdx.x; mb < s.num_blocks; mb += gridDim.x) {
-        const bool local = block_src_lo(s, mb) == s.rank && block_src_hi(s, mb) == s.rank;
+        const bool local = block_src_lo(s, mb) == s.rank;
         if ((pass == 0) == local && n < kMaxOwned) {
           seq[n++] = mb;
           nl += local ? 1 : 0;
@@ -255,8 +271,8 @@ __global__ void __launch_bounds__(kAgThreads, 1)
     *nseq_slot = n;
     *nlocal_slot = nl;
     fence_barrier_init();
-    prefetch_tensormap(&tmA);
-    prefetch_tensormap(&tmL);
+    prefetch_tensormap(&maps.full);
+    prefetch_tensormap(&maps.local);
     prefetch_tensormap(&tmB);
   }
   if (warp == 1) {
@@ -270,74 +286,11 @@ __global__ void __launch_bounds__(kAgThreads, 1)
   const int nseq = *nseq_slot;
   const int nlocal = *nlocal_slot;
   const int num_n = (p.N + BN - 1) / BN;
-  constexpr int kCopyWarp0 = 2 + kEpi;
+  int* my_flags = reinterpret_cast<int*>(pick(P.flags, s.rank));
+  volatile int* stored = reinterpret_cast<volatile int*>(tmem_slot + 4);  // first-N-tile slices stored (store warp)
+  constexpr int kStoreWarp = 2 + kEpi;
 
-  if (warp >= kCopyWarp0) {
-    // ---------------- copy warps
-    const int ct = threadIdx.x - 32 * kCopyWarp0;
-    __nv_bfloat16* my_send = reinterpret_cast<__nv_bfloat16*>(pick(P.send, s.rank)) + par_off;
-    const int row_lo = s.rank * s.S, row_hi = row_lo + s.S;
-    // Phase 1: this rank's rows of every owned block -> send buffer (for the peers) and gathered
-    // output. The tensor cores read local-only blocks straight from A_r, so nothing waits on this.
-    for (int i = 0; i < nseq; ++i) {
-      const int mb = seq[i];
-      const int r0 = max(mb * 128, row_lo), r1 = min(min(mb * 128 + 128, s.M), row_hi);
-      if (r0 < r1)
-        copy_rows<false>(P.a_full + (int64_t)r0 * p.K, p.K,
-                         s.world > 1 ? my_send + (int64_t)(r0 - row_lo) * p.K : nullptr, p.K,
-                         P.a_local + (int64_t)(r0 - row_lo) * p.K, p.K, r1 - r0, 0, p.K, ct);
-    }
-    __threadfence_system();
-    fence_proxy_async_global();
-    named_barrier(1, kCopyThreads);
-    if (ct == 0) {
-      for (int i = 0; i < nseq; ++i) {
-        const int mb = seq[i];
-        if (block_src_lo(s, mb) > s.rank || block_src_hi(s, mb) < s.rank) continue;
-        for (int q = 0; q < s.world; ++q)
-          if (q != s.rank)
-            st_release_sys(reinterpret_cast<int*>(pick(P.flags, q)) + kAgReady + s.rank * kMaxMBlocks + mb, epoch);
-      }
-    }
-    // Phase 2: remote rows of the remaining blocks, in compute order.
-    int done = 0;
-    bool ok = true;
-    const int* my_flags = reinterpret_cast<const int*>(pick(P.flags, s.rank));
-    for (int i = nlocal; i < nseq && ok; ++i) {
-      const int mb = seq[i];
-      const int lo = block_src_lo(s, mb), hi = block_src_hi(s, mb);
-      if (ct < s.world) {
-        const int q = ct;
-        if (q != s.rank && q >= lo && q <= hi &&
-            !wait_flag(my_flags + kAgReady + q * kMaxMBlocks + mb, epoch, P.timeout_ns, abort_flag, p.err,
-                       kErrTpChunkWait))
-          *abort_flag = 1;
-      }
-      // One thread decides for all copy threads (the abort flag may change under their feet).
-      named_barrier(1, kCopyThreads);
-      if (ct == 0) *copy_stop = *abort_flag;
-      named_barrier(1, kCopyThreads);
-      if (*copy_stop) {
-        ok = false;
-        break;
-      }
-      for (int c0 = 0; c0 < p.K; c0 += kCopyCols) {
-        const int ncols = min(kCopyCols, p.K - c0);
-        for (int q = lo; q <= hi; ++q) {
-          if (q == s.rank) continue;
-          const int r0 = max(mb * 128, q * s.S), r1 = min(min(mb * 128 + 128, s.M), (q + 1) * s.S);
-          const __nv_bfloat16* src =
-              reinterpret_cast<const __nv_bfloat16*>(pick(P.send, q)) + par_off + (int64_t)(r0 - q * s.S) * p.K;
-          copy_rows<true>(P.a_full + (int64_t)r0 * p.K, p.K, nullptr, 0, src, p.K, r1 - r0, c0, ncols, ct);
-        }
-        __threadfence();
-        fence_proxy_async_global();
-        named_barrier(1, kCopyThreads);
-        done += (ncols + kBK - 1) / kBK;
-        if (ct == 0) st_release_cta_shared(progress, done);
-      }
-    }
-  } else if (warp == 0) {
+  if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
       int stage = 0;
@@ -346,30 +299,24 @@ __global__ void __launch_bounds__(kAgThreads, 1)
       bool ok = true;
       constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
       for (int i = 0; i < nseq && ok; ++i) {
-        const int m0 = seq[i] * 128;
+        const int mb = seq[i];
+        const int m0 = mb * 128;
+        const int src = block_src_lo(s, mb);
         const bool local = i < nlocal;
+        if (!local) {
+          if (!wait_flag(my_flags + kAgReady + src * kMaxMBlocks + mb, epoch, P.timeout_ns, abort_flag, p.err,
+                         kErrTpChunkWait)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
         for (int nt = 0; nt < num_n && ok; ++nt) {
           const int n0 = nt * BN;
           for (int kb = 0; kb < num_k; ++kb) {
-            if (nt == 0 && !local) {
-              const int need = (i - nlocal) * num_k + kb + 1;
-              if (ld_acquire_cta_shared(progress) < need) {
-                const uint64_t t0 = globaltimer_ns();
-                while (ld_acquire_cta_shared(progress) < need) {
-                  if (*abort_flag) {
-                    ok = false;
-                    break;
-                  }
-                  if (globaltimer_ns() - t0 > P.timeout_ns + MIA_WAIT_LIMIT_NS) {
-                    record_error(p.err, kErrTpChunkWait);
-                    *abort_flag = 1;
-                    ok = false;
-                    break;
-                  }
-                }
-                if (!ok) break;
-              }
-              fence_proxy_async_global();
+            if (!local && nt > 0 && !spin_ge(stored, i * num_k + kb + 1, abort_flag, p.err, kErrTpChunkWait)) {
+              ok = false;
+              break;
             }
             if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
               ok = false;
@@ -379,8 +326,14 @@ __global__ void __launch_bounds__(kAgThreads, 1)
             mbar_arrive_expect_tx(&full_bar[stage], kTx);
             uint8_t* a_dst = smA + stage * kATileBytes;
             uint8_t* b_dst = smB + stage * L::kBTileBytes;
-            if (local) tma_load_2d(a_dst, &tmL, &full_bar[stage], k0, m0 - s.rank * s.S);
-            else tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, m0);
+            if (local) {
+              tma_load_2d(a_dst, &maps.local, &full_bar[stage], k0, m0 - s.rank * s.S);
+            } else if (nt == 0) {
+              tma_load_3d(a_dst, &maps.send[src], &full_bar[stage], k0, m0 - src * s.S, par);
+            } else {
+              fence_proxy_async_global();
+              tma_load_2d(a_dst, &maps.full, &full_bar[stage], k0, m0);
+            }
             if (!B_MN) {
               tma_load_2d(b_dst, &tmB, &full_bar[stage], k0, n0);
             } else {
@@ -456,7 +409,53 @@ __global__ void __launch_bounds__(kAgThreads, 1)
         mbar_wait(drain_bar, 0, nullptr, nullptr, 0);
       }
     }
-  } else {
+  } else if (warp == kStoreWarp) {
+    if (lane == 0) {
+      // ---------------- store warp: first-N-tile A slices -> gathered output (+ send buffer)
+      int stage = 0;
+      uint32_t phase = 0;
+      int done = 0;
+      bool ok = true;
+      for (int i = 0; i < nseq && ok; ++i) {
+        const int mb = seq[i];
+        const int m0 = mb * 128;
+        const bool local = i < nlocal;
+        for (int nt = 0; nt < num_n && ok; ++nt) {
+          for (int kb = 0; kb < num_k; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrTpChunkWait)) {
+              ok = false;
+              break;
+            }
+            if (nt == 0) {
+              const uint8_t* a_src = smA + stage * kATileBytes;
+              tma_store_2d(&maps.full, a_src, kb * kBK, m0);
+              if (local && s.world > 1) tma_store_3d(&maps.send[s.rank], a_src, kb * kBK, m0 - s.rank * s.S, par);
+              bulk_commit();
+              bulk_wait_all();  // written (not only read): the producer may re-read these rows next
+              ++done;
+              asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)stored)), "r"(done)
+                           : "memory");
+            }
+            mbar_arrive(&empty_bar[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (nt == 0 && ok && local && s.world > 1) {
+            // every K slice of this local block is in the send buffer: publish it to the peers
+            fence_proxy_async_global();
+            __threadfence_system();
+            for (int q = 0; q < s.world; ++q)
+              if (q != s.rank)
+                st_release_sys(reinterpret_cast<int*>(pick(P.flags, q)) + kAgReady + s.rank * kMaxMBlocks + mb,
+                               epoch);
+          }
+        }
+      }
+      bulk_wait_all();
+    }
+  } else if (warp >= 2 && warp < 2 + kEpi) {
     // ---------------- epilogue warps 2..9
     const int lane_group = warp % 4;
     const int col_part = (warp - 2) / 4;  // two column halves
@@ -495,7 +494,7 @@ __global__ void __launch_bounds__(kAgThreads, 1)
     tmem_dealloc(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0) {
-    int* wctl = reinterpret_cast<int*>(pick(P.flags, s.rank)) + kCtl;
+    int* wctl = my_flags + kCtl;
     __threadfence();
     if (atomicAdd(wctl + kCtlAgExit, 1) == (int)gridDim.x - 1) {
       wctl[kCtlAgExit] = 0;
@@ -525,25 +524,12 @@ template <int BN, int STAGES>
 struct RsSmem {
   static constexpr int kBTileBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
-  static constexpr int kStagingBytes = 128 * BN * 2;  // one bf16 output tile, 16-byte chunks XOR-swizzled by row
+  // one bf16 output tile, 16-byte chunks XOR-swizzled by row (the staged, 128-column variant only)
+  static constexpr int kStagingBytes = BN == 128 ? 128 * BN * 2 : 0;
   static constexpr int kBytes = STAGES * kStageBytes + kStagingBytes + 1024 + 512 + kMaxOwned * 4 + 256;
 };
 
-// Bounded wait until *counter >= target (shared memory, written by other warps of this CTA).
-__device__ __forceinline__ bool spin_ge(const volatile int* counter, int target, volatile int* abort_flag, int* err,
-                                        int code) {
-  if (*counter >= target) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (*counter < target) {
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > MIA_WAIT_LIMIT_NS) {
-      record_error(err, code);
-      *abort_flag = 1;
-      return false;
-    }
-  }
-  return true;
-}
+
 
 // CTA b owns the 128-row blocks b, b + G, ... and computes every N tile of a block before the next
 // block, so it alone decides when a block's partial rows are complete and publishes them. Blocks
@@ -719,11 +705,11 @@ __global__ void __launch_bounds__(kRsThreads, 1)
     }
   } else {
     // ---------------- epilogue warps: partial rows -> owner's receive slot
-    // Each warp converts its 32 rows x BN / 2 columns to bf16 into the shared staging tile and
-    // releases the accumulator; once all eight warps have staged the tile, warp w stores rows
-    // [16 w, 16 w + 16) out, two rows of BN * 2 contiguous bytes per instruction, so the NVLink
-    // writes go out as whole row segments rather than 16-byte pieces of 32 different rows.
-    static_assert(BN == 128, "the staged reduce-scatter epilogue is written for 128-column tiles");
+    // BN = 128 (staged): each warp converts its 32 rows x 64 columns to bf16 into the shared staging
+    // tile and releases the accumulator; once all eight warps have staged the tile, warp w stores
+    // rows [16 w, 16 w + 16) out, two rows of 256 contiguous bytes per instruction, so NVLink writes
+    // go out as whole row segments. BN = 256 (direct): each thread stores its own row's 64-byte
+    // pieces straight from registers (fewer, wider tiles; better when the stores stay local).
     const int lane_group = warp % 4;
     const int col_part = (warp - 2) / 4;
     const int ew = warp - 2;
@@ -736,9 +722,18 @@ __global__ void __launch_bounds__(kRsThreads, 1)
     bool ok = true;
     for (int i = 0; i < nseq && ok; ++i) {
       const int mb = seq[i];
+      __nv_bfloat16* dst_row = nullptr;  // direct variant: this thread's row in its owner's slot
+      if constexpr (BN != 128) {
+        const int m = mb * 128 + lane_group * 32 + lane;
+        if (m < s.M) {
+          const int owner = m / s.S;
+          dst_row = reinterpret_cast<__nv_bfloat16*>(pick(P.recv, owner)) + par_off + (int64_t)s.rank * slot_elems +
+                    (int64_t)(m - owner * s.S) * s.N;
+        }
+      }
       for (int nt = 0; nt < num_n; ++nt) {
         if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, P.err, kErrGemmEpilogueWait) ||
-            !spin_ge(drained, kEpi * tile_seq, abort_flag, P.err, kErrGemmEpilogueWait)) {
+            (BN == 128 && !spin_ge(drained, kEpi * tile_seq, abort_flag, P.err, kErrGemmEpilogueWait))) {
           ok = false;
           break;
         }
@@ -751,42 +746,61 @@ __global__ void __launch_bounds__(kRsThreads, 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);
           tmem_ld_wait_regs(r);
+          uint4 packed[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = col_part * (kPartCols / 8) + c * 4 + q;
-            staging[row * kChunksPerRow + (chunk ^ (row & 15))] =
-                make_uint4(pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1])),
-                           pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
-                           pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
-                           pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
+          for (int q = 0; q < 4; ++q)
+            packed[q] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1])),
+                                   pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
+                                   pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
+                                   pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
+          if constexpr (BN == 128) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int chunk = col_part * (kPartCols / 8) + c * 4 + q;
+              staging[row * kChunksPerRow + (chunk ^ (row & 15))] = packed[q];
+            }
+          } else {
+            const int n = n0 + col_part * kPartCols + c * 32;
+            if (dst_row != nullptr && n < s.N) {
+              if (n + 32 <= s.N) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(dst_row + n)[q] = packed[q];
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (n + j < s.N) dst_row[n + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+              }
+            }
           }
         }
         tc_fence_before();
         mbar_arrive(&tempty_bar[acc]);  // the MMA may refill this accumulator while we store
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
-        __threadfence_block();
-        __syncwarp();
-        if (lane == 0) atomicAdd(const_cast<int*>(staged), 1);
-        if (!spin_ge(staged, kEpi * (tile_seq + 1), abort_flag, P.err, kErrGemmEpilogueWait)) {
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int tr = 16 * ew + 2 * it + (lane >> 4);
-          const int ch = lane & 15;
-          const int gm = mb * 128 + tr;
-          const int gn = n0 + ch * 8;
-          if (gm < s.M && gn < s.N) {
-            const int owner = gm / s.S;
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(pick(P.recv, owner)) + par_off +
-                                 (int64_t)s.rank * slot_elems + (int64_t)(gm - owner * s.S) * s.N + gn;
-            *reinterpret_cast<uint4*>(dst) = staging[tr * kChunksPerRow + (ch ^ (tr & 15))];
+        if constexpr (BN == 128) {
+          __threadfence_block();
+          __syncwarp();
+          if (lane == 0) atomicAdd(const_cast<int*>(staged), 1);
+          if (!spin_ge(staged, kEpi * (tile_seq + 1), abort_flag, P.err, kErrGemmEpilogueWait)) {
+            ok = false;
+            break;
           }
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int tr = 16 * ew + 2 * it + (lane >> 4);
+            const int ch = lane & 15;
+            const int gm = mb * 128 + tr;
+            const int gn = n0 + ch * 8;
+            if (gm < s.M && gn < s.N) {
+              const int owner = gm / s.S;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(pick(P.recv, owner)) + par_off +
+                                   (int64_t)s.rank * slot_elems + (int64_t)(gm - owner * s.S) * s.N + gn;
+              *reinterpret_cast<uint4*>(dst) = staging[tr * kChunksPerRow + (ch ^ (tr & 15))];
+            }
+          }
+          __syncwarp();
+          if (lane == 0) atomicAdd(const_cast<int*>(drained), 1);
         }
-        __syncwarp();
-        if (lane == 0) atomicAdd(const_cast<int*>(drained), 1);
         ++tile_seq;
       }
       if (!ok) break;
@@ -939,8 +953,8 @@ int64_t flag_bytes() { return (int64_t)kFlagInts * 4; }
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <int BN, bool B_MN, int EPI>
-static void launch_ag(const CUtensorMap& ta, const CUtensorMap& tl, const CUtensorMap& tb, const AgParams& prm,
-                      int grid, cudaStream_t st, int device) {
+static void launch_ag(const AgMaps& maps, const CUtensorMap& tb, const AgParams& prm, int grid, cudaStream_t st,
+                      int device) {
   constexpr int ST = BN == 256 ? 4 : 6;
   using L = AgSmem<BN, ST>;
   auto kern = tp_ag_gemm_kernel<BN, B_MN, ST, EPI>;
@@ -949,15 +963,36 @@ static void launch_ag(const CUtensorMap& ta, const CUtensorMap& tl, const CUtens
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     configured[device] = true;
   }
-  coop_launch(kern, grid, kAgThreads, L::kBytes, st, ta, tl, tb, prm);
+  coop_launch(kern, grid, kAgThreads, L::kBytes, st, maps, tb, prm);
 }
 
 template <int BN, bool B_MN>
-static void dispatch_ag_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tl, const CUtensorMap& tb,
-                            const AgParams& prm, int grid, cudaStream_t st, int device) {
-  if (epi == kEpiGelu) launch_ag<BN, B_MN, kEpiGelu>(ta, tl, tb, prm, grid, st, device);
-  else if (epi == kEpiDGelu) launch_ag<BN, B_MN, kEpiDGelu>(ta, tl, tb, prm, grid, st, device);
-  else launch_ag<BN, B_MN, kEpiPlain>(ta, tl, tb, prm, grid, st, device);
+static void dispatch_ag_epi(int epi, const AgMaps& maps, const CUtensorMap& tb, const AgParams& prm, int grid,
+                            cudaStream_t st, int device) {
+  if (epi == kEpiGelu) launch_ag<BN, B_MN, kEpiGelu>(maps, tb, prm, grid, st, device);
+  else if (epi == kEpiDGelu) launch_ag<BN, B_MN, kEpiDGelu>(maps, tb, prm, grid, st, device);
+  else launch_ag<BN, B_MN, kEpiPlain>(maps, tb, prm, grid, st, device);
+}
+
+// (K, S, 2) bf16 tensor map over a send area: rows of K elements, two parities `parity_bytes` apart.
+static CUtensorMap send_map(int64_t base, int64_t K, int64_t S, int64_t parity_bytes) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr != nullptr, "cuTensorMapEncodeTiled unavailable");
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)S, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)(K * 2), (cuuint64_t)parity_bytes};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, reinterpret_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (send buffer) failed with ", (int)r);
+  return map;
 }
 
 }  // namespace tp
@@ -991,6 +1026,8 @@ void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_f
   TORCH_CHECK(al16(a_local.data_ptr()) && al16(b.data_ptr()) && al16(out.data_ptr()) && al16(a_full.data_ptr()),
               "tp_ag_gemm: 16-byte aligned operands expected");
   TORCH_CHECK(rank >= 0 && rank < world, "tp_ag_gemm: rank out of range");
+  TORCH_CHECK(world == 1 || S % 128 == 0,
+              "tp_ag_gemm: with peers, every rank's row count must be a multiple of 128 (pad the tokens)");
   TORCH_CHECK(act != kActDGelu || aux.has_value(), "tp_ag_gemm: GELU' needs aux");
   c10::cuda::CUDAGuard guard(a_local.device());
   const int device = a_local.get_device();
@@ -1022,10 +1059,6 @@ void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_f
   p.aux = mat(aux);
   p.aux_out = mat(aux_out);
   prm.s = TpShape{(int)M, (int)N, (int)K, (int)S, (int)rank, world, (int)((M + 127) / 128)};
-  prm.a_local = reinterpret_cast<const __nv_bfloat16*>(a_local.data_ptr());
-  prm.a_full = reinterpret_cast<__nv_bfloat16*>(a_full.data_ptr());
-  prm.send = to_peers(send_peers, world, "tp_ag_gemm send");
-  prm.send_parity_elems = send_parity_bytes / 2;
   prm.flags = to_peers(flag_peers, world, "tp_ag_gemm flags");
   prm.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms * 1e6 : 5e9);
 
@@ -1033,15 +1066,18 @@ void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_f
   TORCH_CHECK(prm.s.num_blocks <= (int64_t)grid * kMaxOwned, "tp_ag_gemm: too many row blocks per CTA");
   const int bn = N <= 128 ? 128 : 256;
   const int epi = act == kActGelu ? kEpiGelu : (act == kActDGelu ? kEpiDGelu : kEpiPlain);
-  CUtensorMap ta = make_bf16_map(a_full.data_ptr(), K, M, K, 64, kBM);
-  CUtensorMap tl = make_bf16_map(a_local.data_ptr(), K, S, K, 64, kBM);
+  AgMaps maps{};
+  maps.full = make_bf16_map(a_full.data_ptr(), K, M, K, 64, kBM);
+  maps.local = make_bf16_map(a_local.data_ptr(), K, S, K, 64, kBM);
+  const Peers send = to_peers(send_peers, world, "tp_ag_gemm send");
+  for (int q = 0; q < world; ++q) maps.send[q] = send_map(send.p[q], K, S, send_parity_bytes);
   CUtensorMap tb = b_kmajor ? make_bf16_map(b.data_ptr(), K, N, K, 64, bn) : make_bf16_map(b.data_ptr(), N, K, N, 64, 64);
   if (bn == 256) {
-    if (b_kmajor) dispatch_ag_epi<256, false>(epi, ta, tl, tb, prm, grid, stream, device);
-    else dispatch_ag_epi<256, true>(epi, ta, tl, tb, prm, grid, stream, device);
+    if (b_kmajor) dispatch_ag_epi<256, false>(epi, maps, tb, prm, grid, stream, device);
+    else dispatch_ag_epi<256, true>(epi, maps, tb, prm, grid, stream, device);
   } else {
-    if (b_kmajor) dispatch_ag_epi<128, false>(epi, ta, tl, tb, prm, grid, stream, device);
-    else dispatch_ag_epi<128, true>(epi, ta, tl, tb, prm, grid, stream, device);
+    if (b_kmajor) dispatch_ag_epi<128, false>(epi, maps, tb, prm, grid, stream, device);
+    else dispatch_ag_epi<128, true>(epi, maps, tb, prm, grid, stream, device);
   }
 }
 
@@ -1049,7 +1085,7 @@ namespace tp {
 template <int BN, bool A_MN, bool B_MN>
 static void launch_rs(const CUtensorMap& ta, const CUtensorMap& tb, const RsParams& prm, int grid, cudaStream_t st,
                       int device) {
-  constexpr int ST = 5;
+  constexpr int ST = BN == 128 ? 5 : 4;
   using L = RsSmem<BN, ST>;
   auto kern = tp_gemm_rs_kernel<BN, A_MN, B_MN, ST>;
   static bool configured[64] = {false};
@@ -1116,13 +1152,25 @@ void tp_gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, c10::optional<at::Te
   prm.residual = mat(residual);
   prm.pre_out = mat(pre_out);
   prm.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms * 1e6 : 5e9);
-  const int bn = 128;  // the staged epilogue stores 128-column tiles
+  // 128-column tiles with the shared-memory staged epilogue when partial rows cross NVLink, 256-column
+  // tiles storing straight from registers for one rank (MIA_TP_RS_STAGED=0|1 overrides).
+  static const int staged_env = [] {
+    const char* v = std::getenv("MIA_TP_RS_STAGED");
+    return v == nullptr ? -1 : std::atoi(v);
+  }();
+  const bool staged = staged_env >= 0 ? staged_env != 0 : world > 1;
+  const int bn = staged || N <= 128 ? 128 : 256;
   const int grid = (int)std::min<int64_t>(prm.s.num_blocks, sm_count(device));
   TORCH_CHECK(prm.s.num_blocks <= (int64_t)grid * kMaxOwned, "tp_gemm_rs: too many row blocks per CTA");
   CUtensorMap ta = make_bf16_map(a.data_ptr(), K, M, K, 64, kBM);
   CUtensorMap tb = b_kmajor ? make_bf16_map(b.data_ptr(), K, N, K, 64, bn) : make_bf16_map(b.data_ptr(), N, K, N, 64, 64);
-  if (b_kmajor) launch_rs<128, false, false>(ta, tb, prm, grid, stream, device);
-  else launch_rs<128, false, true>(ta, tb, prm, grid, stream, device);
+  if (bn == 128) {
+    if (b_kmajor) launch_rs<128, false, false>(ta, tb, prm, grid, stream, device);
+    else launch_rs<128, false, true>(ta, tb, prm, grid, stream, device);
+  } else {
+    if (b_kmajor) launch_rs<256, false, false>(ta, tb, prm, grid, stream, device);
+    else launch_rs<256, false, true>(ta, tb, prm, grid, stream, device);
+  }
 }
 
 int64_t tp_flag_bytes() { return tp::flag_bytes(); }

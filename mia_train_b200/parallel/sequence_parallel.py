@@ -2,7 +2,8 @@
 
 Inside a block the residual stream stays sharded by token: rank r of the TP group holds rows
 [r S, (r + 1) S) of the (B * T_pad, C) token matrix (`T_pad` = tokens rounded up to a multiple of
-the TP size; the padding rows never reach attention or the loss). LayerNorms, LayerScale and the
+128 x the TP size, so every rank holds whole 128-row blocks; the padding rows never reach
+attention or the loss). LayerNorms, LayerScale and the
 residual adds run on the shard. The block's four GEMMs are
 
     qkv  = gather(LN1(x)) . Wqkv_r^T           column-parallel, all-gather -> GEMM
@@ -215,7 +216,9 @@ class SequenceParallel:
         return self.comm.group
 
     def padded_tokens(self, t: int) -> int:
-        return -(-t // self.world) * self.world
+        """Tokens rounded up so every rank holds whole 128-row blocks (the fused kernels' unit)."""
+        unit = self.world * 128 if self.world > 1 else 1
+        return -(-t // unit) * unit
 
     def split(self, x: torch.Tensor) -> tuple[torch.Tensor, int]:
         """(B, T, C) replicated -> (this rank's rows of B * T_pad, C), T."""
