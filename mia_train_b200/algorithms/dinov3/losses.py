@@ -37,7 +37,8 @@ def _all_reduce(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
-def _sinkhorn_native(logits: torch.Tensor, temperature: float, n_iterations: int, total: float) -> torch.Tensor:
+def _sinkhorn_native(logits: torch.Tensor, temperature: float, n_iterations: int, total: float,
+                     colsum: torch.Tensor | None = None) -> torch.Tensor:
     """The iterates of `sinkhorn_knopp` as scaling vectors, P[b, k] = E[b, k] r[k] s[b] with
     E = exp(x / T): start r = 1, s = 1 / S0 (S0 = global sum of E); each iteration sets
     r[k] = 1 / (K A[k]) with A[k] = sum_b E[b, k] s[b] (all-reduced, as the reference's row sums)
@@ -50,7 +51,10 @@ def _sinkhorn_native(logits: torch.Tensor, temperature: float, n_iterations: int
     b, k = x.shape
     a = torch.empty(k, device=x.device, dtype=torch.float32)
     t = torch.empty(b, device=x.device, dtype=torch.float32)
-    ext.sinkhorn_colsum(x, float(temperature), None, a)  # sum_b E[b, k]
+    if colsum is not None:  # sum_b E[b, k], already reduced by the prototype GEMM's epilogue
+        a.copy_(colsum)
+    else:
+        ext.sinkhorn_colsum(x, float(temperature), None, a)  # sum_b E[b, k]
     _all_reduce(a)
     s0 = a.sum()
     r = torch.ones(k, device=x.device, dtype=torch.float32)
@@ -70,8 +74,10 @@ def _sinkhorn_native(logits: torch.Tensor, temperature: float, n_iterations: int
 
 
 def sinkhorn_knopp(
-    logits: torch.Tensor, temperature: float, n_iterations: int = 3, batch_size: float | None = None
+    logits: torch.Tensor, temperature: float, n_iterations: int = 3, batch_size: float | None = None,
+    colsum: torch.Tensor | None = None,
 ) -> torch.Tensor:
+    """`colsum` (optional, this rank's sum_b exp(logits / T)) lets the native path skip its first pass."""
     from ...ops._native import use_native
 
     world = _world_size()
@@ -81,7 +87,7 @@ def sinkhorn_knopp(
     # row count (the same on every rank), never from this rank's own, possibly uneven, share.
     if (use_native(logits) and logits.dim() == 2 and total >= 64 * world and logits.shape[1] % 8 == 0
             and logits.dtype in (torch.float32, torch.bfloat16)):
-        return _sinkhorn_native(logits, temperature, n_iterations, total)
+        return _sinkhorn_native(logits, temperature, n_iterations, total, colsum)
     q = torch.exp(logits.float() / temperature).t()  # (K, B_local)
     k = q.shape[0]
     q /= _all_reduce(torch.sum(q))
@@ -100,8 +106,9 @@ class DINOLoss(nn.Module):
         self.out_dim = out_dim
         self.student_temp = student_temp
 
-    def sinkhorn_knopp_teacher(self, teacher_logits: torch.Tensor, teacher_temp: float, n_iterations: int = 3):
-        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations)
+    def sinkhorn_knopp_teacher(self, teacher_logits: torch.Tensor, teacher_temp: float, n_iterations: int = 3,
+                               colsum: torch.Tensor | None = None):
+        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations, colsum=colsum)
 
     def forward(self, student_logits: torch.Tensor, teacher_probs: torch.Tensor, ignore_diagonal: bool = False):
         from ...ops._native import use_native
@@ -146,12 +153,14 @@ class IBOTPatchLoss(nn.Module):
         self.patch_out_dim = patch_out_dim
         self.student_temp = student_temp
 
-    def sinkhorn_knopp_teacher(self, teacher_logits, teacher_temp, n_masked_patches=None, n_iterations=3):
+    def sinkhorn_knopp_teacher(self, teacher_logits, teacher_temp, n_masked_patches=None, n_iterations=3,
+                               colsum=None):
         if n_masked_patches is None:
             n_masked_patches = teacher_logits.shape[0]
         total = torch.tensor(float(n_masked_patches), device=teacher_logits.device, dtype=torch.float32)
         _all_reduce(total)
-        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations, batch_size=float(total.item()))
+        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations, batch_size=float(total.item()),
+                              colsum=colsum)
 
     def forward_masked(self, student_logits, teacher_probs, student_masks_flat, n_masked_patches=None,
                        masks_weight=None):

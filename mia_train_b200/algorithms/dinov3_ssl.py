@@ -177,6 +177,10 @@ class DINOv3(BaseAlgorithm):
         locals_ = [view(self.local_crop_size, self.local_crop_scale) for _ in range(self.n_local_crops)]
         return torch.cat(globals_, dim=0), torch.cat(locals_, dim=0)
 
+    @staticmethod
+    def _colsum_buffer(head: nn.Module, x: torch.Tensor) -> torch.Tensor:
+        return torch.zeros(head.last_layer.weight.shape[0], device=x.device, dtype=torch.float32)
+
     def _step_impl(self, batch: Any, train: bool) -> dict[str, torch.Tensor]:
         backbone = self.student["backbone"]
         volumes = backbone.prepare_input(batch[self.input_key], self.input_axes)
@@ -188,12 +192,19 @@ class DINOv3(BaseAlgorithm):
         n_masked = int(masks.sum().item())
         with torch.no_grad():
             t_out = self.teacher["backbone"].forward_features(global_views)
-            t_cls_logits = self.teacher["dino_head"](t_out["x_norm_clstoken"])
-            t_cls_probs = self.dino_loss.sinkhorn_knopp_teacher(t_cls_logits, temp).unflatten(0, (2, b))
+            # on CUDA the prototype GEMMs also produce Sinkhorn's first column sums in their epilogue
+            fused = t_out["x_norm_clstoken"].is_cuda
+            cls_sum = self._colsum_buffer(self.teacher["dino_head"], t_out["x_norm_clstoken"]) if fused else None
+            t_cls_logits = self.teacher["dino_head"](t_out["x_norm_clstoken"], cls_sum, temp) if fused else \
+                self.teacher["dino_head"](t_out["x_norm_clstoken"])
+            t_cls_probs = self.dino_loss.sinkhorn_knopp_teacher(t_cls_logits, temp, colsum=cls_sum).unflatten(0, (2, b))
             if n_masked > 0:
                 masked_teacher = t_out["x_norm_patchtokens"].flatten(0, 1)[masks.flatten()]
+                patch_sum = self._colsum_buffer(self.teacher["ibot_head"], masked_teacher) if fused else None
+                patch_logits = self.teacher["ibot_head"](masked_teacher, patch_sum, temp) if fused else \
+                    self.teacher["ibot_head"](masked_teacher)
                 t_patch_probs = self.ibot_loss.sinkhorn_knopp_teacher(
-                    self.teacher["ibot_head"](masked_teacher), temp, n_masked_patches=n_masked
+                    patch_logits, temp, n_masked_patches=n_masked, colsum=patch_sum
                 )
         s_global, s_local = backbone.forward_features([global_views, local_views], [masks, None])
         head = self.student["dino_head"]

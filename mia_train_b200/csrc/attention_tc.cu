@@ -42,7 +42,7 @@ namespace {
 typedef __nv_bfloat16 bf16;
 constexpr int kTcBM = 128;  // queries per forward CTA
 constexpr int kTcBN = 128;  // keys per forward block
-constexpr int kTcSoftmaxThreads = 128;
+constexpr int kTcSoftmaxThreads = 256;  // two warps per TMEM lane quarter, one per half of the keys
 constexpr int kTcThreads = 64 + kTcSoftmaxThreads;
 constexpr int kBwdSoftmaxThreads = 256;  // two warps per TMEM lane quarter, one per half of the columns
 constexpr int kBwdThreads = 64 + kBwdSoftmaxThreads;
@@ -58,8 +58,9 @@ struct TcFwdSmem {
   static constexpr int kK = kQ + kQBytes;       // [2]
   static constexpr int kV = kK + 2 * kKVBytes;  // [1]
   static constexpr int kP = kV + kKVBytes;
-  static constexpr int kBar = kP + kPBytes;
-  static constexpr int kBytes = kBar + 128 + 1024;  // barriers, TMEM slot, abort flag; alignment slack
+  static constexpr int kStat = kP + kPBytes;  // (m, l) of both key halves per query row, merged at the end
+  static constexpr int kBar = kStat + 4 * kTcBM * 4;
+  static constexpr int kBytes = kBar + 128 + 1024;  // barriers, TMEM slot, abort flag, merge counter; slack
 };
 
 // All lanes of a warp agree on a bounded wait, so `.sync.aligned` TMEM loads stay warp-uniform.
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     mbar_init(p_full, kTcSoftmaxThreads);
     mbar_init(drain, 1);
     *abort_flag = 0;
+    tmem_slot[2] = 0;  // softmax warps done (merge counter)
     fence_barrier_init();
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_s = tmem;
-  const uint32_t t_o = tmem + kTcBN;
+  const uint32_t t_o = tmem + kTcBN;  // O of keys 0..63 of every block; O of keys 64..127 at t_o + D
 
   if (warp == 0) {
     if (lane == 0) {
@@ -222,9 +224,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         for (int kk = 0; kk < kTcBN / 16; ++kk) {
           // A = P (128 x 128 keys, K-major, two 64-key column blocks of 16 KB); B = V (keys x D,
           // D contiguous: MN-major, 16 keys = 16 rows per step).
-          tc_mma_f16(t_o, make_sdesc_sw<128>(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+          // keys 0..63 of the block accumulate into O_0, keys 64..127 into O_1 (each half of the
+          // softmax warps keeps its own running maximum and sum; they are merged at the end)
+          const uint32_t t_dst = t_o + (kk >> 2) * D;
+          tc_mma_f16(t_dst, make_sdesc_sw<128>(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                      make_sdesc_sw<L::kRowBytes>(v_addr + kk * 16 * L::kRowBytes, L::kKVBytes, kSbo), idesc_o,
-                     (j > 0 || kk > 0) ? 1u : 0u);
+                     (j > 0 || (kk & 3) > 0) ? 1u : 0u);
         }
         tc_commit(v_empty);
         tc_commit(o_full);
@@ -236,16 +241,21 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
   } else {
     // -------------------------------------------------------------------- softmax warps
-    // O accumulates in TMEM over all key blocks (the PV MMAs accumulate), relative to a reference
-    // row maximum m_ref. P_j = exp2(s - m_ref) is used as long as the block's maximum stays within
-    // kRescale (log2 units) of m_ref, so P <= 2^kRescale; past that, the row's O (once the previous
-    // PV MMA has landed) and l are scaled by exp2(m_ref_old - m_ref_new) in TMEM and m_ref moves.
-    // After the first blocks this is rare, so most blocks do no O traffic at all.
+    // Warps 2..9: lane quarter lg = warp & 3, key half `half` = (warp - 2) / 4 (keys 64 * half ..
+    // +63 of every block). The two halves of a row are two independent online softmaxes over
+    // disjoint keys, each with its own O accumulator in TMEM (O_half), reference maximum and sum;
+    // they are merged once at the end. O accumulates over all key blocks (the PV MMAs accumulate),
+    // relative to the reference maximum m_ref: P = exp2(s - m_ref) is used as long as a block's
+    // maximum stays within kRescale (log2 units) of m_ref, so P <= 2^kRescale; past that the half's
+    // O (once the previous PV MMA has landed) and l are scaled by exp2(m_old - m_new) in TMEM.
     constexpr float kRescale = 8.f;
     const int lg = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;
     const int r = lg * 32 + lane;
     const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
+    const uint32_t t_oh = t_o + half * D;
     uint8_t* P = smem + L::kP;
+    float* stat = reinterpret_cast<float*>(smem + L::kStat);  // [2][2][128]: (m, l) of each half
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nb; ++j) {
@@ -254,35 +264,35 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         break;
       }
       tc_fence_after();
-      const int kbase = j * kTcBN;
+      const int kbase = j * kTcBN + half * 64;
       // Full key blocks skip the per-element key mask (only the last block can be ragged).
       auto softmax_block = [&](auto full_tag) -> bool {
         constexpr bool kFull = decltype(full_tag)::value;
         float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kTcBN / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
+          tmem_ld_32x32b_x32(t_s + lane_off + half * 64 + c * 32, v);
           tmem_ld_wait_regs(v);
 #pragma unroll
           for (int e = 0; e < 32; ++e)
             if (kFull || kbase + c * 32 + e < Nk) mx = fmaxf(mx, __uint_as_float(v[e]));
         }
         const float blk = mx * scale_log2;
-        const bool move = blk > m + kRescale;  // always true for the first block (m = -inf)
-        if (__any_sync(0xffffffffu, move) && j > 0) {
-          // rescale O (all PV MMAs so far have landed once o_full of block j - 1 completes)
+        const bool move = blk > m + kRescale;  // always true for the first block with a key (m = -inf)
+        if (__any_sync(0xffffffffu, move && m != -INFINITY)) {
+          // rescale this half's O: every PV MMA issued so far has landed once o_full of block j - 1 completes
           if (!warp_wait(o_full, (j - 1) & 1, abort_flag, err)) return false;
           tc_fence_after();
-          const float alpha = move ? fast_exp2f(m - blk) : 1.f;
+          const float alpha = (move && m != -INFINITY) ? fast_exp2f(m - blk) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(t_oh + lane_off + c * 16, v);
+            tmem_ld_wait_regs16(v);
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(t_o + lane_off + c * 32, v);
-            tmem_ld_wait_regs(v);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st_32x32b_x32(t_o + lane_off + c * 32, v);
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st_32x32b_x16(t_oh + lane_off + c * 16, v);
           }
           tmem_st_wait();
           l *= alpha;
@@ -290,9 +300,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         if (move) m = blk;
         float rs = 0.f;
 #pragma unroll
-        for (int c = 0; c < kTcBN / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
+          tmem_ld_32x32b_x32(t_s + lane_off + half * 64 + c * 32, v);
           tmem_ld_wait_regs(v);
           uint32_t pk[16];
 #pragma unroll
@@ -307,15 +317,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           }
 #pragma unroll
           for (int qd = 0; qd < 4; ++qd) {
-            const int ci = (c & 1) * 4 + qd;  // 16-byte chunk within the 128-byte row of this key block
-            uint4* dst = reinterpret_cast<uint4*>(P + (c >> 1) * 16384 + r * 128 + ((ci ^ (r & 7)) << 4));
+            const int ci = c * 4 + qd;  // 16-byte chunk within the 128-byte row of this half's key block
+            uint4* dst = reinterpret_cast<uint4*>(P + half * 16384 + r * 128 + ((ci ^ (r & 7)) << 4));
             *dst = make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
           }
         }
         l += rs;
         return true;
       };
-      const bool done = (kbase + kTcBN <= Nk) ? softmax_block(std::true_type{}) : softmax_block(std::false_type{});
+      // A half whose keys all lie past Nk (a ragged last block) still writes its zero P.
+      const bool done =
+          (j * kTcBN + kTcBN <= Nk) ? softmax_block(std::true_type{}) : softmax_block(std::false_type{});
       if (!done) {
         ok = false;
         break;
@@ -325,27 +337,56 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       mbar_arrive(p_full);
     }
     if (ok && nb > 0 && !warp_wait(o_full, (nb - 1) & 1, abort_flag, err)) ok = false;
+    // merge the two halves: each publishes (m, l) of its rows, then writes half of the output columns
+    if (ok) {
+      stat[(half * 2 + 0) * 128 + r] = m;
+      stat[(half * 2 + 1) * 128 + r] = l;
+    }
+    __threadfence_block();
+    __syncwarp();
+    if (lane == 0) atomicAdd(reinterpret_cast<int*>(tmem_slot + 2), ok ? 1 : 1000);
+    {
+      const uint64_t t0 = globaltimer_ns();
+      volatile int* cnt = reinterpret_cast<volatile int*>(tmem_slot + 2);
+      while (*cnt < kTcSoftmaxThreads / 32) {
+        if (*abort_flag || globaltimer_ns() - t0 > MIA_WAIT_LIMIT_NS) {
+          ok = false;
+          break;
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok && *cnt < 1000);
+    }
     const int qi = q0 + r;
     if (ok && nb > 0) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      bf16* orow = o + (((size_t)b * Nq + (qi < Nq ? qi : 0)) * H + h) * D;
+      const float m0 = stat[0 * 128 + r], l0 = stat[1 * 128 + r];
+      const float m1 = stat[2 * 128 + r], l1 = stat[3 * 128 + r];
+      const float mm = fmaxf(m0, m1);
+      const float w0 = m0 == -INFINITY ? 0.f : fast_exp2f(m0 - mm);
+      const float w1 = m1 == -INFINITY ? 0.f : fast_exp2f(m1 - mm);
+      const float lt = l0 * w0 + l1 * w1;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      const float a0 = w0 * inv, a1 = w1 * inv;
+      bf16* orow = o + (((size_t)b * Nq + (qi < Nq ? qi : 0)) * H + h) * D + half * (D / 2);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_o + lane_off + c * 32, v);  // warp-wide: every lane takes part
-        tmem_ld_wait_regs(v);
+      for (int c = 0; c < D / 32; ++c) {  // this half's D / 2 output columns, 16 at a time
+        uint32_t v0[16], v1[16];
+        tmem_ld_32x32b_x16(t_o + lane_off + half * (D / 2) + c * 16, v0);
+        tmem_ld_32x32b_x16(t_o + D + lane_off + half * (D / 2) + c * 16, v1);
+        tmem_ld_wait_regs16(v0);
+        tmem_ld_wait_regs16(v1);
         if (qi < Nq) {
 #pragma unroll
-          for (int d = 0; d < 32; d += 8)
-            *reinterpret_cast<uint4*>(orow + c * 32 + d) = make_uint4(
-                pack_bf16x2(__uint_as_float(v[d]) * inv, __uint_as_float(v[d + 1]) * inv),
-                pack_bf16x2(__uint_as_float(v[d + 2]) * inv, __uint_as_float(v[d + 3]) * inv),
-                pack_bf16x2(__uint_as_float(v[d + 4]) * inv, __uint_as_float(v[d + 5]) * inv),
-                pack_bf16x2(__uint_as_float(v[d + 6]) * inv, __uint_as_float(v[d + 7]) * inv));
+          for (int d = 0; d < 16; d += 8) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v0[d + e]) * a0 + __uint_as_float(v1[d + e]) * a1;
+            *reinterpret_cast<uint4*>(orow + c * 16 + d) = make_uint4(
+                pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+          }
         }
       }
-      if (qi < Nq) lse[(size_t)bh * Nq + qi] = m + log2f(fmaxf(l, 1e-30f));
+      if (qi < Nq && half == 0) lse[(size_t)bh * Nq + qi] = mm + log2f(fmaxf(lt, 1e-30f));
     }
   }
   tc_fence_before();

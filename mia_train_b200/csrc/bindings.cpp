@@ -6,7 +6,9 @@
 namespace mia {
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> gamma,
-          c10::optional<torch::Tensor> aux_out, bool a_kmajor, bool b_kmajor, int64_t act, bool accumulate);
+          c10::optional<torch::Tensor> aux_out, bool a_kmajor, bool b_kmajor, int64_t act, bool accumulate,
+          c10::optional<torch::Tensor> colsum, double colsum_scale, c10::optional<torch::Tensor> a2,
+          c10::optional<torch::Tensor> b2);
 void column_sum(torch::Tensor x, torch::Tensor out, bool accumulate);
 int64_t set_gemm_pair_mode(int64_t mode);
 void zscore_u8(torch::Tensor x, torch::Tensor out);
@@ -93,7 +95,10 @@ void axial_angles_bwd(at::Tensor dangles, at::Tensor coords, std::vector<at::Ten
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mia_train_b200 sm_100a kernels";
-  m.def("gemm", &mia::gemm, "tcgen05 bf16 GEMM with fused epilogue");
+  m.def("gemm", &mia::gemm, "tcgen05 bf16 GEMM with fused epilogue", py::arg("a"), py::arg("b"), py::arg("d"),
+        py::arg("bias"), py::arg("residual"), py::arg("aux"), py::arg("gamma"), py::arg("aux_out"), py::arg("a_kmajor"),
+        py::arg("b_kmajor"), py::arg("act"), py::arg("accumulate"), py::arg("colsum") = py::none(),
+        py::arg("colsum_scale") = 1.0, py::arg("a2") = py::none(), py::arg("b2") = py::none());
   m.def("column_sum", &mia::column_sum);
   m.def("layernorm_fwd", &mia::layernorm_fwd);
   m.def("layernorm_bwd", &mia::layernorm_bwd, "LayerNorm / RMSNorm backward; dres (optional) is added to dX",

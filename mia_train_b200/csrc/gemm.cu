@@ -38,6 +38,7 @@ namespace mia {
 template <int BN, bool A_MN, bool B_MN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                         const GemmParams p) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -119,6 +120,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
+        if constexpr (!A_MN && !B_MN) {
+          const int num_k2 = (p.K2 + kBK - 1) / kBK;
+          for (int kb = 0; kb < num_k2 && ok; ++kb) {  // the second operand pair, same accumulator
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrGemmProducerWait)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full_bar[stage], kTx);
+            tma_load_2d(smA + stage * kATileBytes, &tmA2, &full_bar[stage], kb * kBK, m0);
+            tma_load_2d(smB + stage * L::kBTileBytes, &tmB2, &full_bar[stage], kb * kBK, n0);
+            ++issued;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
       }
       if (!ok) {
         // Let the copies already in flight land before this CTA's shared memory goes away.
@@ -173,6 +191,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
+        if constexpr (!A_MN && !B_MN) {
+          const int num_k2 = (p.K2 + kBK - 1) / kBK;
+          for (int kb = 0; kb < num_k2 && ok; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrGemmMmaWait)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(smA + stage * kATileBytes);
+            const uint32_t b_base = smem_u32(smB + stage * L::kBTileBytes);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k)
+              tc_mma_f16(d_tmem, make_sdesc_sw128(a_base + k * 32, 16, 1024), make_sdesc_sw128(b_base + k * 32, 16, 1024),
+                         idesc, 1u);
+            tc_commit(&empty_bar[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
         if (!ok) break;
         tc_commit(&tfull_bar[acc]);
         acc ^= 1;
@@ -206,6 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait_regs(r);
         epilogue_chunk<kEpiAll>(p, m, n0 + c * 32, r);
+        if (p.colsum != nullptr) colsum_exp_chunk(p, m, n0 + c * 32, r, lane);
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -498,7 +538,8 @@ static int num_sms(int device) {
 }
 
 template <int BN, bool A_MN, bool B_MN, int STAGES>
-static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, int device, cudaStream_t stream) {
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2, const CUtensorMap& tb2,
+                        GemmParams& p, int device, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, STAGES>;
   static bool configured[64] = {false};
@@ -516,18 +557,18 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams
   if (p.splits > 1 && !p.accumulate)
     C10_CUDA_CHECK(cudaMemsetAsync(p.D, 0, (size_t)p.M * p.N * sizeof(float), stream));
   const int grid = std::min(p.num_tiles, num_sms(device));
-  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, ta2, tb2, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int BN>
-static void dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
-                            int device, cudaStream_t s) {
+static void dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
+                            const CUtensorMap& tb2, GemmParams& p, int device, cudaStream_t s) {
   constexpr int ST = BN == 256 ? 4 : 6;
-  if (!a_mn && !b_mn) launch_gemm<BN, false, false, ST>(ta, tb, p, device, s);
-  else if (!a_mn && b_mn) launch_gemm<BN, false, true, ST>(ta, tb, p, device, s);
-  else if (a_mn && !b_mn) launch_gemm<BN, true, false, ST>(ta, tb, p, device, s);
-  else launch_gemm<BN, true, true, ST>(ta, tb, p, device, s);
+  if (!a_mn && !b_mn) launch_gemm<BN, false, false, ST>(ta, tb, ta2, tb2, p, device, s);
+  else if (!a_mn && b_mn) launch_gemm<BN, false, true, ST>(ta, tb, ta2, tb2, p, device, s);
+  else if (a_mn && !b_mn) launch_gemm<BN, true, false, ST>(ta, tb, ta2, tb2, p, device, s);
+  else launch_gemm<BN, true, true, ST>(ta, tb, ta2, tb2, p, device, s);
 }
 
 template <int BN, bool A_MN, bool B_MN, int STAGES, int EPI>
@@ -621,7 +662,9 @@ static int choose_bn_pair(int M, int N, int sms) {
 
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> gamma,
-          c10::optional<torch::Tensor> aux_out, bool a_kmajor, bool b_kmajor, int64_t act, bool accumulate) {
+          c10::optional<torch::Tensor> aux_out, bool a_kmajor, bool b_kmajor, int64_t act, bool accumulate,
+          c10::optional<torch::Tensor> colsum, double colsum_scale, c10::optional<torch::Tensor> a2,
+          c10::optional<torch::Tensor> b2) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && d.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && d.dim() == 2, "gemm: 2-D tensors expected");
@@ -674,6 +717,13 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   p.aux = check_mat(aux, "aux");
   p.aux_out = check_mat(aux_out, "aux_out");
   TORCH_CHECK(act != kActDGelu || p.aux != nullptr, "gemm: GELU' needs aux");
+  if (colsum.has_value()) {
+    TORCH_CHECK(colsum->is_cuda() && colsum->scalar_type() == at::kFloat && colsum->is_contiguous() &&
+                    colsum->numel() == N,
+                "gemm: colsum must be a contiguous fp32 vector of length N");
+    p.colsum = colsum->data_ptr<float>();
+    p.colsum_scale = (float)colsum_scale;
+  }
 
   // The CTA-pair kernels carry the activation epilogues only in the layouts the MLP uses: GELU with
   // both operands K-major (fc1 forward), GELU' with B N-major (dX of fc1). Other activated calls
@@ -690,6 +740,18 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   if (epi != kEpiPlain &&
       (d.scalar_type() == at::kFloat || gamma.has_value() || residual.has_value() || accumulate))
     pair_ok = false;
+  if (a2.has_value() != b2.has_value()) TORCH_CHECK(false, "gemm: a2 and b2 come together");
+  if (a2.has_value()) {
+    TORCH_CHECK(a_kmajor && b_kmajor, "gemm: the second operand pair needs K-major A and B");
+    TORCH_CHECK(a2->scalar_type() == at::kBFloat16 && b2->scalar_type() == at::kBFloat16 && a2->dim() == 2 &&
+                    b2->dim() == 2 && a2->stride(1) == 1 && b2->stride(1) == 1 && a2->size(0) == M &&
+                    b2->size(0) == N && a2->size(1) == b2->size(1) && a2->size(1) % 8 == 0 &&
+                    a2->stride(0) % 8 == 0 && b2->stride(0) % 8 == 0 && aligned16(a2->data_ptr()) &&
+                    aligned16(b2->data_ptr()),
+                "gemm: a2 (M, K2) and b2 (N, K2) must be row-major bf16 with K2 % 8 == 0");
+    p.K2 = (int)a2->size(1);
+  }
+  if (p.colsum != nullptr || p.K2 > 0) pair_ok = false;  // column sums and K2 live in the single-CTA kernel
   const bool use_pair = pair_mode() != 0 && M >= 256 && pair_ok;
   int bn = use_pair ? choose_bn_pair((int)M, (int)N, num_sms(device)) : choose_bn((int)M, (int)N, num_sms(device));
   static const bool bn_pinned = std::getenv("MIA_GEMM_BN") != nullptr;
@@ -707,7 +769,7 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   // sum (the weight-gradient GEMMs: tokens are K, the output is a small fp32 matrix).
   p.splits = 1;
   const bool plain_fp32 = p.d_fp32 && !p.bias && !p.gamma && !p.residual && !p.aux && !p.aux_out && act == kActNone;
-  if (plain_fp32) {
+  if (plain_fp32 && p.colsum == nullptr && p.K2 == 0) {
     const long tiles = use_pair ? (long)((M + 255) / 256) * ((N + bn - 1) / bn)
                                 : (long)((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
     const int sms = use_pair ? num_sms(device) / 2 : num_sms(device);
@@ -721,13 +783,18 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
                             : make_map(a.data_ptr(), M, K, a.stride(0), 64, 64);
   CUtensorMap tb = b_kmajor ? make_map(b.data_ptr(), K, N, b.stride(0), 64, b_rows)
                             : make_map(b.data_ptr(), N, K, b.stride(0), 64, 64);
+  CUtensorMap ta2 = ta, tb2 = tb;  // unused unless a second operand pair is given
+  if (p.K2 > 0) {
+    ta2 = make_map(a2->data_ptr(), p.K2, M, a2->stride(0), 64, kBM);
+    tb2 = make_map(b2->data_ptr(), p.K2, N, b2->stride(0), 64, b_rows);
+  }
   if (use_pair) {
     if (bn == 256) dispatch_majors_pair<256>(!a_kmajor, !b_kmajor, epi, ta, tb, p, device, stream);
     else dispatch_majors_pair<128>(!a_kmajor, !b_kmajor, epi, ta, tb, p, device, stream);
   } else if (bn == 256) {
-    dispatch_majors<256>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+    dispatch_majors<256>(!a_kmajor, !b_kmajor, ta, tb, ta2, tb2, p, device, stream);
   } else {
-    dispatch_majors<128>(!a_kmajor, !b_kmajor, ta, tb, p, device, stream);
+    dispatch_majors<128>(!a_kmajor, !b_kmajor, ta, tb, ta2, tb2, p, device, stream);
   }
 }
 

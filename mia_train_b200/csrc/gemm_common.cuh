@@ -37,7 +37,37 @@ struct GemmParams {
   int splits;      // split-K factor (> 1: partial sums added atomically into an fp32 output)
   int k_blocks_per_split;
   int* err;
+  // Optional column sums of exp(acc * colsum_scale) over the tile rows, atomically added into
+  // colsum[N] (single-CTA kernel only): the first column reduction of Sinkhorn-Knopp centring,
+  // computed while the prototype logits are still in TMEM.
+  float* colsum;
+  float colsum_scale;
+  // Optional second operand pair (single-CTA kernel, both K-major): the K loop continues over
+  // K2 more columns of A2 (M x K2) and B2 (N x K2) into the same accumulator, so
+  // D = epi(A B^T + A2 B2^T) -- a low-rank (LoRA) delta added inside the base GEMM's TMEM tile.
+  int K2;
 };
+
+// Adds sum over the warp's 32 rows of exp(v * scale) for the chunk's 32 columns into colsum[n ..
+// n + 31]: a 31-shuffle reduce-scatter across the warp leaves column j's sum in lane j (rows past M
+// and columns past N contribute 0). All 32 lanes must call it.
+__device__ __forceinline__ void colsum_exp_chunk(const GemmParams& p, int m, int n, const uint32_t (&r)[32], int lane) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    v[j] = (m < p.M && n + j < p.N) ? __expf(__uint_as_float(r[j]) * p.colsum_scale) : 0.f;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float keep = upper ? v[i + off] : v[i];
+      const float send = upper ? v[i] : v[i + off];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  if (n + lane < p.N) atomicAdd(p.colsum + n + lane, v[0]);
+}
 
 // Tile index -> (m tile, n tile, K-split); m fastest so concurrently running CTAs share B tiles.
 struct TileCoord {

@@ -100,6 +100,13 @@ def apply_linear(
 
         return tp_linear(module, x, activation=activation, residual=residual, gamma=gamma)
     if isinstance(module, LoRAMixin):
+        if gamma is None:
+            from ...ops.linear import lora_linear
+
+            fused = lora_linear(x, module.weight, module.bias, module.lora_a, module.lora_b,
+                                float(module.lora_scaling), activation=activation, residual=residual)
+            if fused is not None:
+                return fused
         y = linear(x, module.weight, module.bias)
         y = y + module.lora_forward(x).to(y.dtype)
         if activation == "gelu":

@@ -52,11 +52,28 @@ class DINOHead(nn.Module):
                 i += 1
         return x
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, exp_colsum: torch.Tensor | None = None, temperature: float | None = None):
+        """Prototype logits. With `exp_colsum` (fp32, n_prototypes; no autograd -- the teacher's use)
+        the prototype GEMM also adds sum_b exp(logit[b, k] / temperature) into it from its epilogue:
+        the first column reduction of Sinkhorn-Knopp centring, without another pass over the logits."""
         x = self.forward_mlp(x)
         eps = 1e-6 if x.dtype == torch.float16 else 1e-12
         x = F.normalize(x, dim=-1, p=2, eps=eps)
-        return linear(x, self.last_layer.weight)
+        if exp_colsum is None:
+            return linear(x, self.last_layer.weight)
+        from ...ops._native import use_native
+        from ...ops.linear import compute_dtype, gemm
+
+        cdtype = compute_dtype(x)
+        w = self.last_layer.weight
+        if cdtype == torch.bfloat16 and use_native(x) and x.shape[-1] % 8 == 0 and w.shape[0] % 8 == 0:
+            x2 = x.reshape(-1, x.shape[-1]).to(cdtype).contiguous()
+            out = gemm(x2, w.to(cdtype).contiguous(), out_dtype=torch.float32, colsum=exp_colsum,
+                       colsum_scale=1.0 / float(temperature))
+            return out.reshape(*x.shape[:-1], w.shape[0])
+        logits = linear(x, w)
+        exp_colsum.add_(torch.exp(logits.float().reshape(-1, w.shape[0]) / float(temperature)).sum(0))
+        return logits
 
 
 def _init_weights(module: nn.Module) -> None:

@@ -69,13 +69,20 @@ def gemm(
     act: int = ACT_NONE,
     accumulate: bool = False,
     aux_out: torch.Tensor | None = None,
+    colsum: torch.Tensor | None = None,
+    colsum_scale: float = 1.0,
+    a2: torch.Tensor | None = None,
+    b2: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """D[M, N] = sum_k A[m, k] B[n, k] with epilogue; operands given in their physical layout.
 
     `a` is (M, K) when `a_kmajor` else (K, M); `b` is (N, K) when `b_kmajor` else (K, N).
     Epilogue order: acc (+ bias[n]) -> act -> (* gamma[n]) -> (+ residual[m, n]) -> (+ out if
     accumulate). `act=ACT_GELU` writes the pre-activation to `aux_out` when given;
-    `act=ACT_DGELU` multiplies by gelu'(aux[m, n]).
+    `act=ACT_DGELU` multiplies by gelu'(aux[m, n]). `colsum` (fp32, N) receives
+    `+= sum_m exp(acc[m, n] * colsum_scale)` computed from the accumulator in the same epilogue.
+    `a2` (M, K2) and `b2` (N, K2), both K-major, add `a2 @ b2.T` to the accumulator before the
+    epilogue (the K loop continues over them).
     """
     m = a.shape[0] if a_kmajor else a.shape[1]
     n = b.shape[0] if b_kmajor else b.shape[1]
@@ -87,11 +94,14 @@ def gemm(
     if out is None:
         out = torch.empty((m, n), device=a.device, dtype=out_dtype)
     if use_native(a):
-        native().gemm(a, b, out, bias, residual, aux, gamma, aux_out, a_kmajor, b_kmajor, act, accumulate)
+        native().gemm(a, b, out, bias, residual, aux, gamma, aux_out, a_kmajor, b_kmajor, act, accumulate, colsum,
+                      float(colsum_scale), a2, b2)
         return out
     am = a if a_kmajor else a.t()
     bm = b if b_kmajor else b.t()
     acc = am.float() @ bm.float().t()
+    if a2 is not None:
+        acc = acc + a2.float() @ b2.float().t()
     if bias is not None:
         acc = acc + bias.float()
     if act == ACT_GELU:
@@ -106,6 +116,8 @@ def gemm(
         acc = acc + residual.float()
     if accumulate:
         acc = acc + out.float()
+    if colsum is not None:
+        colsum.add_(torch.exp(acc * colsum_scale).sum(0))
     out.copy_(acc)
     return out
 
@@ -212,3 +224,85 @@ def linear(
     if residual is not None:
         y = residual + y
     return y
+
+
+class _NativeLoRALinear(torch.autograd.Function):
+    """`act(x W^T + b + s (x A^T) B^T)` with the low-rank delta accumulated into the base GEMM's tile.
+
+    Forward: h = x A^T (rank r), then one GEMM whose K loop runs over x / W and then over h / (s B)
+    into the same tensor-memory accumulator, with bias and GELU in the epilogue. Backward:
+    dZ = dY (* gelu'), t = dZ (s B); dX = dZ W + t A (the second GEMM accumulates into dX),
+    dA = t^T x, dB = s dZ^T h, dW = dZ^T x (when the base weight trains), db = column sums of dZ.
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, lora_a, lora_b, scaling, residual, act, cdtype):  # type: ignore[override]
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(cdtype).contiguous()
+        w = compute_weight(weight, cdtype).contiguous()
+        a = lora_a.to(cdtype).contiguous()
+        s = float(scaling)
+        bs = (lora_b.float() * s).to(cdtype).contiguous()
+        h = gemm(x2, a, out_dtype=cdtype)
+        res2 = residual.reshape(-1, w.shape[0]).to(cdtype).contiguous() if residual is not None else None
+        pre = torch.empty((x2.shape[0], w.shape[0]), device=x.device, dtype=cdtype) if act == ACT_GELU else None
+        bf = bias.float().contiguous() if bias is not None else None
+        y = gemm(x2, w, out_dtype=cdtype, bias=bf, act=act, aux_out=pre, residual=res2, a2=h, b2=bs)
+        ctx.save_for_backward(x2, w, a, bs, h, pre)
+        ctx.meta = (shape, act, bias is not None, residual is not None, s, weight.dtype, lora_a.dtype, lora_b.dtype,
+                    bias.dtype if bias is not None else None)
+        ctx.sinks = (grad_sink(weight), grad_sink(bias))
+        return y.reshape(*shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):  # type: ignore[override]
+        x2, w, a, bs, h, pre = ctx.saved_tensors
+        shape, act, has_b, has_res, s, wdt, adt, bdt, biasdt = ctx.meta
+        n = w.shape[0]
+        dz = dy.reshape(-1, n).to(x2.dtype).contiguous()
+        if act == ACT_GELU:
+            dz = (dz.float() * gelu_grad_reference(pre)).to(x2.dtype).contiguous()
+        t = gemm(dz, bs, b_kmajor=False, out_dtype=x2.dtype)  # (M, r) = dZ (s B)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(dz, w, b_kmajor=False, out_dtype=x2.dtype)
+            gemm(t, a, b_kmajor=False, out=dx, accumulate=True)
+            dx = dx.reshape(shape)
+        da = gemm(t, x2, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32).to(adt)
+        db_lora = (gemm(dz, h, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32) * s).to(bdt)
+        w_sink, b_sink = ctx.sinks
+        dw = None
+        if ctx.needs_input_grad[1]:
+            if w_sink is not None:
+                gemm(dz, x2, a_kmajor=False, b_kmajor=False, out=w_sink.view(w.shape), accumulate=True)
+            else:
+                dw = gemm(dz, x2, a_kmajor=False, b_kmajor=False, out_dtype=torch.float32).to(wdt)
+        dbias = None
+        if has_b and ctx.needs_input_grad[2]:
+            if b_sink is not None:
+                column_sum(dz, out=b_sink, accumulate=True)
+            else:
+                dbias = column_sum(dz).to(biasdt)
+        return dx, dw, dbias, da, db_lora, None, (dy if has_res else None), None, None
+
+
+def lora_linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None,
+    lora_a: torch.Tensor,
+    lora_b: torch.Tensor,
+    scaling: float,
+    activation: str | None = None,
+    residual: torch.Tensor | None = None,
+) -> torch.Tensor | None:
+    """`residual + act(x W^T + b + scaling (x A^T) B^T)` on one native GEMM, or None when the native
+    path does not apply (the caller then composes it from separate ops)."""
+    act = _ACTS[activation]
+    cdtype = compute_dtype(x)
+    r = lora_a.shape[0]
+    if not (cdtype == torch.bfloat16 and use_native(x) and x.shape[-1] % 8 == 0 and weight.shape[0] % 8 == 0
+            and r % 8 == 0 and weight.dim() == 2):
+        return None
+    return _NativeLoRALinear.apply(x, weight, bias, lora_a, lora_b, float(scaling), residual, act, cdtype)
+

@@ -83,3 +83,27 @@ def test_koleo_native(b, d):
     ref.backward()
     assert abs(float(out) - float(ref)) < 1e-4 * max(1.0, abs(float(ref)))
     assert _rel(xa.grad, xr.grad) < 1e-3
+
+
+@needs_cuda
+def test_prototype_gemm_sinkhorn_colsum():
+    """The prototype GEMM's epilogue column sums equal sum_b exp(logits / T), and Sinkhorn fed with
+    them equals Sinkhorn computing them itself."""
+    from mia_train_b200.algorithms.dinov3.losses import sinkhorn_knopp
+    from mia_train_b200.layers.dinov3.head import DINOHead
+
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    head = DINOHead(in_dim=256, out_dim=8192, nlayers=2, hidden_dim=512, bottleneck_dim=128).to(dev)
+    x = torch.randn(200, 256, device=dev)
+    temp = 0.07
+    colsum = torch.zeros(8192, device=dev)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        fused = head(x, colsum, temp)
+        plain = head(x)
+    assert _rel(fused, plain) < 2e-2
+    ref = torch.exp(fused.float() / temp).sum(0)
+    assert _rel(colsum, ref) < 1e-3
+    a = sinkhorn_knopp(fused, temp, 3, colsum=colsum)
+    b = sinkhorn_knopp(fused, temp, 3)
+    assert _rel(a, b) < 1e-3

@@ -520,3 +520,35 @@ def test_zscore_u8(shape, dtype):
     assert got.dtype == dtype
     _close(got, ref, rel=1e-2 if dtype == torch.bfloat16 else 1e-5, atol=1e-2 if dtype == torch.bfloat16 else 1e-5)
     _no_errors()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs CUDA")
+@pytest.mark.parametrize("activation", [None, "gelu"])
+def test_lora_linear_native(activation):
+    """LoRA delta accumulated into the base GEMM's tile vs the fp32 composition, forward and backward."""
+    from mia_train_b200.ops.linear import lora_linear
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11)
+    m, k, n, r = 1000, 512, 768, 16
+    x = torch.randn(m, k, device=dev, generator=g).bfloat16().requires_grad_(True)
+    w = (torch.randn(n, k, device=dev, generator=g) / k**0.5).requires_grad_(True)
+    b = torch.randn(n, device=dev, generator=g).requires_grad_(True)
+    la = (torch.randn(r, k, device=dev, generator=g) / k**0.5).requires_grad_(True)
+    lb = torch.randn(n, r, device=dev, generator=g).requires_grad_(True)
+    s = 0.5
+    y = lora_linear(x, w, b, la, lb, s, activation=activation)
+    assert y is not None
+    gy = torch.randn_like(y.float())
+    (y.float() * gy).sum().backward()
+    xr, wr, br, lar, lbr = (t.detach().float().requires_grad_(True) for t in (x, w, b, la, lb))
+    z = xr @ wr.t() + br + s * (xr @ lar.t()) @ lbr.t()
+    yr = torch.nn.functional.gelu(z) if activation == "gelu" else z
+    (yr * gy).sum().backward()
+
+    def rel(u, v):
+        return float((u.float() - v.float()).norm() / (v.float().norm() + 1e-6))
+
+    assert rel(y, yr) < 2e-2
+    for got, ref in ((x.grad, xr.grad), (w.grad, wr.grad), (b.grad, br.grad), (la.grad, lar.grad), (lb.grad, lbr.grad)):
+        assert rel(got, ref) < 3e-2
