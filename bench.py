@@ -65,9 +65,11 @@ def parse() -> argparse.Namespace:
                     help="data-parallel gradient path for N > 1 (sharded optimizer over peer memory by default)")
     ap.add_argument("--profile-kernels", type=int, default=0, metavar="STEPS",
                     help="also profile STEPS eager steps and print the per-kernel device-time table")
-    ap.add_argument("--config", choices=("vit_l_mae", "windowed_tp"), default="vit_l_mae",
+    ap.add_argument("--config", choices=("vit_l_mae", "windowed_tp", "affinity_tp", "dinov3_dp"), default="vit_l_mae",
                     help="vit_l_mae: ViT-L 3D MAE at 128^3 (the default headline workload); windowed_tp: windowed "
-                         "dinov3_vit3d ViT-L SimMIM at 256^3 / patch 8 under sequence-parallel TP (TP = min(4, N))")
+                         "dinov3_vit3d ViT-L SimMIM at 256^3 / patch 8 under sequence-parallel TP (TP = min(4, N)); "
+                         "affinity_tp: ViT-L affinity segmentation, 128^3 / patch 8, 12 offsets (TP = min(2, N)); "
+                         "dinov3_dp: DINOv3 on a ViT-H-class 3D encoder, 8 samples of 2 + 8 crops per GPU")
     ap.add_argument("--tp-comm", choices=("fused", "collective"), default="fused",
                     help="windowed_tp: fused collective-GEMM kernels over NVLink, or NCCL collectives")
     return ap.parse_args()
@@ -480,8 +482,15 @@ def timed_loop(fn, steps: int, sampler_index: int | None, world: int) -> tuple[f
     return ms, float(loss.item()) if loss is not None else float("nan"), sampler.summary() if sampler else None
 
 
-def windowed_tp_main(args: argparse.Namespace, rank: int, world: int, local: int) -> None:
-    from mia_train_b200.benchmarks import windowed_tp as wtp
+EXTRA_CONFIGS = ("windowed_tp", "affinity_tp", "dinov3_dp")
+
+
+def extra_config_main(args: argparse.Namespace, rank: int, world: int, local: int) -> None:
+    """The benchmark workloads that live in `mia_train_b200.benchmarks` (one module per workload,
+    each with `native_arm`, `reference_arm`, `describe` and its METRIC / DATA / SEQ_LEN)."""
+    import importlib
+
+    wtp = importlib.import_module(f"mia_train_b200.benchmarks.{args.config}")
 
     def timed(fn, steps, sampler):
         return timed_loop(fn, steps, local if sampler is not None else None, world)
@@ -497,13 +506,13 @@ def windowed_tp_main(args: argparse.Namespace, rank: int, world: int, local: int
         gb = res["global_batch"]
         value = gb * 1000.0 / res["ms"]
         line = {
-            "metric": "samples/sec (windowed dinov3_vit3d ViT-L SimMIM, 256^3, patch 8, bf16), whole box, "
-                      "device-timed max over ranks",
+            "metric": wtp.METRIC,
             "value": round(value, 3), "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(res["ms"], 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (uint8 blurred-noise + ellipsoid 256^3 volumes, z-scored on device; random-init weights)",
-            "config": {**wtp.describe(world), "global_batch": gb, "seq_len": 32769,
+            "data": wtp.DATA,
+            "config": {**wtp.describe(world), "global_batch": gb,
+                       "seq_len": wtp.SEQ_LEN,
                        "parallelism": res["parallelism"], "l2": "activations far larger than L2 (no flush)"},
             "mfu": round(res["flops"] / (res["ms"] / 1000.0) / PEAK_BF16, 4),
             "tflops_per_gpu": round(res["flops"] / (res["ms"] / 1000.0) / 1e12, 1),
@@ -517,14 +526,16 @@ def windowed_tp_main(args: argparse.Namespace, rank: int, world: int, local: int
         else:
             line["kernel_errors"] = res["errors"]
             line["native_library"] = res["lib"]
+        if "memory_gb" in res:
+            line["max_memory_allocated_gb"] = res["memory_gb"]
         print(json.dumps(line), flush=True)
 
 
 def main() -> None:
     args = parse()
     rank, world, local = dist_setup()
-    if args.config == "windowed_tp":
-        windowed_tp_main(args, rank, world, local)
+    if args.config in EXTRA_CONFIGS:
+        extra_config_main(args, rank, world, local)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()

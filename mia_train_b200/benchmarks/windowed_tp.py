@@ -37,6 +37,10 @@ MODEL = dict(img_size=256, patch_size=8, embed_dim=1024, depth=24, num_heads=16,
 WINDOW = dict(window_size=8, global_every=6)
 MASK_RATIO = 0.6
 SIDE = 256
+METRIC = ("samples/sec (windowed dinov3_vit3d ViT-L SimMIM, 256^3, patch 8, bf16), whole box, "
+          "device-timed max over ranks")
+DATA = "synthetic (uint8 blurred-noise + ellipsoid 256^3 volumes, z-scored on device; random-init weights)"
+SEQ_LEN = 32769  # 32768 patch tokens + class token
 
 
 def describe(n_gpus: int) -> dict:
@@ -50,14 +54,14 @@ def describe(n_gpus: int) -> dict:
     }
 
 
-def make_volumes(n: int, seed: int) -> torch.Tensor:
-    """n uint8 volumes (n, 1, 1, 256, 256, 256): blurred noise + ellipsoid blobs."""
+def make_volumes(n: int, seed: int, side: int = SIDE) -> torch.Tensor:
+    """n uint8 volumes (n, 1, 1, side, side, side): blurred noise + ellipsoid blobs."""
     from ..data.synthetic import blobs_volume
 
     vols = []
     for i in range(n):
         g = torch.Generator().manual_seed(seed * 1000 + i)
-        v = blobs_volume((SIDE,) * 3, 3.0, 50.0, (2.0, 8.0), g)
+        v = blobs_volume((side,) * 3, 3.0, 50.0, (2.0, 8.0), g)
         vols.append(((v - v.min()) / (v.max() - v.min()).clamp_min(1e-6) * 255).round().to(torch.uint8))
     return torch.stack(vols)[:, None, None].contiguous()
 
