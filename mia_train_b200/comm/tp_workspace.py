@@ -2,13 +2,14 @@
 
 One CUDA-IPC allocation per rank of the TP group, mapped into every peer:
 
-    [ flags | send buffer, parity 0 | parity 1 | receive slots, parity 0 | parity 1 ]
+    [ flags | gather area, parity 0 | parity 1 | receive slots, parity 0 | parity 1 ]
 
 * flags: the per-block ready flags the peers write, local counters, and the device epochs that
   select the buffer parity of each launch (so a captured CUDA graph stays correct on replay);
-* send buffer: this rank's rows of an all-gathered operand, read by every peer;
+* gather area: one (rows per rank, K) bf16 slot per source rank, into which every peer pushes its
+  rows of an all-gathered operand;
 * receive slots: one (rows per rank, N) bf16 slot per source rank, written by every peer's
-  GEMM epilogue and summed by this rank.
+  GEMM epilogue and added into this rank's accumulators.
 
 Sizes are fixed at construction (`max_rows` rows per rank, at most `max_k` gathered columns and
 `max_n` reduced columns); the kernels refuse larger problems. Construction is collective.
@@ -46,15 +47,17 @@ class TpWorkspace:
         self.max_rows, self.max_k, self.max_n = int(max_rows), int(max_k), int(max_n)
         self.timeout_ms = float(timeout_ms)
         self.flag_bytes = _round256(int(native().tp_flag_bytes()))
-        self.send_parity_bytes = _round256(self.max_rows * self.max_k * 2)
+        self.gather_parity_bytes = _round256(self.world * self.max_rows * self.max_k * 2)
         self.recv_parity_bytes = _round256(self.world * self.max_rows * self.max_n * 2)
-        total = self.flag_bytes + 2 * self.send_parity_bytes + 2 * self.recv_parity_bytes
+        total = self.flag_bytes + 2 * self.gather_parity_bytes + 2 * self.recv_parity_bytes
         self._ipc = IpcBuffers(group, device)
         self.local, peers = self._ipc.allocate(total, torch.uint8)
         self.flag_peers = [int(p) for p in peers]
-        self.send_peers = [p + self.flag_bytes for p in self.flag_peers]
-        self.recv_peers = [p + self.flag_bytes + 2 * self.send_parity_bytes for p in self.flag_peers]
+        self.gather_peers = [p + self.flag_bytes for p in self.flag_peers]
+        self.recv_peers = [p + self.flag_bytes + 2 * self.gather_parity_bytes for p in self.flag_peers]
         self.nbytes = total
+        # B operand of the reduce-scatter kernel's identity MMA (adds received partials in TMEM)
+        self.ident = torch.eye(128, dtype=torch.bfloat16, device=device)
 
     def release(self) -> None:
         self._ipc.release()
@@ -67,7 +70,7 @@ class TpWorkspace:
                 f"({self.max_rows} rows x {self.max_k})"
             )
         native().tp_ag_gemm(a_local, b, out, a_full, bias, aux, aux_out, b_kmajor, act, self.flag_peers,
-                            self.send_peers, self.send_parity_bytes, self.rank, self.timeout_ms)
+                            self.gather_peers, self.gather_parity_bytes, self.rank, self.timeout_ms)
 
     def gemm_rs(self, a, b, out, bias, gamma, residual, pre_out, b_kmajor: bool) -> None:
         rows = a.shape[0] // self.world
@@ -78,4 +81,4 @@ class TpWorkspace:
                 f"({self.max_rows} rows x {self.max_n})"
             )
         native().tp_gemm_rs(a, b, out, bias, gamma, residual, pre_out, b_kmajor, self.flag_peers, self.recv_peers,
-                            self.recv_parity_bytes, self.rank, self.timeout_ms)
+                            self.recv_parity_bytes, self.rank, self.timeout_ms, self.ident)

@@ -77,8 +77,10 @@ void tp_ag_gemm(at::Tensor a_local, at::Tensor b, at::Tensor out, at::Tensor a_f
 void tp_gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, c10::optional<at::Tensor> bias,
                 c10::optional<at::Tensor> gamma, c10::optional<at::Tensor> residual,
                 c10::optional<at::Tensor> pre_out, bool b_kmajor, std::vector<int64_t> flag_peers,
-                std::vector<int64_t> recv_peers, int64_t recv_parity_bytes, int64_t rank, double timeout_ms);
+                std::vector<int64_t> recv_peers, int64_t recv_parity_bytes, int64_t rank, double timeout_ms,
+                at::Tensor ident);
 int64_t tp_flag_bytes();
+at::Tensor tp_trace_read(int64_t device);
 void soft_ce_fwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse, at::Tensor loss);
 void soft_ce_bwd(at::Tensor S, at::Tensor T, at::Tensor tidx, at::Tensor w, double tau, at::Tensor lse,
                  at::Tensor grad_scale, at::Tensor dS);
@@ -134,9 +136,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("zero_advance_epoch", &mia::zero_advance_epoch);
   m.def("zero_reduce_scatter_bf16", &mia::zero_reduce_scatter_bf16,
         "peer-memory gradient reduce-scatter with bf16 on the wire (fp32 sum) + sum of squares");
-  m.def("tp_ag_gemm", &mia::tp_ag_gemm, "fused all-gather (peer memory) -> tcgen05 GEMM, sequence-parallel input");
+  m.def("tp_ag_gemm", &mia::tp_ag_gemm, "fused all-gather (peer pushes) -> tcgen05 GEMM, sequence-parallel input");
   m.def("tp_gemm_rs", &mia::tp_gemm_rs, "fused tcgen05 GEMM -> reduce-scatter (peer stores) + bias/LayerScale/residual");
   m.def("tp_flag_bytes", &mia::tp_flag_bytes, "bytes of one rank's flag area for the fused TP kernels");
+  m.def("tp_trace_read", &mia::tp_trace_read, "per-CTA timelines of the last fused TP launches (MIA_TP_TRACE=1)");
   m.def("soft_ce_fwd", &mia::soft_ce_fwd, "soft-target cross-entropy over prototypes (DINO / iBOT): lse + per-row loss");
   m.def("soft_ce_bwd", &mia::soft_ce_bwd, "gradient of soft_ce_fwd with respect to the student logits");
   m.def("set_attention_poly_exp", &mia::set_attention_poly_exp,

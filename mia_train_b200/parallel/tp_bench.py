@@ -28,6 +28,32 @@ PEAK_FLOPS = 1410.2e12  # measured sustained cuBLAS bf16 on this pool's B200s
 LINK_BPS = 770e9  # measured peer copy bandwidth per direction per GPU
 
 
+AG_POINTS = ("start", "first-N-tile slices stored", "first block pushed", "all blocks pushed",
+             "producer reached peers' tiles", "MMA done", "epilogue done", "exit")
+RS_POINTS = ("start", "MMA done", "epilogue done", "peer tiles landed", "first own block's partials present", "-",
+             "-", "exit")
+
+
+def _timeline(trace: torch.Tensor, kind: int) -> dict:
+    """{point: [min, median, max] us after the earliest CTA start} over the CTAs that recorded it in
+    this launch (a CTA's entries are kept from its own start on)."""
+    t = trace[kind]
+    t = t[t[:, 0] > 0]
+    if t.numel() == 0:
+        return {}
+    t0 = int(t[:, 0].min())
+    names = AG_POINTS if kind == 0 else RS_POINTS
+    out = {}
+    for i, name in enumerate(names):
+        col = t[:, i]
+        col = col[col >= t[:, 0]]
+        if name == "-" or col.numel() == 0:
+            continue
+        us = (col - t0).double() / 1000.0
+        out[name] = [round(float(us.min()), 1), round(float(us.median()), 1), round(float(us.max()), 1)]
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=32768)
@@ -92,16 +118,34 @@ def main() -> None:
             t = torch.tensor([statistics.median(samples)], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             times[label] = float(t) * 1e-3
+        # the fused result against the collective one (same GEMM kernel, NCCL transfer)
+        outs = [fn(cm) for cm in (fused, coll)]
+        outs = [o[0] if isinstance(o, tuple) else o for o in outs]
+        rel = torch.tensor([float((outs[0].float() - outs[1].float()).norm() / (outs[1].float().norm() + 1e-12))],
+                           device=dev)
+        dist.all_reduce(rel, op=dist.ReduceOp.MAX)
         roof = max(flops / PEAK_FLOPS, link_bytes / LINK_BPS)
         results.append({"op": name, "tokens": m, "dim": c, "tp": world, "fused_us": round(times["fused"] * 1e6, 1),
                         "nccl_us": round(times["nccl"] * 1e6, 1), "speedup": round(times["nccl"] / times["fused"], 3),
                         "roofline_us": round(roof * 1e6, 1), "fused_frac_of_roofline": round(roof / times["fused"], 3),
                         "tflops": round(flops / times["fused"] / 1e12, 1),
-                        "link_gbs": round(link_bytes / times["fused"] / 1e9, 1)})
+                        "link_gbs": round(link_bytes / times["fused"] / 1e9, 1),
+                        "rel_err_vs_nccl": round(float(rel), 5)})
+    traces = {}
+    if os.environ.get("MIA_TP_TRACE") == "1":
+        # one more launch of each fused op, then its per-CTA timeline (us after the first CTA started)
+        for name, (fn, _, _) in ops.items():
+            dist.barrier()
+            torch.cuda.synchronize()
+            fn(fused)
+            torch.cuda.synchronize()
+            traces[name] = _timeline(_native.native().tp_trace_read(local), 0 if "all-gather" in name else 1)
     errors = int(_native.native().check_errors(local))
     if rank == 0:
         for r in results:
             print(json.dumps({**r, "kernel_errors": errors}), flush=True)
+        for name, tl in traces.items():
+            print(json.dumps({"trace": name, "rank": rank, "points_us": tl}), flush=True)
     dist.barrier()
     fused.release()
     dist.destroy_process_group()

@@ -63,3 +63,64 @@ def test_reduce_scatter_wait_runs_out(cuda_device):
     torch.cuda.synchronize(cuda_device)
     assert n.check_errors(cuda_device.index) == 401
     assert torch.all(partial == 0)  # no block summed anything after giving up
+
+
+def _tp_buffers(dev, gather_bytes, recv_bytes):
+    """(flags, gather area, receive area) of one rank of the fused TP kernels, zeroed."""
+    n = _native()
+    flags = torch.zeros(n.tp_flag_bytes() // 4, dtype=torch.int32, device=dev)
+    gather = torch.zeros(2 * gather_bytes, dtype=torch.uint8, device=dev)
+    recv = torch.zeros(2 * recv_bytes, dtype=torch.uint8, device=dev)
+    return flags, gather, recv
+
+
+def test_tp_all_gather_gemm_wait_runs_out(cuda_device):
+    """Rank 0 of a 2-rank all-gather -> GEMM whose peer never pushes its rows: the GEMM CTAs give up
+    on the peer's block flags, the kernel records kErrTpChunkWait (502) and returns."""
+    n = _native()
+    n.check_errors(cuda_device.index)
+    s, k, cols = 256, 128, 256
+    gather_bytes = 2 * s * k * 2
+    mine = _tp_buffers(cuda_device, gather_bytes, 256)
+    silent = _tp_buffers(cuda_device, gather_bytes, 256)  # rank 1: nothing ever runs there
+    x = torch.randn(s, k, device=cuda_device).bfloat16()
+    w = torch.randn(cols, k, device=cuda_device).bfloat16()
+    out = torch.zeros(2 * s, cols, device=cuda_device, dtype=torch.bfloat16)
+    full = torch.zeros(2 * s, k, device=cuda_device, dtype=torch.bfloat16)
+    n.tp_ag_gemm(x, w, out, full, None, None, None, True, 0, [mine[0].data_ptr(), silent[0].data_ptr()],
+                 [mine[1].data_ptr(), silent[1].data_ptr()], gather_bytes, 0, 5.0)
+    torch.cuda.synchronize(cuda_device)  # the kernel returned
+    assert n.check_errors(cuda_device.index) == 502
+    # this rank's own rows were still gathered and computed
+    assert torch.equal(full[:s], x)
+    ref = x.float() @ w.float().t()
+    assert float((out[:s].float() - ref).norm() / ref.norm()) < 1e-2
+    # and they were pushed into the peer's gather area (slot 0, parity 1: the first launch) and published
+    pushed = silent[1][gather_bytes:].view(torch.bfloat16).view(2, s, k)[0]
+    assert torch.equal(pushed, x)
+    assert int(silent[0][:4096].max()) == 1
+
+
+def test_tp_gemm_reduce_scatter_wait_runs_out(cuda_device):
+    """Rank 0 of a 2-rank GEMM -> reduce-scatter whose peer never sends its partial rows: the
+    producer gives up before adding them, the kernel records kErrTpSlotWait (503) and returns without
+    writing the output."""
+    n = _native()
+    n.check_errors(cuda_device.index)
+    s, k, cols = 256, 128, 256
+    recv_bytes = 2 * s * cols * 2
+    mine = _tp_buffers(cuda_device, 256, recv_bytes)
+    silent = _tp_buffers(cuda_device, 256, recv_bytes)
+    a = torch.randn(2 * s, k, device=cuda_device).bfloat16()
+    w = torch.randn(cols, k, device=cuda_device).bfloat16()
+    out = torch.zeros(s, cols, device=cuda_device, dtype=torch.bfloat16)
+    n.tp_gemm_rs(a, w, out, None, None, None, None, True, [mine[0].data_ptr(), silent[0].data_ptr()],
+                 [mine[2].data_ptr(), silent[2].data_ptr()], recv_bytes, 0, 5.0,
+                 torch.eye(128, dtype=torch.bfloat16, device=cuda_device))
+    torch.cuda.synchronize(cuda_device)
+    assert n.check_errors(cuda_device.index) == 503
+    assert int(out.view(torch.int16).abs().max()) == 0
+    # the partial rows owned by rank 1 went to its receive slot 0 (parity 1: the first launch)
+    slot = silent[2].view(torch.bfloat16)[recv_bytes // 2:].view(2, s, cols)[0]
+    ref = a[s:].float() @ w.float().t()
+    assert float((slot.float() - ref).norm() / ref.norm()) < 1e-2
