@@ -28,8 +28,8 @@
 // writes the A slices of every block's first N tile from shared memory into the gathered output,
 // which the backward pass needs for dW.
 //
-// GEMM -> reduce-scatter. The peers' row blocks come first (the next rank's, then the one after,
-// ...), this rank's own last. A peer tile is rounded to bf16 into one of two shared-memory staging
+// GEMM -> reduce-scatter. The peers' row blocks come first (block j of every peer in turn), this
+// rank's own last. A peer tile is rounded to bf16 into one of two shared-memory staging
 // tiles and sent by a store warp with TMA stores into the owner's receive slot; once its rows have
 // landed it is counted against its block, and the CTA that completes a block publishes it to the
 // owner. An own tile continues its K loop over the peers' partial tiles (TMA-loaded from this rank's
@@ -601,12 +601,20 @@ struct RsSmem {
   static constexpr int kBytes = kBarOffset + 1024 + 512;
 };
 
-// Ordered block index -> row block: every block of the next rank, then of the rank after, ..., and
-// this rank's own blocks last.
-__device__ __forceinline__ int rs_block(const TpShape& s, int nloc, int bi) {
+// Ordered block index -> row block. Step j sends block j of every peer (interleaved, so every
+// peer's link is busy) and then computes this rank's own block j - delta: own blocks trail by
+// `delta` steps, so that by the time one is computed the peers (which follow the same order) have
+// sent their partials of it. With delta = nloc every own block comes last.
+__device__ __forceinline__ int rs_block(const TpShape& s, int nloc, int delta, int bi) {
   if (s.world == 1) return bi;
-  const int d = bi / nloc + 1, j = bi - (d - 1) * nloc;
-  return ((s.rank + d) % s.world) * nloc + j;
+  const int W = s.world, a = delta * (W - 1);
+  if (bi < a) return ((s.rank + bi % (W - 1) + 1) % W) * nloc + bi / (W - 1);
+  const int r = bi - a;
+  if (r < (nloc - delta) * W) {
+    const int j = delta + r / W, k = r % W;
+    return k < W - 1 ? ((s.rank + k + 1) % W) * nloc + j : s.rank * nloc + j - delta;
+  }
+  return s.rank * nloc + nloc - delta + (r - (nloc - delta) * W);
 }
 
 // Counts one finished tile of `word`'s block in this launch; true for the block's last tile.
@@ -717,7 +725,11 @@ __global__ void __launch_bounds__(kRsThreads, 1)
   const int num_n = (s.N + BN - 1) / BN;
   const int nloc = s.world > 1 ? s.S / 128 : s.num_blocks;
   const int num_tiles = s.num_blocks * num_n;
-  const int first_own = (s.world - 1) * nloc * num_n;  // tiles before this index go to peers
+  // Own blocks come after every peer block. (Trailing the peers' by three rounds of tiles instead, so
+  // that their identity MMAs overlap the sends, measured 4-17% slower at two ranks: each own tile
+  // must first flush the store warp's pending tile counts.)
+  const int delta = s.world > 1 ? nloc : 0;
+  auto is_own = [&](int mb) { return s.world == 1 || mb / nloc == s.rank; };
   // own tiles continue their K loop over the peers' partials (and the residual) times the identity
   const int extra = 2 * (s.world - 1) + (P.fold_residual ? 2 : 0);
   int* my_flags = reinterpret_cast<int*>(pick(P.flags, s.rank));
@@ -764,9 +776,9 @@ __global__ void __launch_bounds__(kRsThreads, 1)
       constexpr uint32_t kTx = kATileBytes + L::kBTileBytes;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const int bi = t / num_n, nt = t - bi * num_n;
-        const int mb = rs_block(s, nloc, bi);
+        const int mb = rs_block(s, nloc, delta, bi);
         const int m0 = mb * 128, n0 = nt * BN;
-        const int slices = num_k + (t >= first_own ? extra : 0);
+        const int slices = num_k + (is_own(mb) ? extra : 0);
         for (int kb = 0; kb < slices; ++kb) {
           if (kb == num_k && s.world > 1) {
             // the peers' partial rows of this block must be in our receive slots before we read them
@@ -849,7 +861,7 @@ __global__ void __launch_bounds__(kRsThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const int slices = num_k + (t >= first_own ? extra : 0);
+        const int slices = num_k + (is_own(rs_block(s, nloc, delta, t / num_n)) ? extra : 0);
         for (int kb = 0; kb < slices; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, P.err, kErrGemmMmaWait)) {
             ok = false;
@@ -896,8 +908,8 @@ __global__ void __launch_bounds__(kRsThreads, 1)
     int jp = 0;  // peer tiles staged so far
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int bi = t / num_n, nt = t - bi * num_n;
-      const int mb = rs_block(s, nloc, bi);
-      const bool own = t >= first_own;
+      const int mb = rs_block(s, nloc, delta, bi);
+      const bool own = is_own(mb);
       const int b = jp & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, P.err, kErrGemmEpilogueWait)) break;
       if (!own && !mbar_wait(&sempty_bar[b], ((jp >> 1) & 1) ^ 1, abort_flag, P.err, kErrGemmEpilogueWait)) break;
@@ -952,7 +964,8 @@ __global__ void __launch_bounds__(kRsThreads, 1)
       // ---------------- store warp: staged peer tiles -> owner's receive slot
       // A staging tile is released once its stores have read it (one tile later, so the wait is
       // normally over); a tile is counted against its block once its rows have landed (three tiles
-      // later). Only the CTA that completes a block pays for a system-scope release.
+      // later, or at once when this CTA reaches one of its own tiles, whose producer may wait on the
+      // peers). Only the CTA that completes a block pays for a system-scope release.
       int ring[4] = {-1, -1, -1, -1};  // blocks of the last four tiles issued
       int j = 0;
       bool ok = true;
@@ -965,14 +978,22 @@ __global__ void __launch_bounds__(kRsThreads, 1)
                          epoch);
         }
       };
-      for (int t = blockIdx.x; t < first_own; t += gridDim.x, ++j) {
+      int landed = 0;  // tiles counted so far
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int bi = t / num_n, nt = t - bi * num_n;
+        const int mb = rs_block(s, nloc, delta, bi);
+        if (is_own(mb)) {
+          // this CTA's producer may now wait for the peers' partials, and the peers for ours: count
+          // every tile sent so far before that can happen
+          bulk_wait_all();
+          for (; landed < j; ++landed) tile_landed(ring[landed & 3]);
+          continue;
+        }
         const int b = j & 1;
         if (!mbar_wait(&sfull_bar[b], (j >> 1) & 1, abort_flag, P.err, kErrGemmEpilogueWait)) {
           ok = false;
           break;
         }
-        const int bi = t / num_n, nt = t - bi * num_n;
-        const int mb = rs_block(s, nloc, bi);
         const int owner = mb / nloc;
         const uint8_t* tile = staging + b * L::kStagingBytes;
 #pragma unroll
@@ -984,11 +1005,12 @@ __global__ void __launch_bounds__(kRsThreads, 1)
         bulk_wait_read_all_but_one();  // tile j - 1's staging buffer has been read
         if (j >= 1) mbar_arrive(&sempty_bar[(j - 1) & 1]);
         bulk_wait_all_but_three();  // tile j - 3's rows are in the owner's slot
-        if (j >= 3) tile_landed(ring[(j - 3) & 3]);
+        for (; landed <= j - 3; ++landed) tile_landed(ring[landed & 3]);
+        ++j;
       }
       bulk_wait_all();
       if (ok)
-        for (int i = j - 3 < 0 ? 0 : j - 3; i < j; ++i) tile_landed(ring[i & 3]);
+        for (; landed < j; ++landed) tile_landed(ring[landed & 3]);
       trace_mark(P.trace, 3);
     }
   }
