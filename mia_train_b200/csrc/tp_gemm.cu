@@ -172,7 +172,6 @@ __device__ __forceinline__ void bulk_wait_read_all_but_one() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all_but_three() { asm volatile("cp.async.bulk.wait_group 3;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all_but_seven() { asm volatile("cp.async.bulk.wait_group 7;" ::: "memory"); }
 
 struct TpShape {
   int M, N, K;      // gathered rows, output columns, reduction length
@@ -228,10 +227,10 @@ __device__ __forceinline__ int ag_block(const TpShape& s, int nloc, int bi) {
 
 // Copy CTA c of C: pushes this rank's row blocks c, c + C, ... to every peer. A block (128
 // contiguous rows) is read in 32 KB bulk loads (six in flight) and each chunk is written by bulk
-// stores into the same place of every peer's gather area (this rank's slot); once a block's stores
-// have all landed it is published to every peer with a system-scope flag. The stores never hold a
-// slot (only their shared-memory reads do), so up to seven chunks' stores stay in flight. One
-// thread works; nothing here waits on another GPU.
+// stores into the same place of every peer's gather area (this rank's slot); after a block's last
+// chunk the thread waits for the block's stores to land and publishes it to every peer with a
+// system-scope flag. The stores never hold a slot (only their shared-memory reads do). One thread
+// works; nothing here waits on another GPU.
 __device__ __forceinline__ void ag_copy_cta(const AgParams& P, uint8_t* smem, int nloc, int epoch, int par,
                                             volatile int* abort_flag) {
   const TpShape& s = P.s;
@@ -285,8 +284,12 @@ __device__ __forceinline__ void ag_copy_cta(const AgParams& P, uint8_t* smem, in
     bulk_commit();
     bulk_wait_read();  // the slot may be refilled
     if (issued < total) issue(issued++);
-    bulk_wait_all_but_seven();  // chunks up to g - 7 have landed in every peer
-    if (g >= 7) publish_upto((g - 6) / chunks);
+    if (ch == chunks - 1) {
+      // the block's last chunk: wait for its stores (the next loads stay in flight) and publish it
+      // at once, so that the peers' GEMMs can start on it
+      bulk_wait_all();
+      publish_upto(it + 1);
+    }
   }
   bulk_wait_all();
   if (ok) {
