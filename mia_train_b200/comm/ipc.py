@@ -3,7 +3,8 @@
 Each rank allocates with `cudaMalloc` and exports a CUDA IPC handle (`_C.ipc_export`); the
 handles are exchanged over the process group and opened on every peer (`_C.ipc_open`), which gives
 every rank a device pointer to every peer's copy. Kernels move data with plain peer loads and
-stores (`csrc/comm.cu`, `csrc/tp_gemm.cu`). Allocation is collective: every rank of the group must
+stores (`csrc/comm.cu`) or with TMA stores and bulk copies into the peers' buffers
+(`csrc/tp_gemm.cu`). Allocation is collective: every rank of the group must
 call `allocate` with the same sizes in the same order.
 """
 
