@@ -69,6 +69,7 @@ class AffinitySegmentation(BaseAlgorithm):
         decoder_zero_init_output: bool = True,
         ignore_index: int = -1,
         split_disconnected: bool = True,
+        split_decoder_over_tp: bool = True,
     ) -> None:
         super().__init__(model, dataset)
         if long_range < 1:
@@ -90,6 +91,11 @@ class AffinitySegmentation(BaseAlgorithm):
         self.decoder_kind = decoder
         self.encoder = model
         self._split_delegated = False
+        # Under sequence-parallel TP the encoder's tokens are gathered on every TP rank; the voxel
+        # decoder and the loss then run on this rank's share of the samples only (the encoder's
+        # final norm and the decoder become partial-gradient parameters summed over the group).
+        self.split_decoder_over_tp = split_decoder_over_tp
+        self._post_gather_marked = False
         embed_dim = int(model.embed_dim)
         n_out = len(self.offsets)
         if decoder == "subpixel":
@@ -153,15 +159,63 @@ class AffinitySegmentation(BaseAlgorithm):
             raise ValueError(
                 f"label crop {tuple(labels.shape)} does not match the image crop {tuple(volumes.shape)}"
             )
-        with torch.profiler.record_function("encoder"):
-            tokens, grid = self.encoder.patch_features(volumes)
+        sp = getattr(self.encoder, "_sequence_parallel", None)
+        part = sp.sample_slice(volumes.shape[0]) if sp is not None and self.split_decoder_over_tp else None
+        if part is not None:
+            self._mark_post_gather(sp)
+            sp.split_samples = True
+        try:
+            with torch.profiler.record_function("encoder"):
+                tokens, grid = self.encoder.patch_features(volumes)
+        finally:
+            if part is not None:
+                sp.split_samples = False
+        if part is not None:
+            tokens, labels = tokens[part], labels[part]
         with torch.profiler.record_function("decoder"):
             logits = self._decode(tokens, grid, volumes.shape[2:])
         if self.split_disconnected and not self._split_delegated:
             with torch.profiler.record_function("relabel_connected"):
                 labels = torch.stack([relabel_connected(s) for s in labels])
         with torch.profiler.record_function("affinity_loss"):
-            return affinity_bce(logits, labels, self.offsets, self.ignore_index)
+            out = affinity_bce(logits, labels, self.offsets, self.ignore_index)
+        return self._combine_over_tp(out, logits.numel(), sp) if part is not None else out
+
+    def _mark_post_gather(self, sp: Any) -> None:
+        if self._post_gather_marked:
+            return
+        from ..parallel.sequence_parallel import mark_post_gather_params
+
+        mods = [self.decoder, self.decoder_out]
+        for name in ("norm", "cls_norm", "local_cls_norm"):
+            mod = getattr(self.encoder, name, None)
+            if isinstance(mod, nn.Module):
+                mods.append(mod)
+        mark_post_gather_params(mods, sp.group)
+        self._post_gather_marked = True
+
+    @staticmethod
+    def _combine_over_tp(out: dict[str, torch.Tensor], numel: int, sp: Any) -> dict[str, torch.Tensor]:
+        """Every TP rank scored its own samples: weight each rank's masked-mean loss by its share of
+        the group's unmasked voxels (so the ranks' gradients sum to the whole batch's), and report
+        the whole batch's loss and metrics on every rank."""
+        import torch.distributed as dist
+
+        count = out["masked_fraction"].detach().float() * numel
+        stats = torch.stack([count, out["loss"].detach().float() * count, out["affinity_accuracy"].float() * count,
+                             out["target_positive_rate"].float() * count, out["boundary_accuracy"].float() * count,
+                             torch.full_like(count, float(numel))])
+        dist.all_reduce(stats, group=sp.group)
+        total = stats[0].clamp_min(1.0)
+        weighted = out["loss"] * (count / total)
+        whole = stats[1] / total
+        return {
+            "loss": weighted + (whole - weighted).detach(),  # the batch's value, this rank's gradient
+            "affinity_accuracy": stats[2] / total,
+            "target_positive_rate": stats[3] / total,
+            "boundary_accuracy": stats[4] / total,  # voxel-weighted across ranks
+            "masked_fraction": stats[0] / stats[5],
+        }
 
     def training_step(self, batch: Any) -> dict[str, torch.Tensor]:
         return self._step(batch)

@@ -39,6 +39,7 @@ from torch.utils.data import DataLoader, DistributedSampler
 from ..algorithms.base import BaseAlgorithm
 from ..data.base import BaseDataset
 from ..ops._native import raise_on_device_errors
+from ..parallel.sequence_parallel import sync_partial_grads
 from ..parallel.parallel_dims import ParallelDims
 from ..parallel.parallelize import parallelize_algorithm
 from ..utils.device import move_to_device
@@ -273,6 +274,9 @@ class Trainer:
                         metrics = self.algorithm(batch)
                     with annotate("backward"):
                         metrics["loss"].backward()
+                        # sequence-parallel TP: norm / LayerScale (and decoder, when the batch is
+                        # split over the TP ranks) gradients are per-rank partial sums
+                        sync_partial_grads(self.algorithm)
                     if self.config.grad_clip_norm is not None:
                         with annotate("grad_clip"):
                             metrics["grad_norm"] = self._clip()

@@ -20,8 +20,8 @@ NCCL (or Gloo) collectives around the GEMMs.
 Parameter gradients: the sharded weights and the biases of the column-parallel layers are
 complete on their rank; the biases of the row-parallel layers are summed over the gathered output
 gradient, so they are complete too. LayerNorm weights / biases and LayerScale gammas see only this
-rank's tokens: they are marked `_sp_partial` and `sync_partial_grads` sums them over the TP group
-(one all-reduce) after backward. Attention runs on all tokens of the local heads, as in the
+rank's tokens: their modules are marked `_sp_partial_group` and `sync_partial_grads` sums them
+over the TP group (one all-reduce) after backward. Attention runs on all tokens of the local heads, as in the
 non-sequence-parallel layout (`parallel/tensor_parallel.py`).
 """
 
@@ -201,11 +201,39 @@ class _GatherRows(torch.autograd.Function):
         return g[rank * rows:(rank + 1) * rows].contiguous(), None
 
 
+class _GatherRowsSummed(torch.autograd.Function):
+    """This rank's rows -> all rows, for computation after it that each TP rank runs on a different
+    part of the batch: the ranks' output gradients differ, so backward sums them over the group and
+    keeps this rank's rows (a reduce-scatter)."""
+
+    @staticmethod
+    def forward(ctx, x, group):  # type: ignore[override]
+        ctx.group = group
+        world = dist.get_world_size(group)
+        if world == 1:
+            return x.clone()
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        return torch.cat(parts, dim=0)
+
+    @staticmethod
+    def backward(ctx, g):  # type: ignore[override]
+        from ..ops.tp import _scatter_sum_rows
+
+        return _scatter_sum_rows(g, ctx.group), None
+
+
 @dataclass
 class SequenceParallel:
-    """What a model needs to run its blocks sequence-parallel over one TP group."""
+    """What a model needs to run its blocks sequence-parallel over one TP group.
+
+    `split_samples`: while True, the computation after the blocks runs on a different slice of the
+    batch on every TP rank (see `sample_slice`), so the final gather sums the ranks' gradients
+    instead of assuming they are equal.
+    """
 
     comm: TpComm
+    split_samples: bool = False
 
     @property
     def world(self) -> int:
@@ -228,8 +256,19 @@ class SequenceParallel:
             x = torch.nn.functional.pad(x, (0, 0, 0, tp - t))
         return _SplitRows.apply(x.reshape(b * tp, c), self.group), t
 
+    def sample_slice(self, batch: int) -> slice | None:
+        """This rank's samples of a batch split over the TP group: rank r of W takes samples
+        [r B // W, (r + 1) B // W). None for a group of one; a batch smaller than the group is an
+        error, since some rank would get no sample."""
+        if self.world == 1:
+            return None
+        if batch < self.world:
+            raise ValueError(f"a batch of {batch} cannot be split over a tensor-parallel group of {self.world}")
+        rank = dist.get_rank(self.group)
+        return slice(rank * batch // self.world, (rank + 1) * batch // self.world)
+
     def gather(self, x_r: torch.Tensor, b: int, t: int) -> torch.Tensor:
-        full = _GatherRows.apply(x_r, self.group)
+        full = (_GatherRowsSummed if self.split_samples else _GatherRows).apply(x_r, self.group)
         tp = full.shape[0] // b
         return full.reshape(b, tp, -1)[:, :t]
 
@@ -279,35 +318,61 @@ def block_forward(
 
 
 def mark_partial_params(blocks: list[nn.Module], group: Any) -> int:
-    """Mark the per-token-shard parameters (norms, LayerScale) whose gradients need a TP sum."""
+    """Mark the per-token-shard parameters (norms, LayerScale) whose gradients need a TP sum. The
+    mark is kept on the owning module, which survives FSDP's replacement of its parameters."""
     count = 0
     for blk in blocks:
         for name in ("norm1", "norm2", "ls1", "ls2"):
             mod = getattr(blk, name, None)
             if mod is None:
                 continue
-            for p in mod.parameters(recurse=False):
-                p._sp_partial = group  # type: ignore[attr-defined]
-                count += 1
+            mod._sp_partial_group = group  # type: ignore[attr-defined]
+            count += sum(1 for _ in mod.parameters(recurse=False))
     return count
 
 
+def mark_post_gather_params(modules: list[nn.Module], group: Any) -> int:
+    """Mark every parameter of modules that run after the final gather on this rank's slice of the
+    batch: each rank's gradient covers its samples only and needs the TP sum."""
+    count = 0
+    for mod in modules:
+        for m in mod.modules():
+            if getattr(m, "_sp_partial_group", None) is None:
+                m._sp_partial_group = group  # type: ignore[attr-defined]
+                count += sum(1 for _ in m.parameters(recurse=False))
+    return count
+
+
+def _partial(module: nn.Module) -> list[tuple[Any, nn.Parameter]]:
+    seen: set[int] = set()
+    out = []
+    for m in module.modules():
+        grp = getattr(m, "_sp_partial_group", None)
+        if grp is None:
+            continue
+        for p in m.parameters(recurse=False):
+            if p.requires_grad and id(p) not in seen:
+                seen.add(id(p))
+                out.append((grp, p))
+    return out
+
+
 def partial_params(module: nn.Module) -> list[nn.Parameter]:
-    return [p for p in module.parameters() if getattr(p, "_sp_partial", None) is not None and p.requires_grad]
+    return [p for _, p in _partial(module)]
 
 
 @torch.no_grad()
 def sync_partial_grads(module: nn.Module) -> int:
     """Sum the sequence-parallel partial gradients over their TP group (one all-reduce per group)."""
     groups: dict[int, tuple[Any, list[torch.Tensor]]] = {}
-    for p in partial_params(module):
+    for grp, p in _partial(module):
         g = getattr(p, "main_grad", None)
         if g is None:
             g = p.grad
         if g is None:
             continue
-        grp = p._sp_partial  # type: ignore[attr-defined]
-        groups.setdefault(id(grp), (grp, []))[1].append(g)
+        to_local = getattr(g, "to_local", None)  # a data-parallel shard (FSDP2): its local part
+        groups.setdefault(id(grp), (grp, []))[1].append(to_local() if to_local is not None else g)
     for grp, grads in groups.values():
         if dist.get_world_size(grp) == 1:
             continue

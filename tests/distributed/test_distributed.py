@@ -162,3 +162,65 @@ def test_device_wait_timeout_stops_training(run_distributed, tmp_path):
     for msg in out.values():
         assert msg.startswith("raised after 1 check"), msg
         assert "code 402" in msg
+
+
+SP_CONFIG = """
+experiment_name = "sp"
+
+[model]
+name = "dinov3_vit3d"
+img_size = 16
+patch_size = 4
+embed_dim = 32
+depth = 2
+num_heads = 2
+
+[algorithm]
+name = "simmim"
+mask_ratio = 0.5
+
+[data]
+name = "synthetic_volumes"
+shape = [16, 16, 16]
+samples_per_epoch = 8
+
+[trainer]
+max_steps = 2
+batch_size = 1
+lr = 1e-3
+warmup_steps = 1
+precision = "fp32"
+log_every = 1
+checkpoint_every = 100
+seed = 0
+
+[parallelism]
+tp = 2
+tp_comm = "collective"
+"""
+
+
+def _sp_trainer_syncs(rank, world, root, config_path):
+    """The Trainer's eager step must sum the sequence-parallel partial gradients over the TP group."""
+    import mia_train_b200.engine.trainer as trainer_module
+    from mia_train_b200.engine.run import run
+
+    counts = []
+    real = trainer_module.sync_partial_grads
+
+    def counting(module):
+        n = real(module)
+        counts.append(n)
+        return n
+
+    trainer_module.sync_partial_grads = counting
+    run(Path(config_path), output_root=Path(root), resume=None)
+    return counts
+
+
+def test_trainer_syncs_sequence_parallel_partial_grads(run_distributed, tmp_path):
+    cfg = tmp_path / "sp.toml"
+    cfg.write_text(SP_CONFIG)
+    out = run_distributed(_sp_trainer_syncs, 2, str(tmp_path / "runs"), str(cfg))
+    for counts in out.values():
+        assert len(counts) == 2 and all(n == 2 * 4 for n in counts), counts  # norm1 / norm2 weight + bias x 2 blocks

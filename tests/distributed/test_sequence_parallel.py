@@ -78,3 +78,78 @@ def test_sequence_parallel_matches_dense(run_distributed, world, window):
         assert abs(loss - ref) < 1e-4 * max(1.0, abs(ref)), (loss, ref)
         assert n_partial == n_marked == 2 * 6  # norm1 / norm2 weight + bias, ls1 / ls2 gamma per block
         assert worst < 1e-4
+
+
+def _gathered_grad(p, mod, world, dense_shape):
+    import torch.distributed as dist
+
+    from mia_train_b200.parallel.tensor_parallel import is_tensor_parallel
+
+    gp = p.grad
+    if not is_tensor_parallel(mod) or p.shape == dense_shape:
+        return gp
+    parts = [torch.empty_like(gp) for _ in range(world)]
+    dist.all_gather(parts, gp.contiguous())
+    if mod._tp_mode == "qkv":
+        per = gp.shape[0] // 3
+        return torch.cat([parts[r][q * per:(q + 1) * per] for q in range(3) for r in range(world)])
+    if mod._tp_mode == "column" or gp.dim() == 1:
+        return torch.cat(parts, dim=0)
+    return torch.cat(parts, dim=1)
+
+
+def _affinity_split_vs_dense(rank, world):
+    import torch.distributed as dist
+
+    from mia_train_b200.algorithms.affinity_seg import AffinitySegmentation
+    from mia_train_b200.data.synthetic import voronoi_volume
+    from mia_train_b200.models.dinov3_vit3d import DinoVisionTransformer3D
+    from mia_train_b200.ops.tp import TpComm
+    from mia_train_b200.parallel.sequence_parallel import SequenceParallel, partial_params, sync_partial_grads
+    from mia_train_b200.parallel.tensor_parallel import apply_tensor_parallel
+
+    torch.manual_seed(0)
+    enc = DinoVisionTransformer3D(img_size=16, patch_size=4, embed_dim=32, depth=2, num_heads=4)
+    dense = AffinitySegmentation(enc, input_axes="lcxyz", offsets="nisb12", decoder="subpixel",
+                                 decoder_hidden_dim=16, decoder_readout_dim=8, decoder_zero_init_output=False,
+                                 split_disconnected=False)
+    tp = copy.deepcopy(dense)
+    group = dist.group.WORLD
+    apply_tensor_parallel(tp.encoder.tensor_parallel_plan(), group)
+    tp.encoder.enable_sequence_parallel(SequenceParallel(TpComm(group, "fused")))
+    imgs, labs = [], []
+    for i in range(2 * world):
+        img, lab = voronoi_volume((16,) * 3, 12, 0.08, 1.0, torch.Generator().manual_seed(i))
+        imgs.append(img)
+        labs.append(lab)
+    batch = {"img": torch.stack(imgs)[:, None, None].float(), "label": torch.stack(labs)[:, None].long()}
+    ref = dense(batch)
+    ref["loss"].backward()
+    out = tp(batch)
+    out["loss"].backward()
+    n_partial = sync_partial_grads(tp)
+    dense_params = dict(dense.named_parameters())
+    worst = 0.0
+    for name, p in tp.named_parameters():
+        rg = dense_params[name].grad
+        if p.grad is None:
+            assert rg is None or float(rg.abs().max()) == 0.0, name
+            continue
+        mod = tp.get_submodule(name.rsplit(".", 1)[0]) if "." in name else tp
+        gp = _gathered_grad(p, mod, world, rg.shape)
+        err = float((gp - rg).norm() / (rg.norm() + 1e-12))
+        worst = max(worst, err)
+        assert err < 1e-4, (name, err)
+    acc = abs(float(out["affinity_accuracy"]) - float(ref["affinity_accuracy"]))
+    return float(out["loss"]), float(ref["loss"]), worst, n_partial, len(partial_params(tp)), acc
+
+
+@pytest.mark.parametrize("world", [2])
+def test_affinity_decoder_split_over_tp_matches_dense(run_distributed, world):
+    """Each TP rank decodes its own samples; loss, metrics and every gradient match the dense model."""
+    res = run_distributed(_affinity_split_vs_dense, world)
+    for loss, ref, worst, n_partial, n_marked, acc in res.values():
+        assert abs(loss - ref) < 1e-5 * max(1.0, abs(ref)), (loss, ref)
+        assert worst < 1e-4
+        assert n_partial == n_marked > 2 * 6  # block norms / LayerScale plus the final norm and decoder
+        assert acc < 1e-6

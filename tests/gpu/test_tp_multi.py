@@ -1,4 +1,4 @@
-"""Tensor parallelism on 2 GPUs with the native kernels against the dense model: replicated
+"""Tensor parallelism on 2 and 4 GPUs with the native kernels against the dense model: replicated
 activations with NCCL all-reduces, and sequence parallelism on NCCL collectives or on the fused
 all-gather -> GEMM / GEMM -> reduce-scatter kernels over NVLink peer memory."""
 
@@ -18,12 +18,18 @@ pytestmark = pytest.mark.gpu
 WORKER = Path(__file__).with_name("tp_worker.py")
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode,port", [("allreduce", 29533), ("collective", 29534), ("fused", 29535)])
-def test_tp_dinov3_matches_dense(mode, port):
+def _gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world,mode,port", [(2, "allreduce", 29533), (2, "collective", 29534), (2, "fused", 29535),
+                                             (4, "collective", 29536), (4, "fused", 29537)])
+def test_tp_dinov3_matches_dense(world, mode, port):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(port), str(WORKER), mode]
+           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(port), str(WORKER), mode]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert out.returncode == 0, out.stderr[-4000:]
     res = json.loads([x for x in out.stdout.splitlines() if x.startswith("{")][-1])
