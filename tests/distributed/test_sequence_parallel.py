@@ -98,7 +98,7 @@ def _gathered_grad(p, mod, world, dense_shape):
     return torch.cat(parts, dim=1)
 
 
-def _affinity_split_vs_dense(rank, world):
+def _affinity_split_vs_dense(rank, world, batch):
     import torch.distributed as dist
 
     from mia_train_b200.algorithms.affinity_seg import AffinitySegmentation
@@ -118,7 +118,7 @@ def _affinity_split_vs_dense(rank, world):
     apply_tensor_parallel(tp.encoder.tensor_parallel_plan(), group)
     tp.encoder.enable_sequence_parallel(SequenceParallel(TpComm(group, "fused")))
     imgs, labs = [], []
-    for i in range(2 * world):
+    for i in range(batch):
         img, lab = voronoi_volume((16,) * 3, 12, 0.08, 1.0, torch.Generator().manual_seed(i))
         imgs.append(img)
         labs.append(lab)
@@ -144,10 +144,11 @@ def _affinity_split_vs_dense(rank, world):
     return float(out["loss"]), float(ref["loss"]), worst, n_partial, len(partial_params(tp)), acc
 
 
-@pytest.mark.parametrize("world", [2])
-def test_affinity_decoder_split_over_tp_matches_dense(run_distributed, world):
-    """Each TP rank decodes its own samples; loss, metrics and every gradient match the dense model."""
-    res = run_distributed(_affinity_split_vs_dense, world)
+@pytest.mark.parametrize("world,batch", [(2, 4), (2, 3)])
+def test_affinity_decoder_split_over_tp_matches_dense(run_distributed, world, batch):
+    """Each TP rank decodes its own samples (an uneven share when the batch does not divide); loss,
+    metrics and every gradient match the dense model."""
+    res = run_distributed(_affinity_split_vs_dense, world, batch)
     for loss, ref, worst, n_partial, n_marked, acc in res.values():
         assert abs(loss - ref) < 1e-5 * max(1.0, abs(ref)), (loss, ref)
         assert worst < 1e-4
