@@ -157,10 +157,14 @@ class IBOTPatchLoss(nn.Module):
                                colsum=None):
         if n_masked_patches is None:
             n_masked_patches = teacher_logits.shape[0]
-        total = torch.tensor(float(n_masked_patches), device=teacher_logits.device, dtype=torch.float32)
-        _all_reduce(total)
-        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations, batch_size=float(total.item()),
-                              colsum=colsum)
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            # the masked patch count of the whole data-parallel batch: one all-reduce and one read
+            total = torch.full((), float(n_masked_patches), device=teacher_logits.device, dtype=torch.float32)
+            _all_reduce(total)
+            count = float(total.item())
+        else:
+            count = float(n_masked_patches)  # known on the host: no device round trip
+        return sinkhorn_knopp(teacher_logits, teacher_temp, n_iterations, batch_size=count, colsum=colsum)
 
     def forward_masked(self, student_logits, teacher_probs, student_masks_flat, n_masked_patches=None,
                        masks_weight=None):

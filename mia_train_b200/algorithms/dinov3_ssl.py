@@ -123,11 +123,20 @@ class DINOv3(BaseAlgorithm):
         self.ibot_loss = IBOTPatchLoss(head_n_prototypes, student_temp=student_temp)
         self.koleo_loss = KoLeoLoss()
         self.register_buffer("_step", torch.zeros((), dtype=torch.long))
+        # host copy of `_step`, so the schedules never read the device; refreshed after a load
+        self._host_step: int | None = None
+        self.register_load_state_dict_post_hook(DINOv3._forget_host_step)
 
     # -- schedules ----------------------------------------------------------------------------
     @property
     def step(self) -> int:
-        return int(self._step.item())
+        if self._host_step is None:
+            self._host_step = int(self._step.item())
+        return self._host_step
+
+    @staticmethod
+    def _forget_host_step(module: nn.Module, incompatible_keys: Any) -> None:
+        module._host_step = None  # type: ignore[attr-defined]
 
     def current_teacher_temp(self, step: int | None = None) -> float:
         step = self.step if step is None else step
@@ -186,10 +195,18 @@ class DINOv3(BaseAlgorithm):
         volumes = backbone.prepare_input(batch[self.input_key], self.input_axes)
         global_views, local_views = self._make_views(volumes)
         b = volumes.shape[0]
-        masks = block_mask(self.global_grid, 2 * b, self.mask_ratio_min_max,
-                           sample_probability=self.mask_sample_probability, device=volumes.device)
+        # the masks are drawn on the host: their count and the masked token indices are known there,
+        # so the step selects masked tokens with index_select and never waits on the device
+        masks_host = block_mask(self.global_grid, 2 * b, self.mask_ratio_min_max,
+                                sample_probability=self.mask_sample_probability)
+        n_masked = int(masks_host.sum())
+        masked_idx_host = masks_host.flatten().nonzero().squeeze(1)
+        if volumes.is_cuda:
+            masks = masks_host.pin_memory().to(volumes.device, non_blocking=True)
+            masked_idx = masked_idx_host.pin_memory().to(volumes.device, non_blocking=True)
+        else:
+            masks, masked_idx = masks_host.to(volumes.device), masked_idx_host.to(volumes.device)
         temp = self.current_teacher_temp()
-        n_masked = int(masks.sum().item())
         with torch.no_grad():
             t_out = self.teacher["backbone"].forward_features(global_views)
             # on CUDA the prototype GEMMs also produce Sinkhorn's first column sums in their epilogue
@@ -199,7 +216,7 @@ class DINOv3(BaseAlgorithm):
                 self.teacher["dino_head"](t_out["x_norm_clstoken"])
             t_cls_probs = self.dino_loss.sinkhorn_knopp_teacher(t_cls_logits, temp, colsum=cls_sum).unflatten(0, (2, b))
             if n_masked > 0:
-                masked_teacher = t_out["x_norm_patchtokens"].flatten(0, 1)[masks.flatten()]
+                masked_teacher = t_out["x_norm_patchtokens"].flatten(0, 1).index_select(0, masked_idx)
                 patch_sum = self._colsum_buffer(self.teacher["ibot_head"], masked_teacher) if fused else None
                 patch_logits = self.teacher["ibot_head"](masked_teacher, patch_sum, temp) if fused else \
                     self.teacher["ibot_head"](masked_teacher)
@@ -219,7 +236,7 @@ class DINOv3(BaseAlgorithm):
         loss = self.dino_loss_weight * (dino_global * (g_terms / total) + dino_local * (l_terms / total))
         metrics = {"dino_global": dino_global.detach(), "dino_local": dino_local.detach()}
         if n_masked > 0:
-            s_masked = self.student["ibot_head"](s_global["x_norm_patchtokens"].flatten(0, 1)[masks.flatten()])
+            s_masked = self.student["ibot_head"](s_global["x_norm_patchtokens"].flatten(0, 1).index_select(0, masked_idx))
             ibot = self.ibot_loss.forward_masked(s_masked, t_patch_probs, masks, n_masked_patches=n_masked)
             loss = loss + self.ibot_loss_weight * ibot
             metrics["ibot"] = ibot.detach()
@@ -229,11 +246,14 @@ class DINOv3(BaseAlgorithm):
             loss = loss + self.koleo_loss_weight * 2 * koleo
             metrics["koleo"] = koleo.detach()
         if train:
+            host_step = self.step
             self._step += 1
+            self._host_step = host_step + 1
+        momentum = self.current_momentum()
         metrics["loss"] = loss
-        metrics["teacher_temp"] = torch.tensor(temp, device=loss.device)
-        metrics["teacher_momentum"] = torch.tensor(self.current_momentum(), device=loss.device)
-        metrics["masked_fraction"] = masks.float().mean()
+        metrics["teacher_temp"] = torch.full((), temp, device=loss.device)
+        metrics["teacher_momentum"] = torch.full((), momentum, device=loss.device)
+        metrics["masked_fraction"] = torch.full((), n_masked / masks_host.numel(), device=loss.device)
         return metrics
 
     def training_step(self, batch: Any) -> dict[str, torch.Tensor]:

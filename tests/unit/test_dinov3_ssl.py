@@ -117,3 +117,38 @@ def test_requires_forward_features():
 
     with pytest.raises(TypeError, match="forward_features"):
         DINOv3(ViT3D(img_size=(16, 16, 16), patch_size=(8, 8, 8), embed_dim=32, depth=1, num_heads=2), input_axes="lcxyz")
+
+
+def test_step_never_reads_device_values(monkeypatch):
+    """After the first step (which reads the checkpointed counter once), a training step makes no
+    `.item()` call: schedules use a host copy of the step, masks and masked token indices are built
+    on the host. On a GPU each such call would stall the launch queue."""
+    torch.manual_seed(0)
+    alg = make_algorithm()
+    batch = {"img": torch.randn(2, 1, 1, 40, 40, 40)}
+    alg(batch)
+    calls = []
+    real = torch.Tensor.item
+
+    def counting(self):
+        calls.append(tuple(self.shape))
+        return real(self)
+
+    monkeypatch.setattr(torch.Tensor, "item", counting)
+    out = alg(batch)
+    out["loss"].backward()
+    alg.after_optimizer_step(2)
+    monkeypatch.setattr(torch.Tensor, "item", real)
+    assert calls == []
+    assert alg.step == int(alg._step) == 2
+
+
+def test_host_step_follows_a_loaded_checkpoint():
+    alg = make_algorithm()
+    alg({"img": torch.randn(2, 1, 1, 40, 40, 40)})
+    assert alg.step == 1
+    state = alg.state_dict()
+    state["_step"] = torch.tensor(7)
+    alg.load_state_dict(state)
+    assert alg.step == 7
+    assert alg.current_teacher_temp() == pytest.approx(alg.current_teacher_temp(7))
