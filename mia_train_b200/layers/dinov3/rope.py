@@ -22,16 +22,34 @@ import torch.nn.functional as F
 NORMALIZE = ("min", "max", "separate")
 
 
-class RopeTables(tuple):
-    """`(sin, cos)` of shape (HW, D_head), plus `.angles` of shape (HW, D_head // 2)."""
+class RopeTables:
+    """`.angles` of shape (HW, D_head // 2), and the `(sin, cos)` pair of shape (HW, D_head) (angles
+    tiled twice) when unpacked or indexed like the reference's tuple; the pair is computed on first
+    use (the native attention only needs the angles).
 
-    angles: torch.Tensor
+    Not a tuple on purpose: FSDP rebuilds tuple forward arguments element by element (and may cast
+    them), which would lose the angles; an object of this class passes through untouched."""
 
-    def __new__(cls, angles: torch.Tensor) -> RopeTables:
-        tiled = angles.tile(2)
-        obj = super().__new__(cls, (torch.sin(tiled), torch.cos(tiled)))
-        obj.angles = angles
-        return obj
+    __slots__ = ("angles", "_pair")
+
+    def __init__(self, angles: torch.Tensor) -> None:
+        self.angles = angles
+        self._pair: tuple[torch.Tensor, torch.Tensor] | None = None
+
+    def _tables(self) -> tuple[torch.Tensor, torch.Tensor]:
+        if self._pair is None:
+            tiled = self.angles.tile(2)
+            self._pair = (torch.sin(tiled), torch.cos(tiled))
+        return self._pair
+
+    def __iter__(self):
+        return iter(self._tables())
+
+    def __getitem__(self, i: int) -> torch.Tensor:
+        return self._tables()[i]
+
+    def __len__(self) -> int:
+        return 2
 
 
 def _axis_coords(sizes: tuple[int, ...], mode: str, dtype, device) -> list[torch.Tensor]:

@@ -224,3 +224,13 @@ def test_trainer_syncs_sequence_parallel_partial_grads(run_distributed, tmp_path
     out = run_distributed(_sp_trainer_syncs, 2, str(tmp_path / "runs"), str(cfg))
     for counts in out.values():
         assert len(counts) == 2 and all(n == 2 * 4 for n in counts), counts  # norm1 / norm2 weight + bias x 2 blocks
+
+
+def test_trainer_syncs_partial_grads_under_tp_and_fsdp(run_distributed, tmp_path):
+    """TP 2 x FSDP dp_shard 2: the partial marks survive FSDP's parameter replacement and the sharded
+    gradients are summed over the TP group."""
+    cfg = tmp_path / "sp_fsdp.toml"
+    cfg.write_text(SP_CONFIG.replace("tp = 2\n", "tp = 2\ndp_shard = 2\n"))
+    out = run_distributed(_sp_trainer_syncs, 4, str(tmp_path / "runs"), str(cfg), timeout=300)
+    for counts in out.values():
+        assert len(counts) == 2 and all(n == 2 * 4 for n in counts), counts
