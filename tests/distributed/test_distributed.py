@@ -234,3 +234,21 @@ def test_trainer_syncs_partial_grads_under_tp_and_fsdp(run_distributed, tmp_path
     out = run_distributed(_sp_trainer_syncs, 4, str(tmp_path / "runs"), str(cfg), timeout=300)
     for counts in out.values():
         assert len(counts) == 2 and all(n == 2 * 4 for n in counts), counts
+
+
+def test_run_then_resume_under_tensor_parallelism(run_distributed, tmp_path):
+    """Checkpoints written under TP 2 (sequence-parallel) hold unsharded tensors and resume onto the
+    same layout."""
+    cfg = tmp_path / "sp.toml"
+    cfg.write_text(SP_CONFIG.replace("max_steps = 2", "max_steps = 3").replace("checkpoint_every = 100",
+                                                                               "checkpoint_every = 2"))
+    root = tmp_path / "runs"
+    out = run_distributed(_run_training, 2, str(root), str(cfg), None)
+    run_dir = Path(out[0])
+    assert any((run_dir / "checkpoints").glob("step_*"))
+    cfg.write_text(SP_CONFIG.replace("max_steps = 2", "max_steps = 4").replace("checkpoint_every = 100",
+                                                                               "checkpoint_every = 2"))
+    out2 = run_distributed(_run_training, 2, str(root), str(cfg), "latest")
+    assert out2[0] == out[0]
+    steps = sorted(int(p.name.split("_")[1]) for p in (run_dir / "checkpoints").glob("step_*") if "tmp" not in p.name)
+    assert steps[-1] == 4
