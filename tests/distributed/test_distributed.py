@@ -252,3 +252,18 @@ def test_run_then_resume_under_tensor_parallelism(run_distributed, tmp_path):
     assert out2[0] == out[0]
     steps = sorted(int(p.name.split("_")[1]) for p in (run_dir / "checkpoints").glob("step_*") if "tmp" not in p.name)
     assert steps[-1] == 4
+
+
+def test_trainer_affinity_decoder_split_under_tensor_parallelism(run_distributed, tmp_path):
+    """affinity_seg under TP 2 through the Trainer: each rank decodes its own sample, so the decoder
+    and final-norm gradients join the TP sum next to the blocks' norms."""
+    cfg = tmp_path / "aff.toml"
+    text = SP_CONFIG.replace('name = "simmim"\nmask_ratio = 0.5',
+                             'name = "affinity_seg"\ndecoder = "subpixel"\noffsets = "nisb12"\n'
+                             'decoder_hidden_dim = 16\ndecoder_readout_dim = 8\nsplit_disconnected = false')
+    text = text.replace('shape = [16, 16, 16]', 'shape = [16, 16, 16]\ngenerator = "voronoi"\nn_seeds = 12')
+    text = text.replace("batch_size = 1", "batch_size = 2")
+    cfg.write_text(text)
+    out = run_distributed(_sp_trainer_syncs, 2, str(tmp_path / "runs"), str(cfg))
+    for counts in out.values():
+        assert len(counts) == 2 and all(n > 2 * 4 for n in counts), counts
