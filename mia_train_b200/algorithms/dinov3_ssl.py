@@ -123,20 +123,20 @@ class DINOv3(BaseAlgorithm):
         self.ibot_loss = IBOTPatchLoss(head_n_prototypes, student_temp=student_temp)
         self.koleo_loss = KoLeoLoss()
         self.register_buffer("_step", torch.zeros((), dtype=torch.long))
-        # host copy of `_step`, so the schedules never read the device; refreshed after a load
-        self._host_step: int | None = None
-        self.register_load_state_dict_post_hook(DINOv3._forget_host_step)
+        # host copy of `_step` (value, buffer identity, in-place version), so the schedules never read
+        # the device; any other write to the buffer (a checkpoint load, a measurement step that
+        # restores buffers) changes its identity or version and forces one read
+        self._host_step: tuple[int, int, int] | None = None
 
     # -- schedules ----------------------------------------------------------------------------
     @property
     def step(self) -> int:
-        if self._host_step is None:
-            self._host_step = int(self._step.item())
-        return self._host_step
-
-    @staticmethod
-    def _forget_host_step(module: nn.Module, incompatible_keys: Any) -> None:
-        module._host_step = None  # type: ignore[attr-defined]
+        buf = self._step
+        cached = self._host_step
+        if cached is None or cached[1] != id(buf) or cached[2] != buf._version:
+            cached = (int(buf.item()), id(buf), buf._version)
+            self._host_step = cached
+        return cached[0]
 
     def current_teacher_temp(self, step: int | None = None) -> float:
         step = self.step if step is None else step
@@ -248,7 +248,7 @@ class DINOv3(BaseAlgorithm):
         if train:
             host_step = self.step
             self._step += 1
-            self._host_step = host_step + 1
+            self._host_step = (host_step + 1, id(self._step), self._step._version)
         momentum = self.current_momentum()
         metrics["loss"] = loss
         metrics["teacher_temp"] = torch.full((), temp, device=loss.device)

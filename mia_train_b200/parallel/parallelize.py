@@ -85,6 +85,20 @@ def _entry_points(model: nn.Module) -> tuple[str, ...]:
     return model.extra_forward_methods() if isinstance(model, BaseModel) else ()
 
 
+def _shard_unit(module: nn.Module, mesh: DeviceMesh, dims: ParallelDims) -> None:
+    """Shard `module` as one FSDP unit, registering a model's extra entry points. A container without
+    a forward of its own (a `ModuleDict` such as a teacher's backbone and heads) cannot be a unit:
+    each of its children with parameters is sharded instead."""
+    if type(module).forward is nn.Module.forward:
+        for child in module.children():
+            if any(True for _ in child.parameters()):
+                _shard_unit(child, mesh, dims)
+        return
+    if _shard(module, mesh, dims):
+        for name in _entry_points(module):
+            register_fsdp_forward_method(module, name)
+
+
 def _shard_blocks(root: nn.Module, mesh: DeviceMesh, dims: ParallelDims) -> int:
     """Shard every declared block (model's and algorithm's) as its own FSDP2 unit."""
     if dims.fsdp_unit != "block" or _dp_mesh(mesh, dims) is None:
@@ -132,7 +146,7 @@ def parallelize_algorithm(algorithm: BaseAlgorithm, mesh: DeviceMesh, dims: Para
     extra = getattr(algorithm, "extra_sharded_modules", None)
     if extra is not None:
         for module in extra():
-            _shard(module, mesh, dims)
+            _shard_unit(module, mesh, dims)
     if _shard(algorithm, mesh, dims):
         register_fsdp_forward_method(algorithm, "validation_step")
     elif dims.dp_replicate > 1:

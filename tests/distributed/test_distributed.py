@@ -267,3 +267,77 @@ def test_trainer_affinity_decoder_split_under_tensor_parallelism(run_distributed
     out = run_distributed(_sp_trainer_syncs, 2, str(tmp_path / "runs"), str(cfg))
     for counts in out.values():
         assert len(counts) == 2 and all(n > 2 * 4 for n in counts), counts
+
+
+DINO_CONFIG = """
+experiment_name = "dino"
+
+[model]
+name = "dinov3_vit3d"
+img_size = 16
+patch_size = 4
+embed_dim = 32
+depth = 2
+num_heads = 2
+
+[algorithm]
+name = "dinov3"
+global_crop_size = 16
+local_crop_size = 8
+n_local_crops = 2
+head_n_prototypes = 64
+head_hidden_dim = 32
+head_bottleneck_dim = 16
+total_steps = 10
+warmup_teacher_temp_steps = 4
+
+[data]
+name = "synthetic_volumes"
+shape = [24, 24, 24]
+samples_per_epoch = 16
+
+[trainer]
+max_steps = {steps}
+batch_size = 2
+lr = 1e-3
+warmup_steps = 1
+precision = "fp32"
+log_every = 1
+checkpoint_every = 2
+seed = 0
+
+[parallelism]
+dp_shard = 2
+"""
+
+
+def _dino_steps_seen(rank, world, root, config_path, resume):
+    """Run training and record the algorithm's step counter at the start of every training step."""
+    from mia_train_b200.algorithms.dinov3_ssl import DINOv3
+    from mia_train_b200.engine.run import run
+
+    seen = []
+    real = DINOv3._step_impl
+
+    def recording(self, batch, train):
+        if train:
+            seen.append(self.step)
+        return real(self, batch, train)
+
+    DINOv3._step_impl = recording
+    run(Path(config_path), output_root=Path(root), resume=resume)
+    return seen
+
+
+def test_dinov3_step_counter_survives_resume_under_fsdp(run_distributed, tmp_path):
+    """DINOv3 trains under FSDP (its teacher, a container, is sharded child by child) and its step
+    counter - hence the teacher temperature and momentum schedules - resumes where it stopped."""
+    cfg = tmp_path / "dino.toml"
+    cfg.write_text(DINO_CONFIG.format(steps=2))
+    root = tmp_path / "runs"
+    first = run_distributed(_dino_steps_seen, 2, str(root), str(cfg), None)
+    # the first call of each run is the FLOP measurement, which restores the counter afterwards
+    assert all(v[-2:] == [0, 1] for v in first.values()), first
+    cfg.write_text(DINO_CONFIG.format(steps=4))
+    second = run_distributed(_dino_steps_seen, 2, str(root), str(cfg), "latest")
+    assert all(v[-2:] == [2, 3] for v in second.values()), second
