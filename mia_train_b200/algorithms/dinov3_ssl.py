@@ -170,6 +170,11 @@ class DINOv3(BaseAlgorithm):
     def checkpointable_modules(self) -> tuple[nn.Module, ...]:
         return ()
 
+    def extra_tensor_parallel_models(self) -> tuple[nn.Module, ...]:
+        """The teacher backbone takes the student's tensor-parallel layout, so the EMA pairs
+        matching shards."""
+        return (self.teacher["backbone"],)
+
     def extra_sharded_modules(self) -> tuple[nn.Module, ...]:
         """Shard the teacher backbone and heads as their own FSDP units (used by parallelize)."""
         return (self.teacher,)

@@ -75,6 +75,12 @@ class VoxelHead(nn.Sequential):
 
     def forward(self, x: torch.Tensor, size: tuple[int, ...]) -> torch.Tensor:  # type: ignore[override]
         x = self.upsample(x, tuple(size))
+        if not torch.is_autocast_enabled(x.device.type):
+            # the upsampling ran in fp32; the layers may hold lower-precision parameters (FSDP's
+            # compute dtype) and there is no autocast to cast the input for them
+            w = next((p for p in self.parameters() if p.is_floating_point()), None)
+            if w is not None and w.dtype != x.dtype:
+                x = x.to(w.dtype)
         for layer in self:
             x = layer(x)
         return x

@@ -139,6 +139,9 @@ def parallelize_model(model: nn.Module, mesh: DeviceMesh, dims: ParallelDims) ->
 def parallelize_algorithm(algorithm: BaseAlgorithm, mesh: DeviceMesh, dims: ParallelDims) -> BaseAlgorithm:
     """Parallelize a strategy and its model; the algorithm is the outer FSDP unit."""
     _apply_tensor_parallel(algorithm.model, mesh, dims)
+    # models that must share the main model's tensor-parallel layout (a teacher updated from it)
+    for extra_model in getattr(algorithm, "extra_tensor_parallel_models", lambda: ())():
+        _apply_tensor_parallel(extra_model, mesh, dims)
     _shard_blocks(algorithm, mesh, dims)
     if _shard(algorithm.model, mesh, dims):
         for name in _entry_points(algorithm.model):

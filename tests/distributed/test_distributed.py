@@ -341,3 +341,24 @@ def test_dinov3_step_counter_survives_resume_under_fsdp(run_distributed, tmp_pat
     cfg.write_text(DINO_CONFIG.format(steps=4))
     second = run_distributed(_dino_steps_seen, 2, str(root), str(cfg), "latest")
     assert all(v[-2:] == [2, 3] for v in second.values()), second
+
+
+def test_dinov3_trains_under_tensor_parallelism(run_distributed, tmp_path):
+    """The teacher backbone takes the student's TP layout, so the EMA pairs matching shards."""
+    cfg = tmp_path / "dino_tp.toml"
+    cfg.write_text(DINO_CONFIG.format(steps=2).replace("dp_shard = 2", 'tp = 2\ntp_comm = "collective"'))
+    out = run_distributed(_dino_steps_seen, 2, str(tmp_path / "runs"), str(cfg), None)
+    assert all(v[-2:] == [0, 1] for v in out.values()), out
+
+
+def test_affinity_interpolate_decoder_under_fsdp(run_distributed, tmp_path):
+    """The voxel head's fp32 upsampling output meets FSDP's low-precision compute parameters."""
+    cfg = tmp_path / "aff_fsdp.toml"
+    text = CONFIG.format(steps=2, parallelism="dp_shard = 2")
+    text = text.replace('name = "mae"\nmask_ratio = 0.5\ndecoder_embed_dim = 16\ndecoder_depth = 1\ndecoder_num_heads = 2',
+                        'name = "affinity_seg"\nsplit_disconnected = false')
+    text = text.replace('shape = [16, 16, 16]', 'shape = [16, 16, 16]\ngenerator = "voronoi"\nn_seeds = 12')
+    assert 'name = "affinity_seg"' in text
+    cfg.write_text(text)
+    out = run_distributed(_run_training, 2, str(tmp_path / "runs"), str(cfg), None)
+    assert len(set(out.values())) == 1
