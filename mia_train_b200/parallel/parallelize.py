@@ -38,6 +38,13 @@ from .tensor_parallel import BlockTensorParallelPlan, apply_tensor_parallel
 def _apply_tensor_parallel(model: nn.Module, mesh: DeviceMesh, dims: ParallelDims) -> None:
     if not dims.tp_enabled:
         return
+    adapted = [name for name, m in model.named_modules() if hasattr(m, "lora_a")]
+    if adapted:
+        # the tensor-parallel block paths read the base weights and would skip the adapters
+        raise ValueError(
+            f"[lora] adapters ({adapted[0]}, ... {len(adapted)} layers) cannot be combined with tensor "
+            f"parallelism (tp = {dims.tp}): train the adapters with data parallelism (dp_shard / dp_replicate)"
+        )
     plan = model.tensor_parallel_plan() if isinstance(model, BaseModel) else None
     if plan is None:
         raise ValueError(

@@ -362,3 +362,22 @@ def test_affinity_interpolate_decoder_under_fsdp(run_distributed, tmp_path):
     cfg.write_text(text)
     out = run_distributed(_run_training, 2, str(tmp_path / "runs"), str(cfg), None)
     assert len(set(out.values())) == 1
+
+
+def _lora_under_tp(rank, world, root, config_path):
+    from mia_train_b200.engine.run import run
+
+    try:
+        run(Path(config_path), output_root=Path(root), resume=None)
+    except ValueError as error:
+        return str(error)
+    return "no error"
+
+
+def test_lora_with_tensor_parallelism_is_refused(run_distributed, tmp_path):
+    """The sequence-parallel blocks read the base weights: LoRA under TP must fail loudly rather
+    than train without its adapters."""
+    cfg = tmp_path / "lora_tp.toml"
+    cfg.write_text(SP_CONFIG + '\n[lora]\nrank = 4\nalpha = 8.0\ntargets = ["attn_qkv"]\n')
+    out = run_distributed(_lora_under_tp, 2, str(tmp_path / "runs"), str(cfg))
+    assert all("cannot be combined with tensor parallelism" in v for v in out.values()), out
