@@ -23,6 +23,7 @@ from ..common.layer_scale import LayerScale
 from ..common.rms_norm import RMSNorm
 from .attention import SelfAttention
 from .ffn import Mlp, SwiGLUFFN
+from .rope import RopeTables
 
 
 def _norm(module: nn.Module, x: torch.Tensor) -> torch.Tensor:
@@ -71,8 +72,8 @@ class SelfAttentionBlock(nn.Module):
 
     @staticmethod
     def _maybe_index_rope(rope, indices):
-        if rope is None:
-            return None
+        if rope is None or isinstance(rope, RopeTables):
+            return rope  # per-token angles shared by every sample: nothing to select
         sin, cos = rope
         if sin.ndim == 4:
             return sin[indices], cos[indices]
@@ -100,7 +101,7 @@ class SelfAttentionBlock(nn.Module):
         flat, shapes, counts = cat_keep_shapes(sub1)
         res1 = self.attn.forward_list(uncat_with_shapes(_norm(self.norm1, flat), shapes, counts), rope_list=ropes)
         x_attn = [
-            torch.index_add(x, 0, self.ls1(r), i, alpha=a)
+            torch.index_add(x, 0, index=i, source=self.ls1(r).to(x.dtype), alpha=a)
             for x, r, i, a in zip(x_list, res1, idx1, scales, strict=True)
         ]
         idx2 = [torch.randperm(b, device=x.device)[:s] for x, b, s in zip(x_list, sizes, subsets, strict=True)]
@@ -108,7 +109,7 @@ class SelfAttentionBlock(nn.Module):
         flat, shapes, counts = cat_keep_shapes(sub2)
         res2 = self.mlp.forward_list(uncat_with_shapes(_norm(self.norm2, flat), shapes, counts))
         return [
-            torch.index_add(x, 0, self.ls2(r), i, alpha=a)
+            torch.index_add(x, 0, index=i, source=self.ls2(r).to(x.dtype), alpha=a)
             for x, r, i, a in zip(x_attn, res2, idx2, scales, strict=True)
         ]
 

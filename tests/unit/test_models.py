@@ -76,6 +76,41 @@ def test_dinov3_2d():
     assert out["x_norm_patchtokens"].shape == (2, 4, 32)
 
 
+def test_block_drop_path_passes_rope_tables_through():
+    """A block with drop_path > 0 in training runs the sample-subset path; with one sample the
+    subset is that sample at scale 1, so the output must equal the plain (eval) path, and the shared
+    per-token RoPE angles must reach the attention unchanged."""
+    from mia_train_b200.layers.dinov3.block import SelfAttentionBlock
+    from mia_train_b200.layers.dinov3.rope import RopePositionEmbedding3D, RopeTables
+
+    torch.manual_seed(0)
+    block = SelfAttentionBlock(32, 2, drop_path=0.5, init_values=0.5)
+    rope = RopePositionEmbedding3D(32, num_heads=2)(D=2, H=2, W=2)
+    assert isinstance(rope, RopeTables) and rope.angles.shape[0] == 8
+    x = torch.randn(1, 9, 32)  # one prefix token + 8 patch tokens
+    block.train()
+    dropped = block(x, rope)
+    block.eval()
+    plain = block(x, rope)
+    torch.testing.assert_close(dropped, plain)
+    no_rope = block(x, None)
+    assert not torch.allclose(plain, no_rope)
+
+    # four samples, half of them per branch: the update lands on the drawn rows, scaled by 4 / 2
+    x4 = torch.randn(4, 9, 32)
+    block.train()
+    torch.manual_seed(5)
+    out = block(x4, rope)
+    torch.manual_seed(5)
+    i1, i2 = torch.randperm(4)[:2], torch.randperm(4)[:2]
+    with torch.no_grad():
+        mid = x4.clone()
+        mid[i1] += 2 * block.ls1(block.attn(block.norm1(x4[i1]), rope=rope))
+        ref = mid.clone()
+        ref[i2] += 2 * block.ls2(block.mlp(block.norm2(mid[i2])))
+    torch.testing.assert_close(out, ref)
+
+
 def test_registry_builds_every_model():
     for name, kw in {
         "vit3d": dict(img_size=(16, 16, 16), patch_size=(8, 8, 8), embed_dim=32, depth=1, num_heads=2),
