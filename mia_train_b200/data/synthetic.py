@@ -13,6 +13,14 @@ each deterministic in `(seed, index)`:
 
 Samples are `{"img": (1, 1, X, Y, Z) float32}` with `sample_axes = "lcxyz"`; the voronoi generator
 adds `"label": (1, X, Y, Z) int64`.
+
+`levels = [1, 4, 16]` (finest first, each a whole multiple of the previous) makes a scale pyramid
+for multi-level encoders (`muvit3d`): `"img"` is (L, 1, X, Y, Z), level l covering `levels[l]`
+times the field of view of level 0 at the same voxel shape, and `"bbox"` is (L, 2, 3) float32,
+the concentric world-coordinate box of each level (voxels of level 0, centred on a random offset).
+The coarsest level is drawn by the generator; each finer level is the central `1 / ratio` crop of
+the next coarser one upsampled trilinearly, plus fresh detail from the same generator, so the
+levels agree where they overlap. Multi-level sampling takes the noise and blobs generators.
 """
 
 from __future__ import annotations
@@ -119,6 +127,31 @@ def voronoi_volume(
     return gaussian_blur3d(image, sigma), labels
 
 
+def _draw(s: dict[str, Any], shape: tuple[int, int, int], gen: torch.Generator) -> torch.Tensor:
+    if s["generator"] == "noise":
+        return noise_volume(shape, float(s["sigma"]), gen)
+    return blobs_volume(shape, float(s["sigma"]), float(s["blob_rate"]), tuple(s["blob_radii"]), gen)
+
+
+def pyramid(s: dict[str, Any], gen: torch.Generator) -> tuple[torch.Tensor, torch.Tensor]:
+    """(L, X, Y, Z) levels, finest first, and their (L, 2, 3) concentric boxes."""
+    shape = tuple(int(v) for v in s["shape"])
+    levels = tuple(int(v) for v in s["levels"])
+    out = [_draw(s, shape, gen)]  # the coarsest level
+    for fine, coarse in zip(reversed(levels[:-1]), reversed(levels[1:]), strict=True):
+        ratio = coarse // fine
+        crop = [n // ratio for n in shape]
+        lo = [(n - c) // 2 for n, c in zip(shape, crop, strict=True)]
+        centre = out[-1][lo[0]:lo[0] + crop[0], lo[1]:lo[1] + crop[1], lo[2]:lo[2] + crop[2]]
+        up = F.interpolate(centre[None, None], size=shape, mode="trilinear", align_corners=False)[0, 0]
+        out.append(_zscore(up + _draw(s, shape, gen)))
+    volumes = torch.stack(out[::-1])
+    offset = (torch.rand(3, generator=gen) - 0.5) * 2.0 * max(shape)
+    half = torch.tensor([[lv * (n / 2 - 0.5) for n in shape] for lv in levels], dtype=torch.float32)
+    bbox = torch.stack((offset - half, offset + half), dim=1)
+    return volumes, bbox
+
+
 class _SyntheticSource(data.Dataset):
     def __init__(self, settings: dict[str, Any]) -> None:
         self.s = settings
@@ -131,6 +164,9 @@ class _SyntheticSource(data.Dataset):
         gen = torch.Generator().manual_seed(int(s["seed"]) * 1_000_003 + int(index))
         shape = tuple(int(v) for v in s["shape"])
         sample: dict[str, Any] = {}
+        if len(s["levels"]) > 1:
+            volumes, bbox = pyramid(s, gen)
+            return {"img": volumes[:, None].contiguous(), "bbox": bbox}
         if s["generator"] == "noise":
             img = noise_volume(shape, float(s["sigma"]), gen)
         elif s["generator"] == "blobs":
@@ -155,6 +191,7 @@ class SyntheticVolumes(BaseDataset):
         blob_radii: tuple[float, float] = (2.0, 8.0),
         n_seeds: int = 300,
         noise: float = 0.08,
+        levels: tuple[int, ...] = (1,),
     ) -> None:
         super().__init__()
         self.settings = self.resolve_settings(
@@ -167,6 +204,7 @@ class SyntheticVolumes(BaseDataset):
             blob_radii=blob_radii,
             n_seeds=n_seeds,
             noise=noise,
+            levels=levels,
         )
 
     @classmethod
@@ -181,6 +219,7 @@ class SyntheticVolumes(BaseDataset):
             "blob_radii": (2.0, 8.0),
             "n_seeds": 300,
             "noise": 0.08,
+            "levels": (1,),
         }
         unknown = sorted(set(kwargs) - set(defaults))
         if unknown:
@@ -192,6 +231,16 @@ class SyntheticVolumes(BaseDataset):
         if len(out["shape"]) != 3 or min(out["shape"]) < 1:
             raise ValueError(f"shape must be three positive extents, got {out['shape']}")
         out["blob_radii"] = tuple(float(v) for v in out["blob_radii"])
+        levels = tuple(int(v) for v in out["levels"])
+        if not levels or levels[0] < 1 or any(b <= a or b % a for a, b in zip(levels, levels[1:], strict=False)):
+            raise ValueError(f"levels must be increasing, each a whole multiple of the previous; got {levels}")
+        if len(levels) > 1:
+            if out["generator"] == "voronoi":
+                raise ValueError("multi-level samples take the noise or blobs generator")
+            ratio = max(b // a for a, b in zip(levels, levels[1:], strict=False))
+            if any(n % ratio for n in out["shape"]):
+                raise ValueError(f"shape {out['shape']} must divide by the level ratio {ratio}")
+        out["levels"] = levels
         if int(out["samples_per_epoch"]) < 1:
             raise ValueError("samples_per_epoch must be >= 1")
         return out

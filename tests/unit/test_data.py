@@ -27,6 +27,34 @@ def test_synthetic_rejects_unknown():
         SyntheticVolumes.resolve_settings(bogus=1)
 
 
+def test_synthetic_pyramid_levels_agree_and_boxes_are_concentric():
+    ds = SyntheticVolumes(generator="noise", shape=(16, 16, 16), levels=(1, 2, 8), samples_per_epoch=2, seed=3)
+    sample = ds.dataset[1]
+    img, bbox = sample["img"], sample["bbox"]
+    assert img.shape == (3, 1, 16, 16, 16) and bbox.shape == (3, 2, 3)
+    torch.testing.assert_close(ds.dataset[1]["img"], img)  # deterministic in (seed, index)
+    centres = bbox.mean(dim=1)
+    torch.testing.assert_close(centres, centres[:1].expand(3, 3))
+    spans = bbox[:, 1] - bbox[:, 0]
+    torch.testing.assert_close(spans, torch.tensor([[1.0], [2.0], [8.0]]) * 15.0 * torch.ones(3, 3))
+    # level 0 is level 1's central half, upsampled, plus fresh detail: the two correlate
+    centre = img[1, 0, 4:12, 4:12, 4:12]
+    up = torch.nn.functional.interpolate(centre[None, None], size=(16, 16, 16), mode="trilinear")[0, 0]
+    corr = torch.corrcoef(torch.stack((img[0, 0].flatten(), up.flatten())))[0, 1]
+    assert corr > 0.2
+
+
+def test_synthetic_levels_validation():
+    with pytest.raises(ValueError, match="levels"):
+        SyntheticVolumes(levels=(1, 3, 4))
+    with pytest.raises(ValueError, match="levels"):
+        SyntheticVolumes(levels=(2, 1))
+    with pytest.raises(ValueError, match="noise or blobs"):
+        SyntheticVolumes(generator="voronoi", levels=(1, 2))
+    with pytest.raises(ValueError, match="divide"):
+        SyntheticVolumes(shape=(30, 32, 32), levels=(1, 4))
+
+
 def test_dataloader_shards_by_dp_rank():
     ds = SyntheticVolumes(shape=(8, 8, 8), samples_per_epoch=8)
     loaders = [ds.build_dataloader(batch_size=2, rank=r, world_size=2, num_workers=0, shuffle=False)
