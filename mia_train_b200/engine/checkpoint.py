@@ -23,6 +23,7 @@ import torch.distributed as dist
 import torch.distributed.checkpoint as dcp
 import torch.nn as nn
 from torch.distributed.checkpoint.state_dict import (
+    StateDictOptions,
     get_model_state_dict,
     get_optimizer_state_dict,
     set_model_state_dict,
@@ -58,6 +59,21 @@ class TrainState(Stateful):
 
 def _is_complete(path: Path) -> bool:
     return path.is_dir() and not path.name.endswith(_TMP_SUFFIX) and (path / ".metadata").is_file()
+
+
+def _drop_unsaved_optimizer_state(optim_state: dict[str, Any], path: Path) -> list[str]:
+    """A fresh optimizer holds (zero) state for every trainable parameter, a saved one only for the
+    parameters that had a gradient by then (an adapter or token that no loss reached yet). Drop the
+    entries the checkpoint lacks, so those parameters resume as they were saved: without state."""
+    saved = set(dcp.FileSystemReader(str(path)).read_metadata().state_dict_metadata)
+    per_param = optim_state.get("state", {})
+    unsaved = [fqn for fqn, entry in per_param.items() if any(f"optim.state.{fqn}.{k}" not in saved for k in entry)]
+    for fqn in unsaved:
+        del per_param[fqn]
+    if unsaved:
+        logger.warning("checkpoint %s has no optimizer state for %d parameter(s) (no gradient before it was "
+                       "saved); they resume without state: %s", path, len(unsaved), ", ".join(unsaved[:8]))
+    return unsaved
 
 
 class CheckpointManager:
@@ -126,7 +142,9 @@ class CheckpointManager:
     def _load(self, path: Path) -> int:
         train_state = TrainState()
         state = self._state_dict(train_state)
+        unsaved = _drop_unsaved_optimizer_state(state["optim"], path)
         dcp.load(state, checkpoint_id=str(path), process_group=self._process_group)
         set_model_state_dict(self._module, state["model"])
-        set_optimizer_state_dict(self._module, self._optimizer, state["optim"])
+        set_optimizer_state_dict(self._module, self._optimizer, state["optim"],
+                                 options=StateDictOptions(strict=not unsaved))
         return train_state.step

@@ -13,6 +13,7 @@ fused-epilogue GEMM on the base weight and, for an adapted module, adds the low-
 from __future__ import annotations
 
 import math
+from typing import Any
 
 import torch
 import torch.nn as nn
@@ -87,34 +88,41 @@ def merge_all(root: nn.Module) -> list[str]:
     return merged
 
 
+_OWN_BIAS = object()
+
+
 def apply_linear(
     module: nn.Linear,
     x: torch.Tensor,
     activation: str | None = None,
     residual: torch.Tensor | None = None,
     gamma: torch.Tensor | None = None,
+    bias: Any = _OWN_BIAS,
 ) -> torch.Tensor:
-    """`residual + gamma * act(module(x))` with the epilogue fused into the native GEMM."""
+    """`residual + gamma * act(module(x))` with the epilogue fused into the native GEMM; `bias`
+    replaces the module's own bias (a masked-key-bias qkv passes its masked bias), adapter included."""
+    b = module.bias if bias is _OWN_BIAS else bias
     if hasattr(module, "_tp_mode"):  # a tensor-parallel shard: local GEMM plus its collective
         from ...parallel.tensor_parallel import tp_linear
 
-        return tp_linear(module, x, activation=activation, residual=residual, gamma=gamma)
+        extra = {} if bias is _OWN_BIAS else {"bias": b}
+        return tp_linear(module, x, activation=activation, residual=residual, gamma=gamma, **extra)
     if isinstance(module, LoRAMixin):
         if gamma is None:
             from ...ops.linear import lora_linear
 
-            fused = lora_linear(x, module.weight, module.bias, module.lora_a, module.lora_b,
+            fused = lora_linear(x, module.weight, b, module.lora_a, module.lora_b,
                                 float(module.lora_scaling), activation=activation, residual=residual)
             if fused is not None:
                 return fused
-        y = linear(x, module.weight, module.bias)
+        y = linear(x, module.weight, b)
         y = y + module.lora_forward(x).to(y.dtype)
         if activation == "gelu":
             y = F.gelu(y)
         if gamma is not None:
             y = y * gamma
         return y if residual is None else residual + y
-    return linear(x, module.weight, module.bias, activation=activation, residual=residual, gamma=gamma)
+    return linear(x, module.weight, b, activation=activation, residual=residual, gamma=gamma)
 
 
 def is_adapted(module: nn.Module) -> bool:

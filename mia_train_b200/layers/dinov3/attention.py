@@ -99,13 +99,8 @@ class SelfAttention(nn.Module):
     # -- projections ----------------------------------------------------------------------
     def _qkv(self, x: torch.Tensor) -> torch.Tensor:
         if isinstance(self.qkv, LinearKMaskedBias) and self.qkv.bias is not None:
-            if hasattr(self.qkv, "_tp_mode"):
-                from ...parallel.tensor_parallel import tp_linear
-
-                return tp_linear(self.qkv, x, bias=self.qkv.masked_bias())
-            from ...ops.linear import linear
-
-            return linear(x, self.qkv.weight, self.qkv.masked_bias())
+            # the masked key bias replaces the layer's bias on every path (LoRA adapter included)
+            return apply_linear(self.qkv, x, bias=self.qkv.masked_bias())
         return apply_linear(self.qkv, x)
 
     def _pairs_on(self, device: torch.device) -> torch.Tensor:

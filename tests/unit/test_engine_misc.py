@@ -46,6 +46,35 @@ def test_checkpoint_roundtrip_and_latest(tmp_path):
         CheckpointManager(m2, opt2, tmp_path).load_step(5)
 
 
+def test_resume_with_a_parameter_that_never_had_a_gradient(tmp_path):
+    """A trainable parameter no loss has reached yet has no optimizer state in the checkpoint; the
+    resume loads everything else and leaves that parameter without state, as it was saved."""
+
+    class TwoHeads(nn.Module):
+        def __init__(self) -> None:
+            super().__init__()
+            self.used = nn.Linear(4, 4)
+            self.unused = nn.Linear(4, 4)  # e.g. a head whose loss term has not fired yet
+
+    def build():
+        m = TwoHeads()
+        return m, build_optimizer(m, TrainerConfig(max_steps=5, batch_size=1, fused_optimizer="off"))
+
+    torch.manual_seed(0)
+    m, opt = build()
+    m.used(torch.randn(2, 4)).sum().backward()
+    opt.step()
+    CheckpointManager(m, opt, tmp_path).save(1)
+    m2, opt2 = build()
+    assert CheckpointManager(m2, opt2, tmp_path).load_latest() == 1
+    torch.testing.assert_close(m2.used.weight, m.used.weight)
+    state = opt2.state_dict()["state"]
+    saved = opt.state_dict()["state"]
+    assert len(state) == len(saved) == 2  # used.weight and used.bias only
+    m2.used(torch.randn(2, 4)).sum().backward()
+    opt2.step()  # the resumed optimizer steps normally
+
+
 def test_activation_checkpointing_wraps_declared_blocks():
     alg = MAE(vit(), input_axes="lcxyz", decoder_embed_dim=16, decoder_depth=1, decoder_num_heads=2)
     targets = checkpointable_targets(alg)
@@ -79,6 +108,32 @@ def test_lora_freezes_base_and_trains_adapters():
     assert torch.isfinite(y0).all()
     with pytest.raises(ValueError):
         apply_lora(vit(), LoRAConfig(rank=4, alpha=8.0, targets=("nope",)))
+
+
+@pytest.mark.parametrize("mask_k_bias", [False, True])
+def test_lora_adapters_train_on_every_dinov3_target(mask_k_bias):
+    """Every adapted layer of a DINOv3 encoder is in the graph (a masked-key-bias qkv included), and
+    the adapted forward equals the forward of the merged weights."""
+    torch.manual_seed(0)
+    m = DinoVisionTransformer3D(img_size=16, patch_size=8, embed_dim=32, depth=2, num_heads=2,
+                                qkv_bias=True, mask_k_bias=mask_k_bias)
+    apply_lora(m, LoRAConfig(rank=4, alpha=8.0, targets=("attn_qkv", "attn_proj", "mlp")))
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if name.endswith("lora_b"):
+                p.normal_(0.0, 0.5)  # a trained adapter: its delta changes the output
+    x = torch.randn(2, 1, 16, 16, 16)
+    out = m.forward_features(x)["x_norm_patchtokens"]
+    out.square().mean().backward()
+    adapters = {n: p for n, p in m.named_parameters() if "lora_" in n}
+    assert len(adapters) == 2 * 2 * 4  # 2 blocks x (qkv, proj, fc1, fc2) x (A, B)
+    for name, p in adapters.items():
+        assert p.grad is not None and p.grad.abs().sum() > 0, name
+    with torch.no_grad():
+        for module in m.modules():
+            if hasattr(module, "merge_lora"):
+                module.merge_lora()
+        torch.testing.assert_close(m.forward_features(x)["x_norm_patchtokens"], out.detach(), atol=1e-5, rtol=1e-4)
 
 
 def test_flop_counter_sees_attention():
