@@ -41,7 +41,7 @@ from ..data.base import BaseDataset
 from ..ops._native import raise_on_device_errors
 from ..parallel.sequence_parallel import sync_partial_grads
 from ..parallel.parallel_dims import ParallelDims
-from ..parallel.parallelize import parallelize_algorithm
+from ..parallel.parallelize import parallelize_algorithm, refresh_fsdp_grad_dtypes
 from ..utils.device import move_to_device
 from ..utils.hardware_flops import peak_flops
 from ..utils.metrics import MetricLogger, reduce_metrics
@@ -184,6 +184,7 @@ class Trainer:
         params = self._backbone_parameters()
         for _, p in params:
             p.requires_grad_(not frozen)
+        refresh_fsdp_grad_dtypes(self.algorithm)
         if self.is_primary:
             count = sum(p.numel() for _, p in params)
             print(

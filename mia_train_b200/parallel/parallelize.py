@@ -162,3 +162,20 @@ def parallelize_algorithm(algorithm: BaseAlgorithm, mesh: DeviceMesh, dims: Para
     elif dims.dp_replicate > 1:
         replicate(algorithm, device_mesh=mesh["dp_replicate"])
     return algorithm
+
+
+def refresh_fsdp_grad_dtypes(root: nn.Module) -> int:
+    """Re-derive every FSDP2 unit's gradient dtypes after `requires_grad` changed.
+
+    FSDP2 takes a unit's reduce and original dtypes from the parameters that require grad when it
+    first runs; a unit whose parameters were all frozen then (a backbone frozen for the first
+    steps) keeps none, so once unfrozen it reduces gradients in the bf16 compute dtype and assigns
+    them to fp32 parameters, which autograd refuses. Returns the number of units refreshed."""
+    count = 0
+    for module in root.modules():
+        get_state = getattr(module, "_get_fsdp_state", None)
+        group = getattr(get_state(), "_fsdp_param_group", None) if get_state is not None else None
+        if group is not None:
+            group._init_mp_dtypes()
+            count += 1
+    return count

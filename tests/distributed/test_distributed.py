@@ -364,6 +364,19 @@ def test_affinity_interpolate_decoder_under_fsdp(run_distributed, tmp_path):
     assert len(set(out.values())) == 1
 
 
+def test_backbone_unfreezes_under_fsdp_mixed_precision(run_distributed, tmp_path):
+    """A backbone frozen for the first steps trains once unfrozen under FSDP with bf16 parameters:
+    the units' gradient dtypes are re-derived when requires_grad flips (FSDP fixes them from the
+    parameters that require grad at its first forward, and a frozen unit then has none)."""
+    cfg = tmp_path / "freeze.toml"
+    text = CONFIG.format(steps=4, parallelism='dp_shard = 2\nparam_dtype = "bf16"')
+    text = text.replace("seed = 0\n", "seed = 0\nfreeze_backbone_steps = 2\nunfreeze_warmup_steps = 1\n", 1)
+    assert "freeze_backbone_steps" in text
+    cfg.write_text(text)
+    out = run_distributed(_run_training, 2, str(tmp_path / "runs"), str(cfg), None)
+    assert len(set(out.values())) == 1
+
+
 def _lora_under_tp(rank, world, root, config_path):
     from mia_train_b200.engine.run import run
 
