@@ -9,7 +9,9 @@ each deterministic in `(seed, index)`:
 * `"voronoi"` -- instance labels from a 3D Voronoi partition of `n_seeds` uniform seeds, with a
   1-voxel boundary (label 0) wherever a 6-neighbour belongs to another cell. The image is a
   per-cell mean intensity U(0.3, 0.7), minus 0.4 on boundary voxels, plus N(0, `noise`) noise,
-  blurred with `sigma`.
+  blurred with `sigma`. With `classes = K >= 2` the labels are semantic instead: each cell draws a
+  class in [1, K) (0 stays the boundary) and its mean intensity is set by its class (evenly spaced
+  over [0.25, 0.75], N(0, 0.03) jitter per cell), for `semantic_seg`.
 
 Samples are `{"img": (1, 1, X, Y, Z) float32}` with `sample_axes = "lcxyz"`; the voronoi generator
 adds `"label": (1, X, Y, Z) int64`.
@@ -102,7 +104,7 @@ def blobs_volume(
 
 
 def voronoi_volume(
-    shape: tuple[int, int, int], n_seeds: int, noise: float, sigma: float, gen: torch.Generator
+    shape: tuple[int, int, int], n_seeds: int, noise: float, sigma: float, gen: torch.Generator, classes: int = 0
 ) -> tuple[torch.Tensor, torch.Tensor]:
     seeds = torch.rand(n_seeds, 3, generator=gen) * torch.tensor(shape, dtype=torch.float32)
     coords = torch.stack(
@@ -121,7 +123,12 @@ def voronoi_volume(
         differ = a != b
         boundary.narrow(axis, 1, shape[axis] - 1).logical_or_(differ)
     labels = cells.masked_fill(boundary, 0)
-    means = 0.3 + 0.4 * torch.rand(n_seeds + 1, generator=gen)
+    if classes >= 2:  # semantic labels: each cell draws a class in [1, classes), its mean intensity follows it
+        cls = torch.randint(1, classes, (n_seeds + 1,), generator=gen)
+        means = 0.25 + 0.5 * (cls.float() - 1) / max(1, classes - 2) + 0.03 * torch.randn(n_seeds + 1, generator=gen)
+        labels = cls[cells].masked_fill(boundary, 0)
+    else:
+        means = 0.3 + 0.4 * torch.rand(n_seeds + 1, generator=gen)
     image = means[cells] - 0.4 * boundary.float()
     image = image + noise * torch.randn(shape, generator=gen)
     return gaussian_blur3d(image, sigma), labels
@@ -172,7 +179,8 @@ class _SyntheticSource(data.Dataset):
         elif s["generator"] == "blobs":
             img = blobs_volume(shape, float(s["sigma"]), float(s["blob_rate"]), tuple(s["blob_radii"]), gen)
         else:
-            img, labels = voronoi_volume(shape, int(s["n_seeds"]), float(s["noise"]), float(s["sigma"]), gen)
+            img, labels = voronoi_volume(shape, int(s["n_seeds"]), float(s["noise"]), float(s["sigma"]), gen,
+                                         int(s["classes"]))
             sample["label"] = labels[None]
         sample["img"] = img[None, None].contiguous()
         return sample
@@ -192,6 +200,7 @@ class SyntheticVolumes(BaseDataset):
         n_seeds: int = 300,
         noise: float = 0.08,
         levels: tuple[int, ...] = (1,),
+        classes: int = 0,
     ) -> None:
         super().__init__()
         self.settings = self.resolve_settings(
@@ -205,6 +214,7 @@ class SyntheticVolumes(BaseDataset):
             n_seeds=n_seeds,
             noise=noise,
             levels=levels,
+            classes=classes,
         )
 
     @classmethod
@@ -220,6 +230,7 @@ class SyntheticVolumes(BaseDataset):
             "n_seeds": 300,
             "noise": 0.08,
             "levels": (1,),
+            "classes": 0,
         }
         unknown = sorted(set(kwargs) - set(defaults))
         if unknown:
@@ -241,6 +252,9 @@ class SyntheticVolumes(BaseDataset):
             if any(n % ratio for n in out["shape"]):
                 raise ValueError(f"shape {out['shape']} must divide by the level ratio {ratio}")
         out["levels"] = levels
+        out["classes"] = int(out["classes"])
+        if out["classes"] and (out["classes"] < 2 or out["generator"] != "voronoi"):
+            raise ValueError(f"classes = {out['classes']}: semantic classes (>= 2) take the voronoi generator")
         if int(out["samples_per_epoch"]) < 1:
             raise ValueError("samples_per_epoch must be >= 1")
         return out

@@ -14,6 +14,7 @@ from torch.utils.data import default_collate
 
 from mia_train_b200.algorithms.affinity_seg import AffinitySegmentation
 from mia_train_b200.algorithms.mae import MAE
+from mia_train_b200.algorithms.semantic_seg import SemanticSegmentation
 from mia_train_b200.data.synthetic import SyntheticVolumes
 from mia_train_b200.engine.config import TrainerConfig
 from mia_train_b200.engine.optimizer import build_lr_scheduler, build_optimizer
@@ -65,3 +66,13 @@ def test_affinity_overfits_one_volume(decoder):
     batch = default_collate([data.dataset[0]])
     first, last = _fit(alg, lambda: alg.training_step(batch)["loss"], 150, 3e-3)
     assert last < 0.8 * first
+
+
+def test_semantic_seg_overfits_one_volume():
+    torch.manual_seed(0)
+    vit = ViT3D(img_size=(16, 16, 16), patch_size=(4, 4, 4), embed_dim=64, depth=2, num_heads=4)
+    data = SyntheticVolumes(generator="voronoi", shape=(16, 16, 16), n_seeds=12, classes=4)
+    alg = SemanticSegmentation(vit, data, num_classes=4, decoder_hidden_dim=16)
+    batch = default_collate([data.dataset[0]])
+    first, last = _fit(alg, lambda: alg.training_step(batch)["loss"], 150, 3e-3)
+    assert last < 0.5 * first

@@ -55,6 +55,20 @@ def test_synthetic_levels_validation():
         SyntheticVolumes(shape=(30, 32, 32), levels=(1, 4))
 
 
+def test_synthetic_semantic_classes():
+    ds = SyntheticVolumes(generator="voronoi", shape=(16, 16, 16), n_seeds=20, classes=4)
+    sample = ds.dataset[0]
+    labels, img = sample["label"][0], sample["img"][0, 0]
+    assert set(labels.unique().tolist()) <= {0, 1, 2, 3} and labels.max() > 0
+    # the mean intensity rises with the class (away from boundaries, where the blur mixes cells)
+    means = [img[labels == c].mean() for c in (1, 2, 3) if (labels == c).sum() > 20]
+    assert all(a < b for a, b in zip(means, means[1:], strict=False))
+    with pytest.raises(ValueError, match="classes"):
+        SyntheticVolumes(generator="noise", classes=3)
+    with pytest.raises(ValueError, match="classes"):
+        SyntheticVolumes(generator="voronoi", classes=1)
+
+
 def test_dataloader_shards_by_dp_rank():
     ds = SyntheticVolumes(shape=(8, 8, 8), samples_per_epoch=8)
     loaders = [ds.build_dataloader(batch_size=2, rank=r, world_size=2, num_workers=0, shuffle=False)

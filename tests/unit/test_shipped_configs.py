@@ -46,7 +46,7 @@ def _capped(config):
 def test_every_run_config_is_covered():
     names = {p.relative_to(CONFIGS).as_posix() for p in RUN_CONFIGS}
     assert {"mae_smoke_synthetic.toml", "muvit_mae_smoke_synthetic.toml", "affinity_smoke_synthetic.toml",
-            "dinov3_lora_smoke_synthetic.toml", "dinov3_ssl_smoke_synthetic.toml",
+            "dinov3_lora_smoke_synthetic.toml", "dinov3_ssl_smoke_synthetic.toml", "semantic_seg_smoke_synthetic.toml",
             "workloads/vit_l_mae.toml", "workloads/dinov3_vit_h.toml",
             "workloads/windowed_simmim_vit_l.toml", "workloads/affinity_vit_l_tp2.toml"} <= names
 
