@@ -11,6 +11,10 @@ On CUDA the loss is the fused affinity kernel: targets and masks are recomputed 
 inside the loss and its gradient, never stored. Connected-component splitting goes to the
 dataloader workers (native host union-find) when the engine asks for `sample_transform()`;
 otherwise it runs on the device.
+
+Under sequence-parallel tensor parallelism (`split_decoder_over_tp`, default on) each TP rank
+decodes its own share of the batch's samples after the encoder, and the loss is weighted by each
+rank's share of the voxels; a per-replica batch smaller than the TP group decodes replicated.
 """
 
 from __future__ import annotations
@@ -160,7 +164,16 @@ class AffinitySegmentation(BaseAlgorithm):
                 f"label crop {tuple(labels.shape)} does not match the image crop {tuple(volumes.shape)}"
             )
         sp = getattr(self.encoder, "_sequence_parallel", None)
-        part = sp.sample_slice(volumes.shape[0]) if sp is not None and self.split_decoder_over_tp else None
+        split = sp is not None and self.split_decoder_over_tp and volumes.shape[0] >= sp.world
+        if sp is not None and self.split_decoder_over_tp and not split and self._post_gather_marked:
+            # the decoder's gradients are summed over the group once it has been split: a replicated
+            # decode now would count them once per rank
+            raise ValueError(
+                f"a batch of {volumes.shape[0]} is smaller than the tensor-parallel group ({sp.world}) after "
+                "earlier batches split the decoder over it; keep the per-replica batch at least the TP size"
+            )
+        # a per-replica batch smaller than the TP group decodes replicated on every TP rank
+        part = sp.sample_slice(volumes.shape[0]) if split else None
         if part is not None:
             self._mark_post_gather(sp)
             sp.split_samples = True

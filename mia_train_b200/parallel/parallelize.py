@@ -45,6 +45,15 @@ def _apply_tensor_parallel(model: nn.Module, mesh: DeviceMesh, dims: ParallelDim
             f"[lora] adapters ({adapted[0]}, ... {len(adapted)} layers) cannot be combined with tensor "
             f"parallelism (tp = {dims.tp}): train the adapters with data parallelism (dp_shard / dp_replicate)"
         )
+    dropping = [name for name, m in model.named_modules() if getattr(m, "sample_drop_ratio", 0.0) > 0.0]
+    if dropping and dims.tp_comm != "allreduce":
+        # stochastic depth trains a random subset of samples per block; the sequence-parallel
+        # blocks hold token rows of every sample and have no subset path
+        raise ValueError(
+            f"drop_path ({dropping[0]}, ... {len(dropping)} blocks) cannot be combined with sequence-parallel "
+            f"tensor parallelism (tp = {dims.tp}, tp_comm = {dims.tp_comm!r}): set [model] drop_path_rate = 0, "
+            "use tp_comm = \"allreduce\", or train with data parallelism"
+        )
     plan = model.tensor_parallel_plan() if isinstance(model, BaseModel) else None
     if plan is None:
         raise ValueError(

@@ -269,6 +269,46 @@ def test_trainer_affinity_decoder_split_under_tensor_parallelism(run_distributed
         assert len(counts) == 2 and all(n > 2 * 4 for n in counts), counts
 
 
+def test_affinity_batch_smaller_than_tp_group_decodes_replicated(run_distributed, tmp_path):
+    """A per-replica batch of 1 under TP 2 cannot be split by samples: every TP rank decodes it, and
+    the decoder's gradients are not summed over the group (only the blocks' norms are)."""
+    cfg = tmp_path / "aff1.toml"
+    text = SP_CONFIG.replace('name = "simmim"\nmask_ratio = 0.5',
+                             'name = "affinity_seg"\ndecoder = "subpixel"\noffsets = "nisb12"\n'
+                             'decoder_hidden_dim = 16\ndecoder_readout_dim = 8\nsplit_disconnected = false')
+    text = text.replace('shape = [16, 16, 16]', 'shape = [16, 16, 16]\ngenerator = "voronoi"\nn_seeds = 12')
+    assert "batch_size = 1" in text
+    cfg.write_text(text)
+    out = run_distributed(_sp_trainer_syncs, 2, str(tmp_path / "runs"), str(cfg))
+    for counts in out.values():
+        assert len(counts) == 2 and all(n == 2 * 4 for n in counts), counts
+
+
+def _run_or_error(rank, world, root, config_path):
+    from mia_train_b200.engine.run import run
+
+    try:
+        run(Path(config_path), output_root=Path(root), resume=None)
+    except ValueError as error:
+        return str(error)
+    return "trained"
+
+
+def test_drop_path_under_tensor_parallelism(run_distributed, tmp_path):
+    """Stochastic depth is refused at setup under sequence-parallel TP (its blocks have no
+    sample-subset path) and trains with replicated activations (tp_comm = "allreduce")."""
+    text = SP_CONFIG.replace('name = "dinov3_vit3d"\n', 'name = "dinov3_vit3d"\ndrop_path_rate = 0.5\n', 1)
+    assert "drop_path_rate" in text
+    cfg = tmp_path / "drop_sp.toml"
+    cfg.write_text(text)
+    out = run_distributed(_run_or_error, 2, str(tmp_path / "runs"), str(cfg))
+    assert all("drop_path" in v and "allreduce" in v for v in out.values()), out
+    cfg = tmp_path / "drop_allreduce.toml"
+    cfg.write_text(text.replace('tp_comm = "collective"', 'tp_comm = "allreduce"'))
+    out = run_distributed(_run_or_error, 2, str(tmp_path / "runs2"), str(cfg))
+    assert set(out.values()) == {"trained"}, out
+
+
 DINO_CONFIG = """
 experiment_name = "dino"
 
