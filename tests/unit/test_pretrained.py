@@ -58,3 +58,42 @@ def test_read_state_dict_unwraps_teacher(tmp_path):
     path = tmp_path / "t.pth"
     torch.save({"teacher": {"w": torch.ones(1)}}, path)
     assert "w" in read_state_dict(path)
+
+
+def test_released_2d_dinov3_checkpoint_initialises_the_3d_encoder(tmp_path):
+    """The chain the fine-tuning recipes use: a 2-D DINOv3 checkpoint (RGB patch kernel, LayerScale,
+    masked key bias, 4 registers) loads strictly into `dinov3_vit3d` through a config's `[init]`
+    (inflate_2d_to_3d, rope buffers skipped), and the inflated kernel answers a z-constant volume
+    like the 2-D kernel answers its plane."""
+    from mia_train_b200 import components  # noqa: F401
+    from mia_train_b200.engine.run import prepare_model
+    from mia_train_b200.models.dinov3_vit import DinoVisionTransformer
+    from mia_train_b200.utils.config import parse_run_config
+
+    torch.manual_seed(0)
+    dims = dict(patch_size=8, embed_dim=48, depth=2, num_heads=2, n_storage_tokens=4,
+                layerscale_init=1e-5, mask_k_bias=True)
+    src = DinoVisionTransformer(img_size=32, in_chans=3, **dims)
+    path = tmp_path / "dinov3_2d.pth"
+    torch.save(src.state_dict(), path)
+    config = parse_run_config({
+        "experiment_name": "init_chain",
+        "model": {"name": "dinov3_vit3d", "img_size": 32, "in_chans": 1, "pos_embed_rope_type": "superposition",
+                  **dims},
+        "init": {"path": str(path), "inflate_2d_to_3d": True, "skip": ["rope_embed."], "strict": True},
+        "algorithm": {"name": "simmim"},
+        "data": {"name": "synthetic_volumes"},
+        "trainer": {"max_steps": 1, "batch_size": 1},
+    })
+    model = prepare_model(config)
+    torch.testing.assert_close(model.blocks[1].attn.qkv.weight, src.blocks[1].attn.qkv.weight)
+    torch.testing.assert_close(model.blocks[0].ls1.gamma, src.blocks[0].ls1.gamma)
+    torch.testing.assert_close(model.storage_tokens, src.storage_tokens)
+    # a z-constant single-channel volume through the inflated kernel == the plane through the RGB kernel
+    # averaged over its channels
+    plane = torch.randn(1, 1, 8, 8)
+    vol = plane[:, :, None].expand(1, 1, 8, 8, 8)  # the kernel is (out, in, depth, h, w)
+    w3, w2 = model.patch_embed.proj.weight, src.patch_embed.proj.weight
+    out3 = torch.einsum("ocdhw,bcdhw->bo", w3, vol)
+    out2 = torch.einsum("ochw,bchw->bo", w2.mean(dim=1, keepdim=True), plane)
+    torch.testing.assert_close(out3, out2, atol=1e-5, rtol=1e-4)
