@@ -97,3 +97,39 @@ def test_released_2d_dinov3_checkpoint_initialises_the_3d_encoder(tmp_path):
     out3 = torch.einsum("ocdhw,bcdhw->bo", w3, vol)
     out2 = torch.einsum("ochw,bchw->bo", w2.mean(dim=1, keepdim=True), plane)
     torch.testing.assert_close(out3, out2, atol=1e-5, rtol=1e-4)
+
+
+def test_own_run_checkpoint_initialises_the_next_stage(tmp_path):
+    """Stage chaining: a simmim run's DCP checkpoint directory (the whole algorithm, the encoder
+    under `model.`) initialises a fresh encoder through `[init] prefix = "model."`, strictly."""
+    from pathlib import Path
+
+    from mia_train_b200 import components  # noqa: F401
+    from mia_train_b200.engine.run import prepare_model, run
+    from mia_train_b200.utils.config import parse_run_config
+
+    model_kw = {"name": "dinov3_vit3d", "img_size": 16, "patch_size": 8, "embed_dim": 32, "depth": 2, "num_heads": 2}
+    cfg = tmp_path / "ssl.toml"
+    cfg.write_text(
+        'experiment_name = "ssl"\n[model]\n' + "".join(f"{k} = {v!r}\n".replace("'", '"') for k, v in model_kw.items())
+        + '[algorithm]\nname = "simmim"\nmask_ratio = 0.5\n'
+        + '[data]\nname = "synthetic_volumes"\nshape = [16, 16, 16]\nsamples_per_epoch = 4\n'
+        + '[trainer]\nmax_steps = 2\nbatch_size = 2\nlr = 1e-2\nwarmup_steps = 1\nprecision = "fp32"\n'
+        + "checkpoint_every = 2\nlog_every = 1\n"
+    )
+    run_dir = Path(run(cfg, output_root=tmp_path / "runs"))
+    step_dir = run_dir / "checkpoints" / "step_2"
+    assert (step_dir / ".metadata").is_file()
+    saved = read_state_dict(step_dir)
+    config = parse_run_config({
+        "experiment_name": "stage2",
+        "model": model_kw,
+        "init": {"path": str(step_dir), "prefix": "model.", "strict": True},
+        "algorithm": {"name": "affinity_seg"},
+        "data": {"name": "synthetic_volumes"},
+        "trainer": {"max_steps": 1, "batch_size": 1},
+    })
+    model = prepare_model(config)
+    key = "model.blocks.1.mlp.fc2.weight"
+    assert key in saved
+    torch.testing.assert_close(model.blocks[1].mlp.fc2.weight, saved[key])
